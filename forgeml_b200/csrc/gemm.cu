@@ -1,0 +1,960 @@
+// tcgen05 GEMM with fused bias / GELU / residual epilogue for sm_100a.
+//
+// Replaces the Triton tile template of the reference
+// (src/forgeml/_triton.py:6-62, launched by :65-93) and the cuBLAS F.linear
+// calls of Nebula (src/nebula/runtime.py:131-133,145,152-153,186).
+//
+// Design (one persistent kernel, warp-specialised, 192 threads):
+//   warp 0      TMA producer: 2-D tiled loads of 128-byte K slabs of both
+//               operands into a ring of shared-memory stages (SWIZZLE_128B).
+//   warp 1      TMEM allocator + single-thread UMMA issuer
+//               (tcgen05.mma.cta_group::1, M=128, N=BN, fp32 accumulate in
+//               TMEM, two accumulator buffers so the epilogue of tile t
+//               overlaps the main loop of tile t+1).
+//   warps 2..5  epilogue: tcgen05.ld the accumulator, apply the reference's
+//               rounding contract (round to output dtype, + bias, round,
+//               GELU in fp32), optional residual add, store.
+//
+// The kernel works in "MMA space": D[i][j] = sum_k P[i][k] * Q[j][k] where P
+// supplies the 128 TMEM lanes and Q the BN columns.  For ordinary shapes
+// P = A and Q = B^T; for skinny M ("swap") P = B^T and Q = A so that the wide
+// weight dimension fills the 128-row tile and the small batch becomes the
+// UMMA N dimension.  Each operand may be K-major or MN-major in global
+// memory (both are native UMMA smem layouts), so row-major A, [K,N] weights
+// (ForgeML) and [N,K] weights (Nebula) need no copies.
+//
+// Split-K: for few output tiles the K range is split across the CTAs of a
+// thread-block cluster; partial tiles are reduced through distributed shared
+// memory (no global scratch), each CTA reducing a slice of the rows.
+#include <algorithm>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+
+namespace fml {
+namespace gemm {
+
+constexpr int kBM = 128;        // UMMA M
+constexpr int kSlab = 128;      // bytes of K per smem row (one swizzle row)
+constexpr int kThreads = 192;   // 6 warps
+constexpr int kSmemLimit = 232448;  // 227 KB opt-in per block
+constexpr int kMaxStages = 8;
+constexpr int kPromoteKb = 2;  // K slabs per promoted chunk (fp32 path)
+
+struct Params {
+  int I, J;              // rows of P and of Q (MMA space)
+  int num_kb;            // K blocks of kSlab bytes over the (effective) reduction
+  int tiles_i, tiles_j, num_tiles, group_i;
+  int ksplit;            // CTAs per cluster sharing one tile's K range
+  int fmt;               // 0 f16, 1 bf16, 2 tf32
+  int p_mn, q_mn;        // 1 if the operand is MN-major in smem
+  int swap;              // 1: out[j][i], 0: out[i][j]
+  int out_dtype;
+  int act;
+  int stages;
+  int esize;             // element size of the MMA inputs (2 or 4)
+  void* out;
+  long long ldo;
+  const void* bias;
+  long long bias_stride;
+  const void* residual;
+  long long ldr;
+  int rows_out, cols_out;  // M, N of the output
+  int red_stride;          // floats per row of the split-K partial buffer
+  int promote_kb;          // K slabs per TMEM chunk when partial sums are promoted to registers
+};
+
+struct Smem {
+  uint32_t stage_base;  // 1024-aligned smem address of stage 0
+  uint32_t stage_bytes;
+  uint32_t p_bytes;
+  uint32_t bars;        // base of the barrier block
+  uint32_t red;         // split-K partial buffer
+};
+
+__device__ __forceinline__ uint32_t bar_full(const Smem& s, int i) { return s.bars + 8 * i; }
+__device__ __forceinline__ uint32_t bar_empty(const Smem& s, int i) {
+  return s.bars + 8 * (kMaxStages + i);
+}
+__device__ __forceinline__ uint32_t bar_tfull(const Smem& s, int a) {
+  return s.bars + 8 * (2 * kMaxStages + a);
+}
+__device__ __forceinline__ uint32_t bar_tempty(const Smem& s, int a) {
+  return s.bars + 8 * (2 * kMaxStages + 2 + a);
+}
+__device__ __forceinline__ uint32_t bar_red_ready(const Smem& s) {
+  return s.bars + 8 * (2 * kMaxStages + 4);
+}
+__device__ __forceinline__ uint32_t bar_red_done(const Smem& s) {
+  return s.bars + 8 * (2 * kMaxStages + 5);
+}
+__device__ __forceinline__ uint32_t bar_drain(const Smem& s) {
+  return s.bars + 8 * (2 * kMaxStages + 6);
+}
+constexpr int kNumBars = 2 * kMaxStages + 7;
+constexpr int kBarBytes = 8 * kNumBars + 16;  // + tmem holder
+
+__device__ __forceinline__ void tile_coords(const Params& p, int t, int& ti, int& tj) {
+  int per_group = p.group_i * p.tiles_j;
+  int g = t / per_group;
+  int first_i = g * p.group_i;
+  int gsize = min(p.group_i, p.tiles_i - first_i);
+  int local = t - g * per_group;
+  ti = first_i + local % gsize;
+  tj = local / gsize;
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+__device__ __forceinline__ void epi_bar_sync() {
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+__device__ __forceinline__ void fence_cluster() {
+  asm volatile("fence.acq_rel.cluster;" ::: "memory");
+}
+
+// Epilogue for one output element at MMA coordinates (i, j) with fp32 value v.
+__device__ __forceinline__ void epilogue_store(const Params& p, int i, int j, float v) {
+  int m, n;
+  if (p.swap) { m = j; n = i; } else { m = i; n = j; }
+  if (m >= p.rows_out || n >= p.cols_out) return;
+  const int od = p.out_dtype;
+  float x = round_to(v, od);
+  if (p.bias != nullptr) {
+    float b;
+    if (od == FML_F32) b = reinterpret_cast<const float*>(p.bias)[n * p.bias_stride];
+    else if (od == FML_BF16) b = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.bias)[n * p.bias_stride]);
+    else b = __half2float(reinterpret_cast<const __half*>(p.bias)[n * p.bias_stride]);
+    x = round_to(x + b, od);
+  }
+  if (p.act == FML_ACT_GELU_ERF) x = gelu_erf(x);
+  else if (p.act == FML_ACT_GELU_TANH) x = gelu_tanh(x);
+  long long off = (long long)m * p.ldo + n;
+  if (p.residual != nullptr) {
+    long long roff = (long long)m * p.ldr + n;
+    float r;
+    if (od == FML_F32) r = reinterpret_cast<const float*>(p.residual)[roff];
+    else if (od == FML_BF16) r = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.residual)[roff]);
+    else r = __half2float(reinterpret_cast<const __half*>(p.residual)[roff]);
+    x = round_to(x, od) + r;
+  }
+  if (od == FML_F32) reinterpret_cast<float*>(p.out)[off] = x;
+  else if (od == FML_BF16) reinterpret_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16_rn(x);
+  else reinterpret_cast<__half*>(p.out)[off] = __float2half_rn(x);
+}
+
+// Fast path: 32 consecutive output columns of one row (non-swap), 16-bit
+// output, no residual, aligned.  Applies the same per-element contract.
+__device__ __forceinline__ bool epilogue_row32_fast(const Params& p, int m, int n0,
+                                                    const float (&v)[32]) {
+  if (p.swap || p.residual != nullptr || p.out_dtype == FML_F32) return false;
+  if (m >= p.rows_out || n0 + 32 > p.cols_out) return false;
+  long long off = (long long)m * p.ldo + n0;
+  if ((off & 7) != 0 || (reinterpret_cast<uintptr_t>(p.out) & 15) != 0) return false;
+  const int od = p.out_dtype;
+  uint32_t packed[16];
+#pragma unroll
+  for (int e = 0; e < 32; e += 2) {
+    float x0 = round_to(v[e], od), x1 = round_to(v[e + 1], od);
+    if (p.bias != nullptr) {
+      float b0, b1;
+      if (od == FML_BF16) {
+        const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(p.bias);
+        b0 = __bfloat162float(bb[(n0 + e) * p.bias_stride]);
+        b1 = __bfloat162float(bb[(n0 + e + 1) * p.bias_stride]);
+      } else {
+        const __half* bb = reinterpret_cast<const __half*>(p.bias);
+        b0 = __half2float(bb[(n0 + e) * p.bias_stride]);
+        b1 = __half2float(bb[(n0 + e + 1) * p.bias_stride]);
+      }
+      x0 = round_to(x0 + b0, od);
+      x1 = round_to(x1 + b1, od);
+    }
+    if (p.act == FML_ACT_GELU_ERF) { x0 = gelu_erf(x0); x1 = gelu_erf(x1); }
+    else if (p.act == FML_ACT_GELU_TANH) { x0 = gelu_tanh(x0); x1 = gelu_tanh(x1); }
+    if (od == FML_BF16) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+      packed[e / 2] = *reinterpret_cast<uint32_t*>(&h);
+    } else {
+      __half2 h = __floats2half2_rn(x0, x1);
+      packed[e / 2] = *reinterpret_cast<uint32_t*>(&h);
+    }
+  }
+  uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + off);
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+  return true;
+}
+
+template <int BN, bool PROMOTE>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
+                const Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  Smem s;
+  s.stage_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  s.p_bytes = kBM * kSlab;
+  s.stage_bytes = s.p_bytes + BN * kSlab;
+  s.bars = s.stage_base + p.stages * s.stage_bytes;
+  s.red = s.bars + kBarBytes;
+  s.red = (s.red + 15u) & ~15u;
+  const uint32_t tmem_holder = s.bars + 8 * kNumBars;
+
+  const int ksplit = p.ksplit;
+  const uint32_t crank = ksplit > 1 ? cluster_ctarank() : 0u;
+  const int cluster_id = blockIdx.x / ksplit;
+  const int num_clusters = gridDim.x / ksplit;
+  const int kb_begin = (int)((long long)crank * p.num_kb / ksplit);
+  const int kb_end = (int)((long long)(crank + 1) * p.num_kb / ksplit);
+
+  constexpr int kAccStride = BN < 32 ? 32 : BN;
+  constexpr int kTmemCols = (2 * kAccStride <= 32) ? 32
+                            : (2 * kAccStride <= 64) ? 64
+                            : (2 * kAccStride <= 128) ? 128
+                            : (2 * kAccStride <= 256) ? 256 : 512;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < p.stages; ++i) {
+      mbar_init(bar_full(s, i), 1);
+      mbar_init(bar_empty(s, i), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(bar_tfull(s, a), 1);
+      mbar_init(bar_tempty(s, a), 4);
+    }
+    mbar_init(bar_red_ready(s), ksplit);
+    mbar_init(bar_red_done(s), ksplit);
+    mbar_init(bar_drain(s), 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmP);
+    tma_prefetch_desc(&tmQ);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (ksplit > 1) cluster_sync_all();
+  tc_fence_after();
+  uint32_t tmem_base;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(tmem_base) : "r"(tmem_holder) : "memory");
+
+  const int bke = kSlab / p.esize;            // K elements per slab
+  const int mn_box = kSlab / p.esize;         // MN elements per MN-major box
+  const uint32_t slab_box_bytes = (uint32_t)bke * kSlab;  // bytes of one MN-major box
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
+        int ti, tj;
+        tile_coords(p, t, ti, tj);
+        for (int kb = kb_begin; kb < kb_end; ++kb) {
+          if (!mbar_wait(bar_empty(s, stage), phase ^ 1u, DEV_ERR_GEMM_TIMEOUT)) { ok = false; break; }
+          const uint32_t fb = bar_full(s, stage);
+          mbar_arrive_expect_tx(fb, s.stage_bytes);
+          const uint32_t sp = s.stage_base + stage * s.stage_bytes;
+          const uint32_t sq = sp + s.p_bytes;
+          if (!p.p_mn) {
+            tma_load_2d(&tmP, fb, sp, kb * bke, ti * kBM);
+          } else {
+            for (int b = 0; b < kBM / mn_box; ++b)
+              tma_load_2d(&tmP, fb, sp + b * slab_box_bytes, ti * kBM + b * mn_box, kb * bke);
+          }
+          if (!p.q_mn) {
+            tma_load_2d(&tmQ, fb, sq, kb * bke, tj * BN);
+          } else {
+            for (int b = 0; b < BN / mn_box; ++b)
+              tma_load_2d(&tmQ, fb, sq + b * slab_box_bytes, tj * BN + b * mn_box, kb * bke);
+          }
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == p.stages) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (!ok) {
+        // Unwind: let every load we issued land before the CTA can exit.
+        for (int i = 0; i < p.stages; ++i)
+          if (issued_mask & (1u << i))
+            mbar_wait(bar_full(s, i), (issued_parity >> i) & 1u, DEV_ERR_GEMM_TIMEOUT);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ UMMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc(p.fmt, p.p_mn, p.q_mn, BN);
+      const uint32_t p_lbo = p.p_mn ? slab_box_bytes : 16u;
+      const uint32_t q_lbo = p.q_mn ? slab_box_bytes : 16u;
+      // Advance per UMMA K step (32 bytes of K): within the swizzle row for
+      // K-major, by (32/esize) rows of 128 B for MN-major.
+      const uint32_t p_kstep = p.p_mn ? (uint32_t)(32 / p.esize) * kSlab : 32u;
+      const uint32_t q_kstep = p.q_mn ? (uint32_t)(32 / p.esize) * kSlab : 32u;
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
+        // PROMOTE (fp32 / 3xTF32): the K range is cut into chunks of
+        // promote_kb slabs, each accumulated from zero in TMEM and summed by
+        // the epilogue in fp32 registers with round-to-nearest adds, which
+        // bounds the tensor core accumulator's rounding error.
+        int kb = kb_begin;
+        while (kb < kb_end && ok) {
+          const int kb_stop = PROMOTE ? min(kb + p.promote_kb, kb_end) : kb_end;
+          const int chunk_begin = kb;
+          if (!mbar_wait(bar_tempty(s, acc), acc_phase ^ 1u, DEV_ERR_GEMM_TIMEOUT)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + acc * kAccStride;
+          for (; kb < kb_stop; ++kb) {
+            if (!mbar_wait(bar_full(s, stage), phase, DEV_ERR_GEMM_TIMEOUT)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sp = s.stage_base + stage * s.stage_bytes;
+            const uint32_t sq = sp + s.p_bytes;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint64_t ad = umma_desc_sw128(sp + k * p_kstep, p_lbo, 1024u);
+              const uint64_t bd = umma_desc_sw128(sq + k * q_kstep, q_lbo, 1024u);
+              const uint32_t accum = (kb > chunk_begin || k > 0) ? 1u : 0u;
+              if (p.fmt == 2) umma_tf32(d_tmem, ad, bd, idesc, accum);
+              else umma_f16(d_tmem, ad, bd, idesc, accum);
+            }
+            umma_commit(bar_empty(s, stage));
+            if (++stage == p.stages) { stage = 0; phase ^= 1u; }
+          }
+          if (!ok) break;
+          umma_commit(bar_tfull(s, acc));
+          if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+        }
+      }
+      // Drain: every UMMA issued above has completed before TMEM is freed.
+      umma_commit(bar_drain(s));
+      mbar_wait(bar_drain(s), 0, DEV_ERR_GEMM_TIMEOUT);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;              // TMEM lane quadrant of this warp
+    const int row = quad * 32 + lane;       // MMA row within the tile
+    const int ep_tid = threadIdx.x - 64;    // 0..127
+    int acc = 0;
+    uint32_t acc_phase = 0, red_phase = 0;
+    bool ok = true;
+    constexpr int kChunks = (BN + 31) / 32;
+    float* red = reinterpret_cast<float*>(smem_raw + (s.red - smem_u32(smem_raw)));
+    for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
+      int ti, tj;
+      tile_coords(p, t, ti, tj);
+      const int i = ti * kBM + row;
+      float racc[PROMOTE ? BN : 1];
+#pragma unroll
+      for (int e = 0; e < (PROMOTE ? BN : 1); ++e) racc[e] = 0.f;
+      const int nchunks = PROMOTE ? (kb_end - kb_begin + p.promote_kb - 1) / p.promote_kb : 1;
+      for (int ch = 0; ch < nchunks && ok; ++ch) {
+        if (!mbar_wait(bar_tfull(s, acc), acc_phase, DEV_ERR_GEMM_TIMEOUT)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * kAccStride;
+        if (PROMOTE) {
+#pragma unroll
+          for (int c = 0; c < kChunks; ++c) {
+            float v[32];
+            tmem_ld32(tbase + c * 32, v);
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (c * 32 + e < BN) racc[(c * 32 + e) % (PROMOTE ? BN : 1)] += v[e];
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_tempty(s, acc));
+        } else if (ksplit == 1) {
+#pragma unroll 1
+          for (int c = 0; c < kChunks; ++c) {
+            float v[32];
+            tmem_ld32(tbase + c * 32, v);
+            if (c == kChunks - 1) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(bar_tempty(s, acc));
+            }
+            const int j0 = tj * BN + c * 32;
+            const int nvalid = min(32, BN - c * 32);
+            if (nvalid == 32 && epilogue_row32_fast(p, i, j0, v)) continue;
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (e < nvalid) epilogue_store(p, i, j0 + e, v[e]);
+          }
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < kChunks; ++c) {
+            float v[32];
+            tmem_ld32(tbase + c * 32, v);
+            if (c == kChunks - 1) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(bar_tempty(s, acc));
+            }
+            const int nvalid = min(32, BN - c * 32);
+            float4* dst = reinterpret_cast<float4*>(red + row * p.red_stride + c * 32);
+            if (nvalid == 32) {
+#pragma unroll
+              for (int q = 0; q < 8; ++q)
+                dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                if (e < nvalid) red[row * p.red_stride + c * 32 + e] = v[e];
+            }
+          }
+        }
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+      if (!ok) break;
+      if (PROMOTE) {
+        if (ksplit == 1) {
+#pragma unroll
+          for (int e = 0; e < BN; ++e) epilogue_store(p, i, tj * BN + e, racc[e]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < BN; ++e) red[row * p.red_stride + e] = racc[e];
+        }
+      }
+      if (ksplit > 1) {
+        // Split-K: the partial tile is parked in this CTA's smem; reduce a
+        // slice of rows across the cluster through distributed shared memory.
+        epi_bar_sync();
+        if (ep_tid == 0) {
+          fence_cluster();
+          for (int r = 0; r < ksplit; ++r) mbar_arrive_remote(mapa(bar_red_ready(s), r));
+        }
+        if (!mbar_wait_cluster(bar_red_ready(s), red_phase, DEV_ERR_REDUCE_TIMEOUT)) { ok = false; break; }
+        const int rows_per = kBM / ksplit;
+        const int r0 = crank * rows_per;
+        const int slice = rows_per * BN;
+        for (int idx = ep_tid; idx < slice; idx += 128) {
+          int rr, cc;
+          if (p.swap) { rr = idx % rows_per; cc = idx / rows_per; }
+          else { rr = idx / BN; cc = idx % BN; }
+          const uint32_t local = s.red + (uint32_t)(((r0 + rr) * p.red_stride + cc) * 4);
+          float sum = 0.f;
+          for (int r = 0; r < ksplit; ++r) sum += ld_cluster_f32(mapa(local, r));
+          epilogue_store(p, ti * kBM + r0 + rr, tj * BN + cc, sum);
+        }
+        epi_bar_sync();
+        if (ep_tid == 0) {
+          fence_cluster();
+          for (int r = 0; r < ksplit; ++r) mbar_arrive_remote(mapa(bar_red_done(s), r));
+        }
+        if (!mbar_wait_cluster(bar_red_done(s), red_phase, DEV_ERR_REDUCE_TIMEOUT)) { ok = false; break; }
+        red_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Operand packing (workspace): K-major copy with 16-byte aligned rows, and the
+// 3xTF32 split of fp32 operands.
+//   mode 0: dst[r, k] = X[r, k]                              (width Kp)
+//   mode 1: dst = [lo | hi | hi] (P side)                    (width 3 Kp)
+//   mode 2: dst = [hi | lo | hi] (Q side)                    (width 3 Kp)
+// so that P' . Q'^T = lo_P hi_Q + hi_P lo_Q + hi_P hi_Q, the three-product
+// tf32 error-compensated form ("3xTF32"), smallest terms accumulated first.
+// hi = x rounded to tf32 (cvt.rna), lo = x - hi rounded to tf32.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float tf32_round(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+template <typename T>
+__global__ void pack_kernel(const T* __restrict__ x, long long s_r, long long s_k, int R, int K,
+                            int Kp, int mode, T* __restrict__ dst) {
+  __shared__ float tile[32][33];
+  const int r0 = blockIdx.y * 32, k0 = blockIdx.x * 32;
+  const bool r_contig = (s_r == 1 && s_k != 1);
+  // Load a 32x32 tile with the unit-stride dimension across threadIdx.x.
+  for (int yy = threadIdx.y; yy < 32; yy += blockDim.y) {
+    int r, k;
+    if (r_contig) { r = r0 + threadIdx.x; k = k0 + yy; }
+    else { r = r0 + yy; k = k0 + threadIdx.x; }
+    float v = 0.f;
+    if (r < R && k < K) v = to_f32<T>(x[(long long)r * s_r + (long long)k * s_k]);
+    if (r_contig) tile[threadIdx.x][yy] = v;
+    else tile[yy][threadIdx.x] = v;
+  }
+  __syncthreads();
+  for (int yy = threadIdx.y; yy < 32; yy += blockDim.y) {
+    const int r = r0 + yy, k = k0 + threadIdx.x;
+    if (r >= R || k >= Kp) continue;
+    const float v = tile[yy][threadIdx.x];  // zero in the padding columns
+    if (mode == 0) {
+      dst[(long long)r * Kp + k] = from_f32<T>(v);
+    } else {
+      const float hi = tf32_round(v);
+      const float lo = tf32_round(v - hi);
+      float* d = reinterpret_cast<float*>(dst) + (long long)r * 3 * Kp;
+      if (mode == 1) { d[k] = lo; d[Kp + k] = hi; d[2 * Kp + k] = hi; }
+      else { d[k] = hi; d[Kp + k] = lo; d[2 * Kp + k] = hi; }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// Operand description in MMA space: X[r][k] at ptr + r*s_r + k*s_k.
+struct Operand {
+  const void* ptr;
+  long long s_r, s_k;
+  long long rows, k;
+  bool mn;       // MN-major (s_r == 1) when used directly
+  bool pack;     // needs a packed copy in workspace
+  size_t ws_off; // workspace offset of the packed copy
+  long long kp;  // padded row length of the packed copy (elements)
+};
+
+static inline long long round_up(long long v, long long m) { return (v + m - 1) / m * m; }
+
+// Decide whether TMA can address the operand directly.
+static void classify(Operand& o, int dtype, int box_mn, bool allow_mn) {
+  const long long es = (long long)dtype_size(dtype);
+  o.pack = true;
+  o.mn = false;
+  if (dtype == FML_F32) return;  // 3xTF32 always splits into workspace
+  if (reinterpret_cast<uintptr_t>(o.ptr) % 16 != 0) return;
+  const bool k_unit = (o.s_k == 1 || o.k == 1);
+  const bool r_unit = (o.s_r == 1 || o.rows == 1);
+  if (k_unit) {
+    long long stride_bytes = (o.rows == 1 ? round_up(o.k * es, 16) : o.s_r * es);
+    if (stride_bytes % 16 == 0 && stride_bytes > 0 && (o.rows == 1 || o.s_r >= o.k)) {
+      if (o.rows == 1) o.s_r = stride_bytes / es;
+      if (o.k == 1) o.s_k = 1;
+      o.pack = false;
+      return;
+    }
+  }
+  if (r_unit && allow_mn && box_mn % (128 / es) == 0) {
+    long long stride_bytes = (o.k == 1 ? round_up(o.rows * es, 16) : o.s_k * es);
+    if (stride_bytes % 16 == 0 && stride_bytes > 0 && (o.k == 1 || o.s_k >= o.rows)) {
+      if (o.k == 1) o.s_k = stride_bytes / es;
+      o.s_r = 1;
+      o.mn = true;
+      o.pack = false;
+    }
+  }
+}
+
+static int encode(CUtensorMap* map, const void* ptr, int dtype, bool tf32, bool mn,
+                  long long rows, long long keff, long long stride_elems, int box_rows) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return fail(FML_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  const long long es = (long long)dtype_size(dtype);
+  CUtensorMapDataType dt = dtype == FML_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                           : dtype == FML_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  (void)tf32;
+  cuuint64_t dims[2], strides[1];
+  cuuint32_t box[2], estr[2] = {1, 1};
+  const cuuint32_t slab_elems = (cuuint32_t)(kSlab / es);
+  if (!mn) {
+    dims[0] = (cuuint64_t)keff;
+    dims[1] = (cuuint64_t)rows;
+    box[0] = slab_elems;
+    box[1] = (cuuint32_t)box_rows;
+  } else {
+    dims[0] = (cuuint64_t)rows;
+    dims[1] = (cuuint64_t)keff;
+    box[0] = slab_elems;
+    box[1] = slab_elems;  // one slab of K rows per box (kSlab/es)
+  }
+  strides[0] = (cuuint64_t)(stride_elems * es);
+  CUresult r = fn(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(FML_EINVAL, "cuTensorMapEncodeTiled failed (code " + std::to_string((int)r) +
+                                ") rows=" + std::to_string(rows) + " k=" + std::to_string(keff) +
+                                " stride=" + std::to_string(stride_elems));
+  return FML_OK;
+}
+
+struct Plan {
+  bool swap;
+  bool promote;  // fp32: sum TMEM partials in fp32 registers every kPromoteKb slabs
+  int bn;
+  int ksplit;
+  int stages;
+  Operand P, Q;
+  long long keff;  // effective reduction length (3*Kp for tf32)
+  size_t ws_bytes;
+};
+
+static const int kBNs[] = {16, 32, 64, 128, 256};
+
+static int smem_bytes_for(int bn, int stages, int ksplit, int* red_stride) {
+  int stage_bytes = (kBM + bn) * kSlab;
+  int rs = bn + 4;
+  if (red_stride) *red_stride = rs;
+  int red = ksplit > 1 ? kBM * rs * 4 + 16 : 0;
+  return 1024 + stages * stage_bytes + kBarBytes + 16 + red;
+}
+
+static int make_plan(Plan& pl, const void* a, long long lda_m, long long lda_k, const void* b,
+                     long long ldb_k, long long ldb_n, long long M, long long N, long long K,
+                     int dtype, const fml_tile_cfg* cfg, int sms) {
+  // MMA-space orientation.
+  pl.swap = (M <= 128 && N > M);
+  if (pl.swap) {
+    pl.P = Operand{b, ldb_n, ldb_k, N, K, false, false, 0, 0};
+    pl.Q = Operand{a, lda_m, lda_k, M, K, false, false, 0, 0};
+  } else {
+    pl.P = Operand{a, lda_m, lda_k, M, K, false, false, 0, 0};
+    pl.Q = Operand{b, ldb_n, ldb_k, N, K, false, false, 0, 0};
+  }
+  const long long J = pl.Q.rows, I = pl.P.rows;
+  // UMMA N tile.
+  int bn = 256;
+  if (cfg && cfg->block_n > 0) {
+    bn = 0;
+    for (int c : kBNs)
+      if (c >= std::min<long long>(cfg->block_n, 256)) { bn = c; break; }
+    if (bn == 0) bn = 256;
+  } else if (pl.swap) {
+    bn = 256;
+    for (int c : kBNs)
+      if (c >= J) { bn = c; break; }
+  } else {
+    // Pick the wider tile unless it leaves too many SMs idle.
+    long long ti = (I + kBM - 1) / kBM;
+    auto util = [&](int c) {
+      long long tiles = ti * ((J + c - 1) / c);
+      long long waves = (tiles + sms - 1) / sms;
+      return (double)tiles / (double)(waves * sms) * std::min(1.0, (double)J / c);
+    };
+    bn = 256;
+    if (J <= 128) { for (int c : kBNs) if (c >= J) { bn = c; break; } }
+    else if (util(128) > util(256) * 1.15) bn = 128;
+  }
+  pl.promote = (dtype == FML_F32);
+  if (pl.promote && bn > 64) bn = 64;  // register-resident row accumulator
+  pl.bn = bn;
+  classify(pl.P, dtype, kBM, true);
+  classify(pl.Q, dtype, bn, true);
+  // Effective K and packing layout.
+  const long long es = (long long)dtype_size(dtype);
+  const long long kp = round_up(K, 16 / es);
+  pl.keff = dtype == FML_F32 ? 3 * kp : K;
+  size_t ws = 0;
+  for (Operand* o : {&pl.P, &pl.Q}) {
+    if (!o->pack) continue;
+    o->kp = kp;
+    o->ws_off = ws;
+    ws += (size_t)round_up(o->rows * (dtype == FML_F32 ? 3 * kp : kp) * es, 256);
+  }
+  pl.ws_bytes = ws;
+  // Split-K through the cluster when there are too few tiles to fill the GPU.
+  const long long tiles = ((I + kBM - 1) / kBM) * ((J + bn - 1) / bn);
+  const long long num_kb = (pl.keff * es + kSlab - 1) / kSlab;
+  int ks = 1;
+  if (bn <= 128 && tiles * 2 <= sms && num_kb >= 8) {
+    long long want = sms / std::max<long long>(tiles, 1);
+    want = std::min<long long>(want, num_kb / 4);
+    want = std::min<long long>(want, 8);
+    while (want > 1 && (kBM % want) != 0) --want;  // rows split evenly
+    ks = (int)std::max<long long>(want, 1);
+  }
+  pl.ksplit = ks;
+  int stages = kMaxStages;
+  if (cfg && cfg->num_stages > 0) stages = std::min(cfg->num_stages, kMaxStages);
+  while (stages > 2 && smem_bytes_for(bn, stages, ks, nullptr) > kSmemLimit) --stages;
+  pl.stages = stages;
+  if (smem_bytes_for(bn, stages, ks, nullptr) > kSmemLimit)
+    return fail(FML_EUNSUPPORTED, "gemm tile does not fit in shared memory");
+  return FML_OK;
+}
+
+template <int BN, bool PROMOTE>
+static int launch_bn(const CUtensorMap& mp, const CUtensorMap& mq, const Params& prm, int grid,
+                     int smem, cudaStream_t st) {
+  static std::once_flag once[64];
+  const int dev = current_device();
+  cudaError_t e = cudaSuccess;
+  std::call_once(once[dev & 63], [&]() {
+    e = cudaFuncSetAttribute(gemm_kernel<BN, PROMOTE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemLimit);
+  });
+  if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(gemm)");
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(grid);
+  lc.blockDim = dim3(kThreads);
+  lc.dynamicSmemBytes = smem;
+  lc.stream = st;
+  cudaLaunchAttribute attr[1];
+  int na = 0;
+  if (prm.ksplit > 1) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = prm.ksplit;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    na = 1;
+  }
+  lc.attrs = attr;
+  lc.numAttrs = na;
+  e = cudaLaunchKernelEx(&lc, gemm_kernel<BN, PROMOTE>, mp, mq, prm);
+  if (e != cudaSuccess) return check_cuda(e, "gemm launch");
+  count_launch();
+  return FML_OK;
+}
+
+template <int BN, bool PROMOTE>
+static int max_clusters(int ksplit, int smem) {
+  if (ksplit <= 1) return -1;
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(ksplit);
+  lc.blockDim = dim3(kThreads);
+  lc.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = ksplit;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  cudaFuncSetAttribute(gemm_kernel<BN, PROMOTE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_kernel<BN, PROMOTE>, &lc) != cudaSuccess) return -1;
+  return n;
+}
+
+static int pack_operand(const Operand& o, int dtype, int mode, void* ws, cudaStream_t st) {
+  dim3 blk(32, 8);
+  const long long kp_w = o.kp;
+  dim3 grd((unsigned)((kp_w + 31) / 32), (unsigned)((o.rows + 31) / 32));
+  if (grd.y > 65535) return fail(FML_EUNSUPPORTED, "pack: too many rows");
+  void* dst = static_cast<uint8_t*>(ws) + o.ws_off;
+  if (dtype == FML_F32)
+    pack_kernel<float><<<grd, blk, 0, st>>>(static_cast<const float*>(o.ptr), o.s_r, o.s_k,
+                                            (int)o.rows, (int)o.k, (int)o.kp, mode,
+                                            static_cast<float*>(dst));
+  else if (dtype == FML_BF16)
+    pack_kernel<__nv_bfloat16><<<grd, blk, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(o.ptr), o.s_r, o.s_k, (int)o.rows, (int)o.k,
+        (int)o.kp, 0, static_cast<__nv_bfloat16*>(dst));
+  else
+    pack_kernel<__half><<<grd, blk, 0, st>>>(static_cast<const __half*>(o.ptr), o.s_r, o.s_k,
+                                             (int)o.rows, (int)o.k, (int)o.kp, 0,
+                                             static_cast<__half*>(dst));
+  count_launch();
+  return check_cuda(cudaGetLastError(), "pack launch");
+}
+
+}  // namespace gemm
+}  // namespace fml
+
+using namespace fml;
+using namespace fml::gemm;
+
+static int validate_gemm(const void* a, const void* b, void* c, long long m, long long n,
+                         long long k, int dtype) {
+  if (!valid_dtype(dtype)) return fail(FML_EINVAL, "gemm: dtype must be f32, f16 or bf16");
+  if (m <= 0 || n <= 0 || k <= 0) return fail(FML_EINVAL, "gemm: M, N, K must be positive");
+  if (m > (1ll << 31) - 1 || n > (1ll << 31) - 1 || k > (1ll << 31) - 1)
+    return fail(FML_EUNSUPPORTED, "gemm: dimension exceeds int32");
+  if (!a || !b || !c) return fail(FML_EINVAL, "gemm: null operand pointer");
+  return FML_OK;
+}
+
+extern "C" size_t fml_gemm_workspace_size(int64_t m, int64_t n, int64_t k, int dtype,
+                                          int64_t lda_m, int64_t lda_k, int64_t ldb_k,
+                                          int64_t ldb_n, const void* a, const void* b,
+                                          const fml_tile_cfg* cfg) {
+  if (!valid_dtype(dtype) || m <= 0 || n <= 0 || k <= 0) return 0;
+  Plan pl;
+  const void* ap = a ? a : reinterpret_cast<const void*>(uintptr_t(256));
+  const void* bp = b ? b : reinterpret_cast<const void*>(uintptr_t(256));
+  if (make_plan(pl, ap, lda_m, lda_k, bp, ldb_k, ldb_n, m, n, k, dtype, cfg,
+                num_sms(current_device())) != FML_OK)
+    return 0;
+  return pl.ws_bytes;
+}
+
+extern "C" int fml_gemm(const void* a, int64_t lda_m, int64_t lda_k, const void* b,
+                        int64_t ldb_k, int64_t ldb_n, const void* bias, int64_t bias_stride,
+                        const void* residual, int64_t ldr, void* c, int64_t ldc, int64_t m,
+                        int64_t n, int64_t k, int dtype, int act, const fml_tile_cfg* cfg,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = validate_gemm(a, b, c, m, n, k, dtype);
+  if (rc) return rc;
+  if (act < 0 || act > 2) return fail(FML_EINVAL, "gemm: act must be 0 (none), 1 (erf) or 2 (tanh)");
+  if (ldc < n) return fail(FML_EINVAL, "gemm: ldc < N");
+  if (residual && ldr < n) return fail(FML_EINVAL, "gemm: ldr < N");
+  if (cfg) {
+    if (cfg->block_n < 0 || cfg->block_n > 256 || cfg->num_stages < 0 || cfg->num_stages > 16)
+      return fail(FML_EINVAL, "gemm: tile config out of range");
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int sms = num_sms(current_device());
+  Plan pl;
+  rc = make_plan(pl, a, lda_m, lda_k, b, ldb_k, ldb_n, m, n, k, dtype, cfg, sms);
+  if (rc) return rc;
+  if (pl.ws_bytes > 0 && (workspace == nullptr || workspace_bytes < pl.ws_bytes))
+    return fail(FML_EWORKSPACE, "gemm: workspace of " + std::to_string(pl.ws_bytes) +
+                                    " bytes required");
+  if (workspace && (reinterpret_cast<uintptr_t>(workspace) % 256) != 0)
+    return fail(FML_EINVAL, "gemm: workspace must be 256-byte aligned");
+  const bool tf32 = dtype == FML_F32;
+  // Pack operands that TMA cannot read directly.
+  if (pl.P.pack) {
+    rc = pack_operand(pl.P, dtype, tf32 ? 1 : 0, workspace, st);
+    if (rc) return rc;
+  }
+  if (pl.Q.pack) {
+    rc = pack_operand(pl.Q, dtype, tf32 ? 2 : 0, workspace, st);
+    if (rc) return rc;
+  }
+  CUtensorMap mp, mq;
+  for (int w = 0; w < 2; ++w) {
+    Operand& o = w == 0 ? pl.P : pl.Q;
+    CUtensorMap* map = w == 0 ? &mp : &mq;
+    const int box_rows = w == 0 ? kBM : pl.bn;
+    if (o.pack) {
+      const void* ptr = static_cast<uint8_t*>(workspace) + o.ws_off;
+      rc = encode(map, ptr, dtype, tf32, false, o.rows, pl.keff, tf32 ? 3 * o.kp : o.kp,
+                  box_rows);
+    } else if (!o.mn) {
+      rc = encode(map, o.ptr, dtype, tf32, false, o.rows, pl.keff, o.s_r, box_rows);
+    } else {
+      rc = encode(map, o.ptr, dtype, tf32, true, o.rows, pl.keff, o.s_k, box_rows);
+    }
+    if (rc) return rc;
+  }
+  Params prm = {};
+  prm.I = (int)pl.P.rows;
+  prm.J = (int)pl.Q.rows;
+  const long long es = (long long)dtype_size(dtype);
+  prm.num_kb = (int)((pl.keff * es + kSlab - 1) / kSlab);
+  prm.tiles_i = (int)((prm.I + kBM - 1) / kBM);
+  prm.tiles_j = (int)((prm.J + pl.bn - 1) / pl.bn);
+  prm.num_tiles = prm.tiles_i * prm.tiles_j;
+  prm.group_i = std::min(prm.tiles_i, 16);
+  prm.ksplit = pl.ksplit;
+  prm.fmt = dtype == FML_F32 ? 2 : dtype == FML_BF16 ? 1 : 0;
+  prm.p_mn = pl.P.pack ? 0 : (pl.P.mn ? 1 : 0);
+  prm.q_mn = pl.Q.pack ? 0 : (pl.Q.mn ? 1 : 0);
+  prm.swap = pl.swap ? 1 : 0;
+  prm.out_dtype = dtype;
+  prm.act = act;
+  prm.stages = pl.stages;
+  prm.esize = (int)es;
+  prm.out = c;
+  prm.ldo = ldc;
+  prm.bias = bias;
+  prm.bias_stride = bias_stride;
+  prm.residual = residual;
+  prm.ldr = ldr;
+  prm.rows_out = (int)m;
+  prm.cols_out = (int)n;
+  int red_stride = 0;
+  const int smem = smem_bytes_for(pl.bn, pl.stages, pl.ksplit, &red_stride);
+  prm.red_stride = red_stride;
+  prm.promote_kb = kPromoteKb;
+  // Persistent grid: one CTA per SM (or as many clusters as fit).
+  long long want = (long long)prm.num_tiles * prm.ksplit;
+  int grid;
+  if (prm.ksplit > 1) {
+    int mc = -1;
+    if (pl.promote) {
+      switch (pl.bn) {
+        case 16: mc = max_clusters<16, true>(prm.ksplit, smem); break;
+        case 32: mc = max_clusters<32, true>(prm.ksplit, smem); break;
+        case 64: mc = max_clusters<64, true>(prm.ksplit, smem); break;
+        default: mc = -1;
+      }
+    } else {
+      switch (pl.bn) {
+        case 16: mc = max_clusters<16, false>(prm.ksplit, smem); break;
+        case 32: mc = max_clusters<32, false>(prm.ksplit, smem); break;
+        case 64: mc = max_clusters<64, false>(prm.ksplit, smem); break;
+        case 128: mc = max_clusters<128, false>(prm.ksplit, smem); break;
+        default: mc = -1;
+      }
+    }
+    if (mc <= 0) mc = sms / prm.ksplit;
+    grid = (int)std::min<long long>(want, (long long)mc * prm.ksplit);
+  } else {
+    grid = (int)std::min<long long>(want, sms);
+  }
+  grid = std::max(grid / prm.ksplit, 1) * prm.ksplit;
+  if (pl.promote) {
+    switch (pl.bn) {
+      case 16: return launch_bn<16, true>(mp, mq, prm, grid, smem, st);
+      case 32: return launch_bn<32, true>(mp, mq, prm, grid, smem, st);
+      case 64: return launch_bn<64, true>(mp, mq, prm, grid, smem, st);
+    }
+  } else {
+    switch (pl.bn) {
+      case 16: return launch_bn<16, false>(mp, mq, prm, grid, smem, st);
+      case 32: return launch_bn<32, false>(mp, mq, prm, grid, smem, st);
+      case 64: return launch_bn<64, false>(mp, mq, prm, grid, smem, st);
+      case 128: return launch_bn<128, false>(mp, mq, prm, grid, smem, st);
+      case 256: return launch_bn<256, false>(mp, mq, prm, grid, smem, st);
+    }
+  }
+  return fail(FML_EUNSUPPORTED, "gemm: no kernel for tile width");
+}

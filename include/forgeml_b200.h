@@ -1,0 +1,190 @@
+/*
+ * forgeml_b200.h -- C ABI of the sm_100a (B200) kernels behind the ForgeML
+ * compiled-forward dispatch and the Nebula decode step.
+ *
+ * Conventions shared by every entry point:
+ *   - All pointers are device pointers unless the comment says "host".
+ *   - Strides are in ELEMENTS, not bytes.
+ *   - `stream` is a cudaStream_t passed as void* (0 = legacy default stream).
+ *   - The return value is 0 on success.  A nonzero value is an FML_E* code and
+ *     fml_last_error() returns a message for the calling thread.  Nothing is
+ *     launched when validation fails.  No entry point falls back to another
+ *     implementation: an unsupported layout is an error.
+ *   - Kernels never allocate.  Entry points that need scratch take a
+ *     caller-owned workspace and have a *_workspace_size() query.
+ *   - dtype codes: FML_F32, FML_F16, FML_BF16.
+ */
+#ifndef FORGEML_B200_H
+#define FORGEML_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FML_API __attribute__((visibility("default")))
+#else
+#define FML_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  FML_OK = 0,
+  FML_EINVAL = 1,        /* invalid argument (shape, stride, dtype, null pointer) */
+  FML_EUNSUPPORTED = 2,  /* layout/size this kernel family does not handle */
+  FML_ECUDA = 3,         /* CUDA runtime / driver error at launch */
+  FML_EWORKSPACE = 4,    /* workspace missing or too small */
+  FML_EDEVICE = 5        /* a kernel reported a device-side error (bounded wait expired) */
+};
+
+enum { FML_F32 = 0, FML_F16 = 1, FML_BF16 = 2 };
+enum { FML_ACT_NONE = 0, FML_ACT_GELU_ERF = 1, FML_ACT_GELU_TANH = 2 };
+
+/* Tile hints; mirrors forgeml.kernels.KernelConfig(block_m, block_n, block_k,
+ * num_warps, num_stages) (src/forgeml/kernels.py:12-18).  block_n selects the
+ * UMMA N tile (16..256), num_stages the shared-memory pipeline depth.  NULL
+ * means "choose by heuristic".  block_m, block_k and num_warps are fixed by the
+ * tcgen05 design (128-row UMMA tiles, 128-byte K slabs, 6 warps) and are only
+ * range-checked. */
+typedef struct fml_tile_cfg {
+  int32_t block_m, block_n, block_k, num_warps, num_stages;
+} fml_tile_cfg;
+
+/* ---------------------------------------------------------------------------
+ * GEMM with fused epilogue.
+ * Replaces src/forgeml/_triton.py:6-62 (_matmul_kernel) and :65-93 (launch);
+ * reached from src/forgeml/kernels.py:52-116 (matmul) and, for Nebula's
+ * F.linear calls, src/nebula/runtime.py:131-133,145,152-153,186.
+ *
+ *   C[m,n] = act( r( r( sum_k A[m,k] B[k,n] ) + bias[n] ) )     (+ residual)
+ *
+ * r() rounds to the output dtype (bf16/fp16; identity for fp32), the same
+ * double rounding as the Triton template (_triton.py:43,46).  When
+ * `residual` is non-null the epilogue instead computes
+ *   C = r( r(act(...)) + residual[m,n] )
+ * which is Nebula's `x + F.linear(...)` in the reference dtype.
+ * A[m,k] lives at a[m*lda_m + k*lda_k]; B[k,n] at b[k*ldb_k + n*ldb_n];
+ * C is row-major with row stride ldc; residual has row stride ldr.
+ * fp32 inputs run as 3xTF32 (split hi/lo, three tf32 products) to keep
+ * IEEE-level accuracy; they need workspace.  16-bit operands whose layout a
+ * TMA descriptor cannot address (unaligned strides, neither stride 1) are
+ * packed into workspace first.
+ * ------------------------------------------------------------------------- */
+FML_API size_t fml_gemm_workspace_size(int64_t m, int64_t n, int64_t k, int dtype,
+                               int64_t lda_m, int64_t lda_k, int64_t ldb_k,
+                               int64_t ldb_n, const void* a, const void* b,
+                               const fml_tile_cfg* cfg);
+
+FML_API int fml_gemm(const void* a, int64_t lda_m, int64_t lda_k,
+             const void* b, int64_t ldb_k, int64_t ldb_n,
+             const void* bias, int64_t bias_stride,
+             const void* residual, int64_t ldr,
+             void* c, int64_t ldc,
+             int64_t m, int64_t n, int64_t k,
+             int dtype, int act, const fml_tile_cfg* cfg,
+             void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * LayerNorm over the trailing `cols` elements of each of `rows` rows.
+ * Replaces the F.layer_norm evaluation of src/forgeml/ops.py:54-60 and
+ * src/nebula/runtime.py:130,151,185.  gamma/beta may both be null (no affine).
+ * Statistics in fp32; y rounded once to dtype.
+ * ------------------------------------------------------------------------- */
+FML_API int fml_layernorm(const void* x, int64_t x_row_stride, const void* gamma,
+                  const void* beta, float eps, void* y, int64_t y_row_stride,
+                  int64_t rows, int64_t cols, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Rank-4 scaled dot-product attention, out = softmax(q k^T * scale + mask) v.
+ * Replaces F.scaled_dot_product_attention in src/forgeml/ops.py:61-70.
+ * q is [B,H,Sq,D], k/v are [B,H,Sk,D], out is [B,H,Sq,D]; each has its own
+ * 4 element strides (innermost stride must be 1).  `mask` (optional) is
+ * broadcast to [B,H,Sq,Sk] through mask_strides (0 for broadcast dims);
+ * mask_kind 0 = none, 1 = bool (nonzero keeps), 2 = additive in dtype.
+ * is_causal keeps key j for query i when j <= i (top-left aligned, as torch).
+ * D <= 256.  Softmax in fp32.
+ * ------------------------------------------------------------------------- */
+FML_API int fml_sdpa(const void* q, const int64_t q_strides[4],
+             const void* k, const int64_t k_strides[4],
+             const void* v, const int64_t v_strides[4],
+             const void* mask, const int64_t mask_strides[4], int mask_kind,
+             int is_causal, float scale,
+             void* out, const int64_t out_strides[4],
+             int64_t batch, int64_t heads, int64_t sq, int64_t sk, int64_t d,
+             int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Nebula attention over the contiguous per-request KV cache.
+ * Replaces src/nebula/runtime.py:139-144 together with the prefix
+ * torch.stack in src/nebula/cache.py:163-165 (no copy of the cache is made).
+ * The cache of one layer is a pool [slots, H, max_seq, D]; request b uses pool
+ * slot slot_of[b] (int32, device).  Query b,t sits at absolute position
+ * start_pos[b] + t (int32, device) and attends keys 0..start_pos[b]+t.
+ * q is [B,T,H,D] with element strides q_strides (innermost 1); out is
+ * [B,T,H,D] contiguous rows of H*D.  Scores and softmax in fp32.
+ * ------------------------------------------------------------------------- */
+FML_API int neb_attention(const void* q, const int64_t q_strides[4],
+                  const void* k_pool, const void* v_pool,
+                  const int32_t* slot_of, const int32_t* start_pos,
+                  void* out, int64_t batch, int64_t t, int64_t heads,
+                  int64_t head_dim, int64_t max_seq, float scale,
+                  int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * KV-cache append: pool[slot_of[b], h, start_pos[b]+t, :] = kv[b,t,h,:] for
+ * both K and V.  Replaces the copy_ in src/nebula/cache.py:158-162.  k/v are
+ * [B,T,H,D] with element strides (innermost 1), e.g. column views of the QKV
+ * GEMM output.  Bit-exact copy.
+ * ------------------------------------------------------------------------- */
+FML_API int neb_kv_append(const void* k, const int64_t k_strides[4],
+                  const void* v, const int64_t v_strides[4],
+                  void* k_pool, void* v_pool,
+                  const int32_t* slot_of, const int32_t* start_pos,
+                  int64_t batch, int64_t t, int64_t heads, int64_t head_dim,
+                  int64_t max_seq, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Token + learned position embedding:
+ *   x[b,t,:] = r( tok_emb[tokens[b,t],:] + pos_emb[start_pos[b]+t,:] )
+ * Replaces src/nebula/runtime.py:166-169.  tokens int64 [B,T] contiguous,
+ * start_pos int32 [B] (device).  Ids outside [0,vocab) raise the device error
+ * flag and write zeros.
+ * ------------------------------------------------------------------------- */
+FML_API int neb_embed(const int64_t* tokens, const int32_t* start_pos,
+              const void* tok_emb, const void* pos_emb, void* x,
+              int64_t batch, int64_t t, int64_t hidden, int64_t vocab,
+              int64_t max_seq, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Greedy sampling: out[b] = argmax_j logits[b*row_stride + j], first index
+ * on ties (torch.argmax semantics, src/nebula/runtime.py:477,485).
+ * ------------------------------------------------------------------------- */
+FML_API int neb_argmax(const void* logits, int64_t row_stride, int64_t rows,
+               int64_t cols, int64_t* out, int dtype, void* stream);
+
+/* Elementwise y = r(a + b) on contiguous buffers (Nebula residual add after
+ * a tensor-parallel all-reduce, src/nebula/runtime.py:177,179). */
+FML_API int neb_add(const void* a, const void* b, void* y, int64_t n, int dtype,
+            void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Diagnostics.
+ * ------------------------------------------------------------------------- */
+/* Message for the last nonzero return on this thread ("" if none). */
+FML_API const char* fml_last_error(void);
+/* Reads and clears the device-side error word of the current device
+ * (bounded waits that expired, out-of-range token ids).  0 = clean.
+ * Synchronizes the current device. */
+FML_API int fml_device_status(void);
+/* Number of kernel launches issued by this library in this process. */
+FML_API int64_t fml_launch_count(void);
+/* Library version string. */
+FML_API const char* fml_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FORGEML_B200_H */
