@@ -1,0 +1,443 @@
+"""Benchmark: Nebula greedy-decode tokens/s (config 4) on the sm_100a kernels.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+
+Workload: 12-layer pre-LN decoder, d_model 2048, 16 heads
+x 128, FFN 8192 tanh-GELU, vocab 32000, max context 2048, weights ~ N(0,0.02)
+(seed 3), bf16; batch of 32 prompts x 512 token ids uniform in [0, 32000)
+(seeded); tensor parallel degree = N (one process per GPU, NCCL).  A "step" is
+one greedy decode step of the whole batch (32 tokens).  Prefill runs before
+the timed region; the W warm-up steps and K timed steps continue the same
+sequences (context 513 .. 512+W+K).  Every step streams > 3 GB of weights and
+KV cache, far more than the 126 MB L2, so no flush is needed between steps.
+
+JSON line keys (one line on rank 0):
+  value        decode tokens/s, device-timed (CUDA events, max over ranks)
+  e2e          the same metric through Engine.forward with the step's tokens
+               copied from pinned host memory and the argmax ids read back
+  roofline     decode-attention kernel (HBM): algorithmic bytes / event time
+  gemm         fused linear+GELU GEMM TFLOP/s at 8192^3 bf16 (N=1)
+  cpu_baseline the CPU oracle of the same decode step on the host cores (N=1)
+--impl reference times that CPU restatement alone (rank 0; other ranks exit 0).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+C4 = dict(vocab_size=32000, hidden_size=2048, num_heads=16, num_layers=12, intermediate_size=8192,
+          max_seq_len=2048, seed=3)
+BATCH, PROMPT, NEW_TOKENS = 32, 512, 128
+
+
+def _peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class Clocks:
+    """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = Path(tempfile.mkstemp(prefix="clocks", suffix=".csv")[1])
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index),
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.15)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in self.path.read_text().splitlines():
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 7:
+                    rows.append(parts)
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(rows[0][1]),
+                "samples": len(rows), "reasons": reasons}
+
+
+def cpu_oracle_decode(steps: int, warmup: int, threads: int, layers: int | None = None) -> dict:
+    """Time the CPU oracle of the c4 decode step (fp32, torch CPU, all host cores).
+
+    The sample: decode steps of the full batch at context 513+ over a KV cache
+    prefilled with seeded random values (a real 512-token prefill would cost
+    ~22 TFLOP on the CPU); weights ~ N(0,0.02) like the GPU arm.
+    """
+    from oracle import nebula as orc
+
+    torch.set_num_threads(threads)
+    cfg = dict(C4)
+    nl = layers or cfg["num_layers"]
+    h, f, v = cfg["hidden_size"], cfg["intermediate_size"], cfg["vocab_size"]
+    g = torch.Generator().manual_seed(3)
+    w = {"tok": torch.randn(v, h, generator=g) * 0.02, "pos": torch.randn(cfg["max_seq_len"], h, generator=g) * 0.02,
+         "lnf_w": torch.ones(h), "lnf_b": torch.zeros(h), "head": torch.randn(v, h, generator=g) * 0.02}
+    for i in range(nl):
+        w[f"{i}.ln1_w"], w[f"{i}.ln1_b"] = torch.ones(h), torch.zeros(h)
+        w[f"{i}.ln2_w"], w[f"{i}.ln2_b"] = torch.ones(h), torch.zeros(h)
+        for name, shape in (("q", (h, h)), ("k", (h, h)), ("v", (h, h)), ("o", (h, h)), ("up", (f, h)), ("down", (h, f))):
+            w[f"{i}.{name}"] = torch.randn(*shape, generator=g) * 0.02
+    heads, hd = cfg["num_heads"], h // cfg["num_heads"]
+    cap = PROMPT + warmup + steps + 1
+    caches = [(torch.randn(BATCH, heads, cap, hd, generator=g), torch.randn(BATCH, heads, cap, hd, generator=g))
+              for _ in range(nl)]
+    tok = torch.randint(0, v, (BATCH, 1), generator=g)
+    pos = PROMPT
+    times = []
+    for it in range(warmup + steps):
+        t0 = time.perf_counter()
+        logits = orc.forward(w, tok, heads, nl, caches=caches, start_pos=pos)
+        tok = logits[:, -1].argmax(-1, keepdim=True)
+        dt = time.perf_counter() - t0
+        if it >= warmup:
+            times.append(dt)
+        pos += 1
+    total = sum(times)
+    scale = cfg["num_layers"] / nl
+    return {"value": BATCH * len(times) / (total * scale), "unit": "tokens/s", "cores": threads,
+            "seconds": total, "steps": len(times),
+            "sample": f"{len(times)} decode steps, batch {BATCH}, context {PROMPT + warmup + 1}.."
+                      f"{PROMPT + warmup + len(times)}, fp32 torch CPU oracle (oracle/nebula.py), "
+                      f"{nl} of {cfg['num_layers']} layers timed and scaled, KV prefilled with random values"}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    res = cpu_oracle_decode(args.steps, args.warmup, threads, layers=args.cpu_layers)
+    line = {
+        "metric": "nebula_decode_tokens_per_s", "value": res["value"], "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": res["steps"], "warmup": args.warmup,
+        "ms_per_step": 1000 * res["seconds"] / max(res["steps"], 1), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": "nebula_c4_greedy_decode", "batch": BATCH, "prompt_len": PROMPT,
+                   "parallelism": "cpu", "model": "12L d2048 h16x128 ffn8192 v32000"},
+        "cpu_baseline": {"value": res["value"], "unit": "tokens/s", "cores": res["cores"], "kind": "port",
+                         "sample": res["sample"]},
+        "e2e": {"value": res["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def gemm_headline(dev) -> dict:
+    """Fused linear+GELU GEMM at 8192^3 bf16 (BASELINE config 3 headline shape)."""
+    from forgeml_b200.forgeml import kernels
+    from forgeml_b200.workloads import make_c3_operands
+
+    m = n = k = 8192
+    a, b, bias = make_c3_operands(m, n, k, torch.bfloat16, device=str(dev))
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    for _ in range(3):
+        kernels.matmul(a, b, bias, activation="gelu", out=out)
+    torch.cuda.synchronize()
+    reps = 10
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        kernels.matmul(a, b, bias, activation="gelu", out=out)
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / reps
+    tf = 2 * m * n * k / (ms * 1e-3) / 1e12
+    pk = _peaks()
+    return {"shape": "8192x8192x8192 bf16 +bias +gelu(erf), B [K,N] N-major", "ms": ms, "tflops": tf,
+            "peak_tflops": pk["bf16_tflops"], "frac": tf / pk["bf16_tflops"], "peak_source": pk["source"]}
+
+
+def attention_roofline(engine, dev, ctx_len: int) -> dict:
+    """Time the decode-attention kernel alone on the engine's own cache pool."""
+    from forgeml_b200.nebula import ops
+
+    dec = engine.decoder
+    lid = dec.owned_layer_ids[0]
+    hl, hd = dec.num_heads_local, dec.head_dim
+    q = torch.randn(BATCH, 1, hl, hd, device=dev, dtype=dec.dtype)
+    slots = torch.arange(BATCH, dtype=torch.int32, device=dev)
+    starts = torch.full((BATCH,), ctx_len - 1, dtype=torch.int32, device=dev)
+    kp, vp = dec.cache.k_pool[lid], dec.cache.v_pool[lid]
+    out = torch.empty(BATCH, 1, hl * hd, device=dev, dtype=dec.dtype)
+    for _ in range(5):
+        ops.attention(q, kp, vp, slots, starts, out)
+    torch.cuda.synchronize()
+    reps = 50
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        ops.attention(q, kp, vp, slots, starts, out)
+    e.record()
+    torch.cuda.synchronize()
+    sec = s.elapsed_time(e) / reps * 1e-3
+    es = torch.empty((), dtype=dec.dtype).element_size()
+    algo = BATCH * hl * (2 * ctx_len * hd + 2 * hd) * es  # K + V rows + q + out
+    pk = _peaks()
+    ach = algo / sec / 1e9
+    return {"kernel": "neb_attn_kernel (decode attention over the KV pool)", "bound": "hbm",
+            "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"],
+            "peak_source": pk["source"], "algorithmic_bytes_per_launch": algo, "us_per_launch": sec * 1e6,
+            "context": ctx_len, "traffic": None}
+
+
+def run_native(args) -> None:
+    import torch.distributed as dist
+
+    from forgeml_b200 import _native
+    from forgeml_b200.nebula import DecoderConfig, Engine, ParallelContext
+    from forgeml_b200.nebula import ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    ctx = ParallelContext.from_env(tp_size=world, pp_size=1, device="cuda", timeout_s=120.0)
+    dev = ctx.device
+    rank = ctx.rank
+    cfg = DecoderConfig(**C4)
+    engine = Engine(cfg, context=ctx, dtype=torch.bfloat16, max_requests=BATCH, init="normal")
+    dec = engine.decoder
+    g = torch.Generator().manual_seed(C4["seed"])
+    prompts = torch.randint(0, cfg.vocab_size, (BATCH, PROMPT), generator=g)
+    ids = tuple(range(100, 100 + BATCH))
+    W, K = args.warmup, args.steps
+    if PROMPT + W + K + 2 > cfg.max_seq_len:
+        raise SystemExit("warmup + steps exceed the context capacity")
+
+    def sync_all():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+
+    # ---- device-timed decode (SPMD: every rank runs the same steps) ----
+    with torch.inference_mode():
+        logits = dec.forward(prompts.to(dev), ids, 0, last_only=True)
+        nxt = ops.argmax(logits[:, -1, :])
+        pos = PROMPT
+        launches0 = _native.launch_count()
+        for _ in range(W):
+            logits = dec.forward(nxt.view(-1, 1), ids, pos, last_only=True)
+            nxt = ops.argmax(logits[:, -1, :])
+            pos += 1
+        per_step_launches = None
+        sync_all()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with Clocks(dev.index) as clk:
+            sync_all()
+            ev0.record()
+            for _ in range(K):
+                logits = dec.forward(nxt.view(-1, 1), ids, pos, last_only=True)
+                nxt = ops.argmax(logits[:, -1, :])
+                pos += 1
+            ev1.record()
+            sync_all()
+        ms = ev0.elapsed_time(ev1)
+        # native launches per step: a captured step replays the kernels counted at capture
+        graphed = world == 1 and dec.use_cuda_graphs
+        if graphed:
+            n0 = _native.launch_count()
+            dec._graphs.clear()
+            logits = dec.forward(nxt.view(-1, 1), ids, pos, last_only=True)  # recapture counts its kernels
+            per_step_launches = (_native.launch_count() - n0) // 2 + 1  # eager warm-up + capture, + argmax
+            nxt = ops.argmax(logits[:, -1, :])
+            pos += 1
+        else:
+            n0 = _native.launch_count()
+            logits = dec.forward(nxt.view(-1, 1), ids, pos, last_only=True)
+            nxt = ops.argmax(logits[:, -1, :])
+            per_step_launches = _native.launch_count() - n0
+            pos += 1
+        t = torch.tensor([ms], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        value = BATCH * K / (ms * 1e-3)
+        dec.cache.release(ids)
+        torch.cuda.synchronize(dev)
+
+    # ---- end-to-end through the public Engine API (host tokens in, ids out) ----
+    e2e = None
+    if world == 1:
+        with torch.inference_mode():
+            host_tok = torch.empty(BATCH, 1, dtype=torch.long).pin_memory()
+            host_out = torch.empty(BATCH, dtype=torch.long).pin_memory()
+            logits = engine.forward(prompts, ids, 0, _internal=True, _last_only=True)
+            host_out.copy_(ops.argmax(logits[:, -1, :]))
+            pos = PROMPT
+            for _ in range(W):
+                host_tok.copy_(host_out.view(-1, 1))
+                logits = engine.forward(host_tok, ids, pos, _internal=True, _last_only=True)
+                host_out.copy_(ops.argmax(logits[:, -1, :]))
+                pos += 1
+            torch.cuda.synchronize(dev)
+            t0 = time.perf_counter()
+            for _ in range(K):
+                host_tok.copy_(host_out.view(-1, 1))
+                logits = engine.forward(host_tok, ids, pos, _internal=True, _last_only=True)
+                host_out.copy_(ops.argmax(logits[:, -1, :]))  # device->host read of the step's result
+                pos += 1
+            torch.cuda.synchronize(dev)
+            e2e_s = time.perf_counter() - t0
+            engine.release(ids)
+        e2e = {"value": BATCH * K / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": BATCH * 8,
+               "d2h_bytes_per_step": BATCH * 8,
+               "path": "Engine.forward(host int64 tokens) + native argmax + D2H ids, per step"}
+
+    extra = {}
+    if rank == 0:
+        extra["roofline"] = attention_roofline(engine, dev, PROMPT + W + K)
+        if world == 1 and not args.no_gemm:
+            extra["gemm"] = gemm_headline(dev)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_oracle_decode(args.cpu_steps, 1, os.cpu_count() or 1, layers=args.cpu_layers)
+        cpu = {k: cpu[k] for k in ("value", "unit", "cores", "sample")} | {"kind": "port"}
+    if rank == 0:
+        line = {
+            "metric": "nebula_decode_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "nebula_c4_greedy_decode", "model": "12L d2048 h16x128 ffn8192 v32000",
+                       "global_batch": BATCH, "prompt_len": PROMPT, "context": [PROMPT + W + 1, PROMPT + W + K],
+                       "parallelism": f"tp{world}", "cuda_graph": bool(world == 1 and dec.use_cuda_graphs),
+                       "l2": "inputs larger than L2 (>3 GB streamed per step)"},
+            "e2e": e2e, "gpu_launches": int(per_step_launches * K), "clocks": clk.summary(),
+            "cpu_baseline": cpu, **extra,
+        }
+        print(json.dumps(line), flush=True)
+    engine.close()
+    if world > 1:
+        dist.barrier()
+        ctx.close()
+
+
+def run_case(args) -> None:
+    """Single-kernel micro-benchmarks on small device footprints (for ncu captures).
+
+    attention    decode attention, batch 32 x 16 heads x 128, context 1024,
+                 one layer's KV pool (268 MB, > L2)
+    gemm-decode  the c4 decode GEMMs at batch 32: QKV 6144x2048, o 2048x2048
+                 (+residual), up 8192x2048 (+tanh GELU), down 2048x8192 (+residual),
+                 lm_head 32000x2048
+    gemm         8192^3 bf16 + bias + GELU
+    """
+    from forgeml_b200.forgeml import kernels
+    from forgeml_b200.nebula import ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    reps = args.steps
+    res = {}
+
+    def timed(fn, n):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(n):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / n * 1e3  # us
+
+    g = torch.Generator(device=dev).manual_seed(0)
+    if args.case == "attention":
+        b, h, d, ctx = BATCH, 16, 128, 1024
+        kp = torch.randn(b, h, ctx, d, device=dev, generator=g).to(torch.bfloat16)
+        vp = torch.randn(b, h, ctx, d, device=dev, generator=g).to(torch.bfloat16)
+        q = torch.randn(b, 1, h, d, device=dev, generator=g).to(torch.bfloat16)
+        slots = torch.arange(b, dtype=torch.int32, device=dev)
+        starts = torch.full((b,), ctx - 1, dtype=torch.int32, device=dev)
+        out = torch.empty(b, 1, h * d, device=dev, dtype=torch.bfloat16)
+        us = timed(lambda: ops.attention(q, kp, vp, slots, starts, out), reps)
+        algo = b * h * (2 * ctx * d + 2 * d) * 2
+        res["attention"] = {"us": us, "GB/s": algo / (us * 1e-6) / 1e9, "algo_bytes": algo}
+    elif args.case == "gemm-decode":
+        m = BATCH
+        for name, n, k, act, resid in (("qkv", 6144, 2048, 0, False), ("o", 2048, 2048, 0, True),
+                                       ("up", 8192, 2048, 2, False), ("down", 2048, 8192, 0, True),
+                                       ("lm_head", 32000, 2048, 0, False)):
+            x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+            w = (torch.randn(n, k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+            r = torch.randn(m, n, device=dev, generator=g).to(torch.bfloat16) if resid else None
+            out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+            actn = "gelu" if act else "none"
+            apx = "tanh" if act == 2 else "none"
+            us = timed(lambda: kernels.matmul(x, w.t(), activation=actn, approximate=apx, out=out, residual=r), reps)
+            algo = (n * k + m * k + m * n * (2 if resid else 1)) * 2
+            res[name] = {"us": us, "GB/s": algo / (us * 1e-6) / 1e9, "TFLOP/s": 2 * m * n * k / (us * 1e-6) / 1e12}
+    elif args.case == "gemm":
+        res["gemm"] = gemm_headline(dev)
+    print(json.dumps({"case": args.case, "results": res}), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("native", "reference"), default="native")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU oracle baseline")
+    ap.add_argument("--no-gemm", action="store_true")
+    ap.add_argument("--cpu-steps", type=int, default=3)
+    ap.add_argument("--cpu-layers", type=int, default=None, help="time this many layers of the CPU oracle")
+    ap.add_argument("--case", choices=("attention", "gemm-decode", "gemm"), default=None,
+                    help="run one kernel micro-benchmark instead of the decode bench")
+    args = ap.parse_args()
+    if args.case:
+        run_case(args)
+        return
+    if args.warmup < 3 and args.impl == "native":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_native(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -67,6 +67,11 @@ _SIGNATURES = {
         [_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I, _I,
          ctypes.POINTER(fml_tile_cfg), _P, ctypes.c_size_t, _P],
     ),
+    "fml_packed_weight_bytes": (ctypes.c_size_t, [_I64, _I64, _I]),
+    "fml_pack_weight": (_I, [_P, _I64, _I64, _I64, _I, _P, _P]),
+    "fml_linear_packed": (
+        _I, [_P, _I64, _P, _I64, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I, _I, ctypes.POINTER(fml_tile_cfg), _P]
+    ),
     "fml_layernorm": (_I, [_P, _I64, _P, _P, _F, _P, _I64, _I64, _I64, _I, _P]),
     "fml_sdpa": (
         _I,

@@ -47,14 +47,39 @@ __device__ __forceinline__ void cluster_sync_all() {
 // ===========================================================================
 // Nebula attention over the KV pool
 // ===========================================================================
-constexpr int kAttnWarps = 4;
+constexpr int kAttnWarps = 8;
 constexpr int kUnroll = 4;
 constexpr int kMaxD = 256;
+
+// One lane's share of a K or V row.  VEC: a raw 16-byte slice at element
+// gl*VE (converted on use).  !VEC: elements gl, gl+G, ... as floats.
+template <typename T, bool VEC, int VE>
+struct RowSlice;
+template <typename T, int VE>
+struct RowSlice<T, true, VE> {
+  uint4 raw;
+  __device__ __forceinline__ void load(const T* row, int gl, int, int, bool ok) {
+    raw = ok ? __ldg(reinterpret_cast<const uint4*>(row + gl * VE)) : make_uint4(0, 0, 0, 0);
+  }
+  __device__ __forceinline__ float get(int i) const { return to_f32<T>(reinterpret_cast<const T*>(&raw)[i]); }
+};
+template <typename T, int VE>
+struct RowSlice<T, false, VE> {
+  float v[VE];
+  __device__ __forceinline__ void load(const T* row, int gl, int G, int D, bool ok) {
+#pragma unroll
+    for (int i = 0; i < VE; ++i) {
+      const int d = gl + G * i;
+      v[i] = (ok && d < D) ? to_f32<T>(row[d]) : 0.f;
+    }
+  }
+  __device__ __forceinline__ float get(int i) const { return v[i]; }
+};
 
 // VEC: each lane of a G-lane group owns one 16-byte slice of the D-vector.
 // !VEC: each lane owns elements gl, gl+G, ... (scalar loads; odd head sizes).
 template <typename T, int G, bool VEC>
-__global__ void __launch_bounds__(kAttnWarps * 32)
+__global__ void __launch_bounds__(kAttnWarps * 32, 3)
     neb_attn_kernel(const T* __restrict__ q, long long qs0, long long qs1, long long qs2,
                     const T* __restrict__ kpool, const T* __restrict__ vpool,
                     const int32_t* __restrict__ slot_of, const int32_t* __restrict__ start_pos,
@@ -119,35 +144,16 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
 
   constexpr int KB = KPW * kUnroll;  // keys per warp iteration
   for (int base = lo + warp * KB; base < hi; base += kAttnWarps * KB) {
-    float kv[kUnroll][VE], vv[kUnroll][VE];
+    // Issue every load of this iteration before any use; the 16-byte slices
+    // stay in raw form and are converted where they are consumed.
+    RowSlice<T, VEC, VE> ks[kUnroll], vs[kUnroll];
     bool valid[kUnroll];
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
       const int key = base + u * KPW + group;
       valid[u] = key < hi;
-      const T* kr = kh + (long long)key * D;
-      const T* vr = vh + (long long)key * D;
-      if (VEC) {
-        if (valid[u] && nel) {
-          uint4 rk = *reinterpret_cast<const uint4*>(kr + gl * VE);
-          uint4 rv = *reinterpret_cast<const uint4*>(vr + gl * VE);
-          const T* ek = reinterpret_cast<const T*>(&rk);
-          const T* ev = reinterpret_cast<const T*>(&rv);
-#pragma unroll
-          for (int i = 0; i < VE; ++i) { kv[u][i] = to_f32<T>(ek[i]); vv[u][i] = to_f32<T>(ev[i]); }
-        } else {
-#pragma unroll
-          for (int i = 0; i < VE; ++i) { kv[u][i] = 0.f; vv[u][i] = 0.f; }
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < VE; ++i) {
-          const int d = gl + G * i;
-          const bool ok = valid[u] && d < D;
-          kv[u][i] = ok ? to_f32<T>(kr[d]) : 0.f;
-          vv[u][i] = ok ? to_f32<T>(vr[d]) : 0.f;
-        }
-      }
+      ks[u].load(kh + (long long)key * D, gl, G, D, valid[u] && nel > 0);
+      vs[u].load(vh + (long long)key * D, gl, G, D, valid[u] && nel > 0);
     }
     float s[kUnroll];
     float bmax = -INFINITY;
@@ -155,7 +161,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
     for (int u = 0; u < kUnroll; ++u) {
       float d = 0.f;
 #pragma unroll
-      for (int i = 0; i < VE; ++i) d = fmaf(qv[i], kv[u][i], d);
+      for (int i = 0; i < VE; ++i) d = fmaf(qv[i], ks[u].get(i), d);
 #pragma unroll
       for (int off = G / 2; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
       s[u] = valid[u] ? d : -INFINITY;
@@ -173,7 +179,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
       const float pr = expf(s[u] - m_new);
       l += pr;
 #pragma unroll
-      for (int i = 0; i < VE; ++i) o[i] = fmaf(pr, vv[u][i], o[i]);
+      for (int i = 0; i < VE; ++i) o[i] = fmaf(pr, vs[u].get(i), o[i]);
     }
     m = m_new;
   }
@@ -449,9 +455,14 @@ extern "C" int neb_attention(const void* q, const int64_t q_strides[4], const vo
   if (head_dim > attn::kMaxD) return fail(FML_EUNSUPPORTED, "neb_attention: head_dim > 256");
   if (q_strides[3] != 1) return fail(FML_EUNSUPPORTED, "neb_attention: q innermost stride must be 1");
   if (batch * t * heads * 8 > (1ll << 31) - 1) return fail(FML_EUNSUPPORTED, "neb_attention: too many queries");
-  // Key splits per query: enough CTAs to cover the context in <= 256-key
-  // chunks, combined in a cluster of at most 8.
-  int nsplit = (int)std::min<long long>(8, std::max<long long>(1, (max_seq + 255) / 256));
+  // Key splits per query (combined in a cluster of at most 8): enough CTAs to
+  // fill every SM about eight times over, but no more, so each CTA streams a
+  // long run of keys.  Depends only on the launch shape (not on the device-side
+  // positions), so a captured decode step keeps a valid split.
+  const long long nq = batch * t * heads;
+  const long long target = 8LL * num_sms(current_device());
+  int nsplit = (int)std::min<long long>(8, std::max<long long>(1, (target + nq - 1) / nq));
+  nsplit = (int)std::min<long long>(nsplit, std::max<long long>(1, max_seq / 64));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == FML_F32)
     return attn::dispatch_neb<float>(q, q_strides, k_pool, v_pool, slot_of, start_pos, out, batch,

@@ -103,11 +103,13 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
                : "memory");
 }
+// Non-blocking probe of an mbarrier phase (test_wait never suspends the
+// thread, so a poller sees the phase flip as soon as it happens).
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
@@ -118,7 +120,7 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
@@ -126,35 +128,34 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
   return ok != 0;
 }
 
-__device__ __forceinline__ uint64_t globaltimer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Every wait in these kernels is bounded: after kWaitBudgetNs the wait gives
-// up, raises `err` in the device error word and returns false so the caller
-// can unwind (drain its own copies, free TMEM, return) instead of hanging.
-constexpr uint64_t kWaitBudgetNs = 2000000000ull;  // 2 s
+// Every wait in these kernels is bounded: after kWaitBudgetCycles SM clock
+// cycles (about 2 s at the B200's clocks, longer when throttled) the wait
+// gives up, raises `err` in the device error word and returns false so the
+// caller can unwind (drain its own copies, free TMEM, return) instead of
+// hanging.  The budget is measured with clock64(), which is cheap to read.
+constexpr long long kWaitBudgetCycles = 4000000000LL;
 
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int err) {
   if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = globaltimer_ns();
+  const long long t0 = clock64();
   while (true) {
-    for (int i = 0; i < 64; ++i)
+#pragma unroll 1
+    for (int i = 0; i < 256; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+    if (clock64() - t0 > kWaitBudgetCycles) {
       raise_device_error(err);
       return false;
     }
   }
 }
 __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int err) {
-  uint64_t t0 = globaltimer_ns();
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const long long t0 = clock64();
   while (true) {
-    for (int i = 0; i < 64; ++i)
+#pragma unroll 1
+    for (int i = 0; i < 256; ++i)
       if (mbar_try_wait_cluster(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+    if (clock64() - t0 > kWaitBudgetCycles) {
       raise_device_error(err);
       return false;
     }
@@ -175,6 +176,15 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint32_t bar
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Untiled bulk copy global -> this CTA's shared memory (16-byte aligned
+// addresses, size a multiple of 16); completion as transaction bytes on `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
       : "memory");
 }
 

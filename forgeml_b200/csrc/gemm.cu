@@ -28,8 +28,10 @@
 // memory (no global scratch), each CTA reducing a slice of the rows.
 #include <algorithm>
 #include <cstdio>
+#include <map>
 #include <mutex>
 #include <string>
+#include <tuple>
 
 #include "common.cuh"
 
@@ -46,6 +48,7 @@ constexpr int kPromoteKb = 2;  // K slabs per promoted chunk (fp32 path)
 struct Params {
   int I, J;              // rows of P and of Q (MMA space)
   int num_kb;            // K blocks of kSlab bytes over the (effective) reduction
+  int slabs;             // K slabs carried by one pipeline stage (1, 2 or 4)
   int tiles_i, tiles_j, num_tiles, group_i;
   int ksplit;            // CTAs per cluster sharing one tile's K range
   int fmt;               // 0 f16, 1 bf16, 2 tf32
@@ -64,6 +67,7 @@ struct Params {
   int rows_out, cols_out;  // M, N of the output
   int red_stride;          // floats per row of the split-K partial buffer
   int promote_kb;          // K slabs per TMEM chunk when partial sums are promoted to registers
+  const uint8_t* p_packed; // P pre-packed as swizzled 16 KB tiles (nullptr: P comes through tmP)
 };
 
 struct Smem {
@@ -119,6 +123,14 @@ __device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
 __device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
   return v;
 }
 __device__ __forceinline__ void cluster_sync_all() {
@@ -216,8 +228,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   Smem s;
   s.stage_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  s.p_bytes = kBM * kSlab;
-  s.stage_bytes = s.p_bytes + BN * kSlab;
+  const int S = p.slabs;
+  s.p_bytes = S * kBM * kSlab;
+  s.stage_bytes = S * (kBM + BN) * kSlab;
   s.bars = s.stage_base + p.stages * s.stage_bytes;
   s.red = s.bars + kBarBytes;
   s.red = (s.red + 15u) & ~15u;
@@ -277,23 +290,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
         int ti, tj;
         tile_coords(p, t, ti, tj);
-        for (int kb = kb_begin; kb < kb_end; ++kb) {
+        for (int kb = kb_begin; kb < kb_end; kb += S) {
           if (!mbar_wait(bar_empty(s, stage), phase ^ 1u, DEV_ERR_GEMM_TIMEOUT)) { ok = false; break; }
+          const int nsl = min(S, kb_end - kb);
           const uint32_t fb = bar_full(s, stage);
-          mbar_arrive_expect_tx(fb, s.stage_bytes);
-          const uint32_t sp = s.stage_base + stage * s.stage_bytes;
-          const uint32_t sq = sp + s.p_bytes;
-          if (!p.p_mn) {
-            tma_load_2d(&tmP, fb, sp, kb * bke, ti * kBM);
-          } else {
-            for (int b = 0; b < kBM / mn_box; ++b)
-              tma_load_2d(&tmP, fb, sp + b * slab_box_bytes, ti * kBM + b * mn_box, kb * bke);
-          }
-          if (!p.q_mn) {
-            tma_load_2d(&tmQ, fb, sq, kb * bke, tj * BN);
-          } else {
-            for (int b = 0; b < BN / mn_box; ++b)
-              tma_load_2d(&tmQ, fb, sq + b * slab_box_bytes, tj * BN + b * mn_box, kb * bke);
+          mbar_arrive_expect_tx(fb, (uint32_t)nsl * (kBM + BN) * kSlab);
+          const uint32_t sp0 = s.stage_base + stage * s.stage_bytes;
+          const uint32_t sq0 = sp0 + s.p_bytes;
+          for (int sl = 0; sl < nsl; ++sl) {
+            const int kk = kb + sl;
+            const uint32_t sp = sp0 + sl * (kBM * kSlab);
+            const uint32_t sq = sq0 + sl * (BN * kSlab);
+            if (p.p_packed != nullptr) {
+              // One sequential 16 KB copy: the tile is stored pre-swizzled.
+              bulk_load(sp, p.p_packed + ((size_t)ti * p.num_kb + kk) * (size_t)(kBM * kSlab),
+                        kBM * kSlab, fb);
+            } else if (!p.p_mn) {
+              tma_load_2d(&tmP, fb, sp, kk * bke, ti * kBM);
+            } else {
+              for (int b = 0; b < kBM / mn_box; ++b)
+                tma_load_2d(&tmP, fb, sp + b * slab_box_bytes, ti * kBM + b * mn_box, kk * bke);
+            }
+            if (!p.q_mn) {
+              tma_load_2d(&tmQ, fb, sq, kk * bke, tj * BN);
+            } else {
+              for (int b = 0; b < BN / mn_box; ++b)
+                tma_load_2d(&tmQ, fb, sq + b * slab_box_bytes, tj * BN + b * mn_box, kk * bke);
+            }
           }
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -335,18 +358,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!mbar_wait(bar_tempty(s, acc), acc_phase ^ 1u, DEV_ERR_GEMM_TIMEOUT)) { ok = false; break; }
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + acc * kAccStride;
-          for (; kb < kb_stop; ++kb) {
+          for (; kb < kb_stop; kb += S) {
             if (!mbar_wait(bar_full(s, stage), phase, DEV_ERR_GEMM_TIMEOUT)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t sp = s.stage_base + stage * s.stage_bytes;
-            const uint32_t sq = sp + s.p_bytes;
+            const int nsl = min(S, kb_end - kb);
+            const uint32_t sp0 = s.stage_base + stage * s.stage_bytes;
+            const uint32_t sq0 = sp0 + s.p_bytes;
+            for (int sl = 0; sl < nsl; ++sl) {
+              const uint32_t sp = sp0 + sl * (kBM * kSlab);
+              const uint32_t sq = sq0 + sl * (BN * kSlab);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint64_t ad = umma_desc_sw128(sp + k * p_kstep, p_lbo, 1024u);
-              const uint64_t bd = umma_desc_sw128(sq + k * q_kstep, q_lbo, 1024u);
-              const uint32_t accum = (kb > chunk_begin || k > 0) ? 1u : 0u;
-              if (p.fmt == 2) umma_tf32(d_tmem, ad, bd, idesc, accum);
-              else umma_f16(d_tmem, ad, bd, idesc, accum);
+              for (int k = 0; k < 4; ++k) {
+                const uint64_t ad = umma_desc_sw128(sp + k * p_kstep, p_lbo, 1024u);
+                const uint64_t bd = umma_desc_sw128(sq + k * q_kstep, q_lbo, 1024u);
+                const uint32_t accum = (kb > chunk_begin || sl > 0 || k > 0) ? 1u : 0u;
+                if (p.fmt == 2) umma_tf32(d_tmem, ad, bd, idesc, accum);
+                else umma_f16(d_tmem, ad, bd, idesc, accum);
+              }
             }
             umma_commit(bar_empty(s, stage));
             if (++stage == p.stages) { stage = 0; phase ^= 1u; }
@@ -458,15 +486,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait_cluster(bar_red_ready(s), red_phase, DEV_ERR_REDUCE_TIMEOUT)) { ok = false; break; }
         const int rows_per = kBM / ksplit;
         const int r0 = crank * rows_per;
-        const int slice = rows_per * BN;
-        for (int idx = ep_tid; idx < slice; idx += 128) {
-          int rr, cc;
-          if (p.swap) { rr = idx % rows_per; cc = idx / rows_per; }
-          else { rr = idx / BN; cc = idx % BN; }
-          const uint32_t local = s.red + (uint32_t)(((r0 + rr) * p.red_stride + cc) * 4);
-          float sum = 0.f;
-          for (int r = 0; r < ksplit; ++r) sum += ld_cluster_f32(mapa(local, r));
-          epilogue_store(p, ti * kBM + r0 + rr, tj * BN + cc, sum);
+        constexpr int kGroups = BN / 4 > 0 ? BN / 4 : 1;  // 4-column groups per row
+        const int items = rows_per * kGroups;
+        for (int idx = ep_tid; idx < items; idx += 128) {
+          // swap: consecutive threads take consecutive rows (output columns) so
+          // the stores coalesce; otherwise consecutive column groups.
+          int rr, cg;
+          if (p.swap) { rr = idx % rows_per; cg = idx / rows_per; }
+          else { rr = idx / kGroups; cg = idx % kGroups; }
+          const uint32_t local = s.red + (uint32_t)(((r0 + rr) * p.red_stride + 4 * cg) * 4);
+          float4 part[8];
+#pragma unroll
+          for (int r = 0; r < 8; ++r)  // all remote loads in flight before any use
+            if (r < ksplit) part[r] = ld_cluster_f32x4(mapa(local, r));
+          float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int r = 0; r < 8; ++r)
+            if (r < ksplit) { sum.x += part[r].x; sum.y += part[r].y; sum.z += part[r].z; sum.w += part[r].w; }
+          const int i = ti * kBM + r0 + rr, j = tj * BN + 4 * cg;
+          epilogue_store(p, i, j, sum.x);
+          epilogue_store(p, i, j + 1, sum.y);
+          epilogue_store(p, i, j + 2, sum.z);
+          epilogue_store(p, i, j + 3, sum.w);
         }
         epi_bar_sync();
         if (ep_tid == 0) {
@@ -533,6 +574,40 @@ __global__ void pack_kernel(const T* __restrict__ x, long long s_r, long long s_
       if (mode == 1) { d[k] = lo; d[Kp + k] = hi; d[2 * Kp + k] = hi; }
       else { d[k] = hi; d[Kp + k] = lo; d[2 * Kp + k] = hi; }
     }
+  }
+}
+
+// Constant-weight packing: W [N, K] (K contiguous, nn.Linear layout) becomes
+// tiles of 128 rows x one 128-byte K slab, each stored exactly as the
+// SWIZZLE_128B K-major shared-memory image the UMMA descriptor expects
+// (16-byte chunk c of row r at r*128 + (c ^ (r & 7))*16), tiles of one
+// 128-row band consecutive along K.  A decode-step GEMM then streams each
+// weight band as one sequential run of 16 KB bulk copies.  Out-of-range rows
+// and columns are zero.
+template <typename T>
+__global__ void pack_weight_kernel(const T* __restrict__ w, long long ldw, int n, int k, int num_kb,
+                                   long long total_chunks, uint8_t* __restrict__ dst) {
+  constexpr int E = 16 / sizeof(T);  // elements per 16-byte chunk
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total_chunks;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(idx & 7);
+    const int r = (int)((idx >> 3) & 127);
+    const long long tile = idx >> 10;          // ti * num_kb + kb
+    const int kb = (int)(tile % num_kb);
+    const long long ti = tile / num_kb;
+    const long long row = ti * kBM + r;
+    const long long col = (long long)kb * (kSlab / sizeof(T)) + c * E;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (row < n) {
+      const T* src = w + row * ldw + col;
+      if (col + E <= k && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        v = *reinterpret_cast<const uint4*>(src);
+      } else {
+        T* e = reinterpret_cast<T*>(&v);
+        for (int i = 0; i < E; ++i) e[i] = (col + i < k) ? src[i] : from_f32<T>(0.f);
+      }
+    }
+    *reinterpret_cast<uint4*>(dst + tile * (kBM * kSlab) + r * kSlab + ((c ^ (r & 7)) * 16)) = v;
   }
 }
 
@@ -637,9 +712,11 @@ static int encode(CUtensorMap* map, const void* ptr, int dtype, bool tf32, bool 
 struct Plan {
   bool swap;
   bool promote;  // fp32: sum TMEM partials in fp32 registers every kPromoteKb slabs
+  bool packed;   // P is a pre-packed constant weight (fml_linear_packed)
   int bn;
   int ksplit;
   int stages;
+  int slabs;     // K slabs per pipeline stage
   Operand P, Q;
   long long keff;  // effective reduction length (3*Kp for tf32)
   size_t ws_bytes;
@@ -647,28 +724,114 @@ struct Plan {
 
 static const int kBNs[] = {16, 32, 64, 128, 256};
 
-static int smem_bytes_for(int bn, int stages, int ksplit, int* red_stride) {
-  int stage_bytes = (kBM + bn) * kSlab;
+static int smem_bytes_for(int bn, int stages, int ksplit, int* red_stride, int slabs = 1) {
+  int stage_bytes = slabs * (kBM + bn) * kSlab;
   int rs = bn + 4;
   if (red_stride) *red_stride = rs;
   int red = ksplit > 1 ? kBM * rs * 4 + 16 : 0;
   return 1024 + stages * stage_bytes + kBarBytes + 16 + red;
 }
 
-static int make_plan(Plan& pl, const void* a, long long lda_m, long long lda_k, const void* b,
-                     long long ldb_k, long long ldb_n, long long M, long long N, long long K,
-                     int dtype, const fml_tile_cfg* cfg, int sms) {
-  // MMA-space orientation.
-  pl.swap = (M <= 128 && N > M);
-  if (pl.swap) {
-    pl.P = Operand{b, ldb_n, ldb_k, N, K, false, false, 0, 0};
-    pl.Q = Operand{a, lda_m, lda_k, M, K, false, false, 0, 0};
-  } else {
-    pl.P = Operand{a, lda_m, lda_k, M, K, false, false, 0, 0};
-    pl.Q = Operand{b, ldb_n, ldb_k, N, K, false, false, 0, 0};
+template <int BN, bool PROMOTE>
+static int resident_ctas_t(int ksplit, int smem, int sms) {
+  cudaFuncSetAttribute(gemm_kernel<BN, PROMOTE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+  if (ksplit <= 1) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemm_kernel<BN, PROMOTE>, kThreads, smem) !=
+            cudaSuccess || per_sm <= 0)
+      per_sm = 1;
+    return per_sm * sms;
   }
-  const long long J = pl.Q.rows, I = pl.P.rows;
-  // UMMA N tile.
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(ksplit);
+  lc.blockDim = dim3(kThreads);
+  lc.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = ksplit;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_kernel<BN, PROMOTE>, &lc) != cudaSuccess || n <= 0) return 0;
+  return n * ksplit;
+}
+
+// CTAs of this kernel configuration that can be resident at once (cached).
+static int resident_ctas(int bn, bool promote, int ksplit, int smem, int sms) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int, int, int>, int> cache;
+  const int dev = current_device();
+  const auto key = std::make_tuple(dev, bn, promote ? 1 : 0, ksplit, smem, sms);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  int r = 0;
+  if (promote) {
+    switch (bn) {
+      case 16: r = resident_ctas_t<16, true>(ksplit, smem, sms); break;
+      case 32: r = resident_ctas_t<32, true>(ksplit, smem, sms); break;
+      case 64: r = resident_ctas_t<64, true>(ksplit, smem, sms); break;
+    }
+  } else {
+    switch (bn) {
+      case 16: r = resident_ctas_t<16, false>(ksplit, smem, sms); break;
+      case 32: r = resident_ctas_t<32, false>(ksplit, smem, sms); break;
+      case 64: r = resident_ctas_t<64, false>(ksplit, smem, sms); break;
+      case 128: r = resident_ctas_t<128, false>(ksplit, smem, sms); break;
+      case 256: r = resident_ctas_t<256, false>(ksplit, smem, sms); break;
+    }
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  cache[key] = r;
+  return r;
+}
+
+static int stages_for(int bn, int ksplit, const fml_tile_cfg* cfg, int slabs) {
+  int stages = kMaxStages;
+  if (cfg && cfg->num_stages > 0) stages = std::min(cfg->num_stages, kMaxStages);
+  while (stages > 2 && smem_bytes_for(bn, stages, ksplit, nullptr, slabs) > kSmemLimit) --stages;
+  return stages;
+}
+
+// K slabs per stage: block_k elements of K per stage when hinted; by default
+// four slabs (64 KB of weights per stage) for the bandwidth-bound narrow tiles
+// (BN <= 64) and one slab for the wide compute-bound tiles.
+static int slabs_for(const fml_tile_cfg* cfg, int dtype, bool promote, int bn) {
+  if (promote) return 1;
+  if (!cfg || cfg->block_k <= 0) return bn <= 64 ? 4 : 1;
+  const int s = cfg->block_k * (int)dtype_size(dtype) / kSlab;
+  return s >= 4 ? 4 : (s >= 2 ? 2 : 1);
+}
+
+// Split-K and pipeline depth.  Each candidate split is costed by the rounds of
+// co-resident CTAs it needs times the K slabs each CTA streams, plus a fixed
+// per-tile cost and the cluster reduction; a split whose clusters cannot all
+// be resident at once pays for the extra round.
+static void choose_split(Plan& pl, long long tiles, long long num_kb, const fml_tile_cfg* cfg, int sms) {
+  int best_ks = 1;
+  double best_cost = 1e30;
+  for (int ks : {1, 2, 4, 8}) {
+    if (ks > 1 && (pl.bn > 128 || num_kb < 2LL * ks || tiles * 2 > sms)) continue;
+    const int st = stages_for(pl.bn, ks, cfg, pl.slabs);
+    const int smem = smem_bytes_for(pl.bn, st, ks, nullptr, pl.slabs);
+    if (smem > kSmemLimit) continue;
+    const int res = resident_ctas(pl.bn, pl.promote, ks, smem, sms);
+    if (res <= 0) continue;
+    const long long ctas = tiles * ks;
+    const long long rounds = (ctas + res - 1) / res;
+    const double per_cta = (double)((num_kb + ks - 1) / ks) + 6.0;
+    const double cost = rounds * per_cta + (ks > 1 ? 4.0 : 0.0);
+    if (cost < best_cost - 1e-9) { best_cost = cost; best_ks = ks; }
+  }
+  pl.ksplit = best_ks;
+  pl.stages = stages_for(pl.bn, best_ks, cfg, pl.slabs);
+}
+
+static int pick_bn(const Plan& pl, long long I, long long J, const fml_tile_cfg* cfg, int sms) {
   int bn = 256;
   if (cfg && cfg->block_n > 0) {
     bn = 0;
@@ -691,12 +854,27 @@ static int make_plan(Plan& pl, const void* a, long long lda_m, long long lda_k, 
     if (J <= 128) { for (int c : kBNs) if (c >= J) { bn = c; break; } }
     else if (util(128) > util(256) * 1.15) bn = 128;
   }
-  pl.promote = (dtype == FML_F32);
   if (pl.promote && bn > 64) bn = 64;  // register-resident row accumulator
-  pl.bn = bn;
+  return bn;
+}
+
+static int make_plan(Plan& pl, const void* a, long long lda_m, long long lda_k, const void* b,
+                     long long ldb_k, long long ldb_n, long long M, long long N, long long K,
+                     int dtype, const fml_tile_cfg* cfg, int sms) {
+  pl.packed = false;
+  pl.swap = (M <= 128 && N > M);
+  if (pl.swap) {
+    pl.P = Operand{b, ldb_n, ldb_k, N, K, false, false, 0, 0};
+    pl.Q = Operand{a, lda_m, lda_k, M, K, false, false, 0, 0};
+  } else {
+    pl.P = Operand{a, lda_m, lda_k, M, K, false, false, 0, 0};
+    pl.Q = Operand{b, ldb_n, ldb_k, N, K, false, false, 0, 0};
+  }
+  const long long J = pl.Q.rows, I = pl.P.rows;
+  pl.promote = (dtype == FML_F32);
+  pl.bn = pick_bn(pl, I, J, cfg, sms);
   classify(pl.P, dtype, kBM, true);
-  classify(pl.Q, dtype, bn, true);
-  // Effective K and packing layout.
+  classify(pl.Q, dtype, pl.bn, true);
   const long long es = (long long)dtype_size(dtype);
   const long long kp = round_up(K, 16 / es);
   pl.keff = dtype == FML_F32 ? 3 * kp : K;
@@ -708,23 +886,11 @@ static int make_plan(Plan& pl, const void* a, long long lda_m, long long lda_k, 
     ws += (size_t)round_up(o->rows * (dtype == FML_F32 ? 3 * kp : kp) * es, 256);
   }
   pl.ws_bytes = ws;
-  // Split-K through the cluster when there are too few tiles to fill the GPU.
-  const long long tiles = ((I + kBM - 1) / kBM) * ((J + bn - 1) / bn);
+  const long long tiles = ((I + kBM - 1) / kBM) * ((J + pl.bn - 1) / pl.bn);
   const long long num_kb = (pl.keff * es + kSlab - 1) / kSlab;
-  int ks = 1;
-  if (bn <= 128 && tiles * 2 <= sms && num_kb >= 8) {
-    long long want = sms / std::max<long long>(tiles, 1);
-    want = std::min<long long>(want, num_kb / 4);
-    want = std::min<long long>(want, 8);
-    while (want > 1 && (kBM % want) != 0) --want;  // rows split evenly
-    ks = (int)std::max<long long>(want, 1);
-  }
-  pl.ksplit = ks;
-  int stages = kMaxStages;
-  if (cfg && cfg->num_stages > 0) stages = std::min(cfg->num_stages, kMaxStages);
-  while (stages > 2 && smem_bytes_for(bn, stages, ks, nullptr) > kSmemLimit) --stages;
-  pl.stages = stages;
-  if (smem_bytes_for(bn, stages, ks, nullptr) > kSmemLimit)
+  pl.slabs = slabs_for(cfg, dtype, pl.promote, pl.bn);
+  choose_split(pl, tiles, num_kb, cfg, sms);
+  if (smem_bytes_for(pl.bn, pl.stages, pl.ksplit, nullptr, pl.slabs) > kSmemLimit)
     return fail(FML_EUNSUPPORTED, "gemm tile does not fit in shared memory");
   return FML_OK;
 }
@@ -762,24 +928,65 @@ static int launch_bn(const CUtensorMap& mp, const CUtensorMap& mq, const Params&
   return FML_OK;
 }
 
-template <int BN, bool PROMOTE>
-static int max_clusters(int ksplit, int smem) {
-  if (ksplit <= 1) return -1;
-  cudaLaunchConfig_t lc = {};
-  lc.gridDim = dim3(ksplit);
-  lc.blockDim = dim3(kThreads);
-  lc.dynamicSmemBytes = smem;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = ksplit;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  lc.attrs = attr;
-  lc.numAttrs = 1;
-  cudaFuncSetAttribute(gemm_kernel<BN, PROMOTE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-  int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, gemm_kernel<BN, PROMOTE>, &lc) != cudaSuccess) return -1;
-  return n;
+// Fill the kernel parameters shared by every entry point and launch.
+static int launch_plan(const Plan& pl, const CUtensorMap& mp, const CUtensorMap& mq, int dtype, int act,
+                       const void* bias, long long bias_stride, const void* residual, long long ldr, void* c,
+                       long long ldc, long long m, long long n, const uint8_t* p_packed, int sms,
+                       cudaStream_t st) {
+  Params prm = {};
+  prm.I = (int)pl.P.rows;
+  prm.J = (int)pl.Q.rows;
+  const long long es = (long long)dtype_size(dtype);
+  prm.num_kb = (int)((pl.keff * es + kSlab - 1) / kSlab);
+  prm.slabs = pl.slabs;
+  prm.tiles_i = (int)((prm.I + kBM - 1) / kBM);
+  prm.tiles_j = (int)((prm.J + pl.bn - 1) / pl.bn);
+  prm.num_tiles = prm.tiles_i * prm.tiles_j;
+  prm.group_i = std::min(prm.tiles_i, 16);
+  prm.ksplit = pl.ksplit;
+  prm.fmt = dtype == FML_F32 ? 2 : dtype == FML_BF16 ? 1 : 0;
+  prm.p_mn = (pl.P.pack || pl.packed) ? 0 : (pl.P.mn ? 1 : 0);
+  prm.q_mn = pl.Q.pack ? 0 : (pl.Q.mn ? 1 : 0);
+  prm.swap = pl.swap ? 1 : 0;
+  prm.out_dtype = dtype;
+  prm.act = act;
+  prm.stages = pl.stages;
+  prm.esize = (int)es;
+  prm.out = c;
+  prm.ldo = ldc;
+  prm.bias = bias;
+  prm.bias_stride = bias_stride;
+  prm.residual = residual;
+  prm.ldr = ldr;
+  prm.rows_out = (int)m;
+  prm.cols_out = (int)n;
+  prm.p_packed = p_packed;
+  int red_stride = 0;
+  const int smem = smem_bytes_for(pl.bn, pl.stages, pl.ksplit, &red_stride, pl.slabs);
+  prm.red_stride = red_stride;
+  prm.promote_kb = kPromoteKb;
+  // Persistent grid: as many CTAs (whole clusters) as are co-resident.
+  const long long want = (long long)prm.num_tiles * prm.ksplit;
+  int res = resident_ctas(pl.bn, pl.promote, pl.ksplit, smem, sms);
+  if (res <= 0) res = std::max(sms / prm.ksplit, 1) * prm.ksplit;
+  int grid = (int)std::min<long long>(want, res);
+  grid = std::max(grid / prm.ksplit, 1) * prm.ksplit;
+  if (pl.promote) {
+    switch (pl.bn) {
+      case 16: return launch_bn<16, true>(mp, mq, prm, grid, smem, st);
+      case 32: return launch_bn<32, true>(mp, mq, prm, grid, smem, st);
+      case 64: return launch_bn<64, true>(mp, mq, prm, grid, smem, st);
+    }
+  } else {
+    switch (pl.bn) {
+      case 16: return launch_bn<16, false>(mp, mq, prm, grid, smem, st);
+      case 32: return launch_bn<32, false>(mp, mq, prm, grid, smem, st);
+      case 64: return launch_bn<64, false>(mp, mq, prm, grid, smem, st);
+      case 128: return launch_bn<128, false>(mp, mq, prm, grid, smem, st);
+      case 256: return launch_bn<256, false>(mp, mq, prm, grid, smem, st);
+    }
+  }
+  return fail(FML_EUNSUPPORTED, "gemm: no kernel for tile width");
 }
 
 static int pack_operand(const Operand& o, int dtype, int mode, void* ws, cudaStream_t st) {
@@ -884,77 +1091,71 @@ extern "C" int fml_gemm(const void* a, int64_t lda_m, int64_t lda_k, const void*
     }
     if (rc) return rc;
   }
-  Params prm = {};
-  prm.I = (int)pl.P.rows;
-  prm.J = (int)pl.Q.rows;
-  const long long es = (long long)dtype_size(dtype);
-  prm.num_kb = (int)((pl.keff * es + kSlab - 1) / kSlab);
-  prm.tiles_i = (int)((prm.I + kBM - 1) / kBM);
-  prm.tiles_j = (int)((prm.J + pl.bn - 1) / pl.bn);
-  prm.num_tiles = prm.tiles_i * prm.tiles_j;
-  prm.group_i = std::min(prm.tiles_i, 16);
-  prm.ksplit = pl.ksplit;
-  prm.fmt = dtype == FML_F32 ? 2 : dtype == FML_BF16 ? 1 : 0;
-  prm.p_mn = pl.P.pack ? 0 : (pl.P.mn ? 1 : 0);
-  prm.q_mn = pl.Q.pack ? 0 : (pl.Q.mn ? 1 : 0);
-  prm.swap = pl.swap ? 1 : 0;
-  prm.out_dtype = dtype;
-  prm.act = act;
-  prm.stages = pl.stages;
-  prm.esize = (int)es;
-  prm.out = c;
-  prm.ldo = ldc;
-  prm.bias = bias;
-  prm.bias_stride = bias_stride;
-  prm.residual = residual;
-  prm.ldr = ldr;
-  prm.rows_out = (int)m;
-  prm.cols_out = (int)n;
-  int red_stride = 0;
-  const int smem = smem_bytes_for(pl.bn, pl.stages, pl.ksplit, &red_stride);
-  prm.red_stride = red_stride;
-  prm.promote_kb = kPromoteKb;
-  // Persistent grid: one CTA per SM (or as many clusters as fit).
-  long long want = (long long)prm.num_tiles * prm.ksplit;
-  int grid;
-  if (prm.ksplit > 1) {
-    int mc = -1;
-    if (pl.promote) {
-      switch (pl.bn) {
-        case 16: mc = max_clusters<16, true>(prm.ksplit, smem); break;
-        case 32: mc = max_clusters<32, true>(prm.ksplit, smem); break;
-        case 64: mc = max_clusters<64, true>(prm.ksplit, smem); break;
-        default: mc = -1;
-      }
-    } else {
-      switch (pl.bn) {
-        case 16: mc = max_clusters<16, false>(prm.ksplit, smem); break;
-        case 32: mc = max_clusters<32, false>(prm.ksplit, smem); break;
-        case 64: mc = max_clusters<64, false>(prm.ksplit, smem); break;
-        case 128: mc = max_clusters<128, false>(prm.ksplit, smem); break;
-        default: mc = -1;
-      }
-    }
-    if (mc <= 0) mc = sms / prm.ksplit;
-    grid = (int)std::min<long long>(want, (long long)mc * prm.ksplit);
-  } else {
-    grid = (int)std::min<long long>(want, sms);
-  }
-  grid = std::max(grid / prm.ksplit, 1) * prm.ksplit;
-  if (pl.promote) {
-    switch (pl.bn) {
-      case 16: return launch_bn<16, true>(mp, mq, prm, grid, smem, st);
-      case 32: return launch_bn<32, true>(mp, mq, prm, grid, smem, st);
-      case 64: return launch_bn<64, true>(mp, mq, prm, grid, smem, st);
-    }
-  } else {
-    switch (pl.bn) {
-      case 16: return launch_bn<16, false>(mp, mq, prm, grid, smem, st);
-      case 32: return launch_bn<32, false>(mp, mq, prm, grid, smem, st);
-      case 64: return launch_bn<64, false>(mp, mq, prm, grid, smem, st);
-      case 128: return launch_bn<128, false>(mp, mq, prm, grid, smem, st);
-      case 256: return launch_bn<256, false>(mp, mq, prm, grid, smem, st);
-    }
-  }
-  return fail(FML_EUNSUPPORTED, "gemm: no kernel for tile width");
+  return launch_plan(pl, mp, mq, dtype, act, bias, bias_stride, residual, ldr, c, ldc, m, n, nullptr, sms, st);
+}
+
+static long long packed_kb(long long k, int dtype) { return (k * (long long)dtype_size(dtype) + kSlab - 1) / kSlab; }
+
+extern "C" size_t fml_packed_weight_bytes(int64_t n, int64_t k, int dtype) {
+  if (dtype != FML_BF16 && dtype != FML_F16) return 0;
+  if (n <= 0 || k <= 0) return 0;
+  return (size_t)((n + kBM - 1) / kBM) * (size_t)packed_kb(k, dtype) * (size_t)(kBM * kSlab);
+}
+
+extern "C" int fml_pack_weight(const void* w, int64_t ldw, int64_t n, int64_t k, int dtype, void* packed,
+                               void* stream) {
+  if (dtype != FML_BF16 && dtype != FML_F16)
+    return fail(FML_EUNSUPPORTED, "pack_weight: 16-bit weights only (fp32 runs the 3xTF32 path)");
+  if (!w || !packed) return fail(FML_EINVAL, "pack_weight: null pointer");
+  if (n <= 0 || k <= 0 || ldw < k) return fail(FML_EINVAL, "pack_weight: bad shape");
+  if (reinterpret_cast<uintptr_t>(packed) % 1024 != 0)
+    return fail(FML_EINVAL, "pack_weight: packed buffer must be 1024-byte aligned");
+  const long long nkb = packed_kb(k, dtype);
+  const long long total = ((n + kBM - 1) / kBM) * nkb * (kBM * 8);
+  const unsigned grid = (unsigned)std::min<long long>((total + 255) / 256, 148LL * 64);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == FML_BF16)
+    pack_weight_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(w), ldw, (int)n,
+                                                            (int)k, (int)nkb, total, static_cast<uint8_t*>(packed));
+  else
+    pack_weight_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(w), ldw, (int)n, (int)k, (int)nkb,
+                                                     total, static_cast<uint8_t*>(packed));
+  count_launch();
+  return check_cuda(cudaGetLastError(), "pack_weight launch");
+}
+
+extern "C" int fml_linear_packed(const void* x, int64_t ldx, const void* packed, int64_t n, int64_t k,
+                                 const void* bias, int64_t bias_stride, const void* residual, int64_t ldr,
+                                 void* out, int64_t ldo, int64_t m, int dtype, int act,
+                                 const fml_tile_cfg* cfg, void* stream) {
+  if (dtype != FML_BF16 && dtype != FML_F16) return fail(FML_EUNSUPPORTED, "linear_packed: 16-bit only");
+  int rc = validate_gemm(x, packed, out, m, n, k, dtype);
+  if (rc) return rc;
+  if (act < 0 || act > 2) return fail(FML_EINVAL, "linear_packed: bad act");
+  if (ldo < n || (residual && ldr < n) || (m > 1 && ldx < k))
+    return fail(FML_EINVAL, "linear_packed: bad leading dimension");
+  if (reinterpret_cast<uintptr_t>(packed) % 1024 != 0)
+    return fail(FML_EINVAL, "linear_packed: packed weight must be 1024-byte aligned");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int sms = num_sms(current_device());
+  // MMA space: P = packed W (N rows), Q = x (M rows): always the swapped form.
+  Plan pl;
+  pl.packed = true;
+  pl.swap = true;
+  pl.promote = false;
+  pl.P = Operand{packed, 0, 1, n, k, false, false, 0, 0};
+  pl.Q = Operand{x, ldx, 1, m, k, false, false, 0, 0};
+  pl.bn = pick_bn(pl, n, m, cfg, sms);
+  classify(pl.Q, dtype, pl.bn, false);
+  if (pl.Q.pack) return fail(FML_EUNSUPPORTED, "linear_packed: x must be row-major with 16-byte aligned rows");
+  pl.keff = k;
+  pl.ws_bytes = 0;
+  pl.slabs = slabs_for(cfg, dtype, false, pl.bn);
+  const long long tiles = ((n + kBM - 1) / kBM) * ((m + pl.bn - 1) / pl.bn);
+  choose_split(pl, tiles, packed_kb(k, dtype), cfg, sms);
+  CUtensorMap mq;
+  rc = encode(&mq, x, dtype, false, false, m, k, pl.Q.s_r, pl.bn);
+  if (rc) return rc;
+  return launch_plan(pl, mq, mq, dtype, act, bias, bias_stride, residual, ldr, out, ldo, m, n,
+                     static_cast<const uint8_t*>(packed), sms, st);
 }

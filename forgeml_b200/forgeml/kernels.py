@@ -54,7 +54,7 @@ CANDIDATES = (
 
 _TILES_M = {16, 32, 64, 128}
 _TILES_N = {16, 32, 64, 128, 256}
-_TILES_K = {16, 32, 64, 128}
+_TILES_K = {16, 32, 64, 128, 256}
 _WARPS = {4, 6, 8}
 _STAGES = {2, 3, 4, 5, 6, 7, 8}
 _DTYPES = {torch.float16, torch.bfloat16, torch.float32}

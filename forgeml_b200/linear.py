@@ -1,0 +1,51 @@
+"""Constant-weight linear layer on the tcgen05 GEMM with a pre-packed weight.
+
+``PackedLinear(W)`` packs an nn.Linear-layout weight W [N, K] once
+(``fml_pack_weight``: 16 KB swizzled tiles, 128 rows x 128 bytes of K) and
+then computes ``y = x W^T`` with the fused epilogue of ``fml_gemm`` (bias,
+GELU, residual) through ``fml_linear_packed``: the weight streams from HBM as
+sequential bulk copies instead of strided row fragments.  16-bit weights
+only; fp32 layers use the 3xTF32 ``fml_gemm`` path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from forgeml_b200 import _native
+
+
+class PackedLinear:
+    def __init__(self, weight: torch.Tensor):
+        if weight.dim() != 2 or not weight.is_cuda or weight.dtype not in (torch.bfloat16, torch.float16):
+            raise ValueError("PackedLinear needs a 2-D 16-bit CUDA weight [N, K]")
+        if weight.stride(1) != 1:
+            raise ValueError("PackedLinear needs K-contiguous rows")
+        self.n, self.k = weight.shape
+        self.dtype = weight.dtype
+        self.code = _native.dtype_code(weight.dtype)
+        lib = _native.load()
+        nbytes = int(lib.fml_packed_weight_bytes(self.n, self.k, self.code))
+        self._buf = torch.empty(nbytes + 1024, dtype=torch.uint8, device=weight.device)
+        self.ptr = (self._buf.data_ptr() + 1023) // 1024 * 1024
+        _native.call("fml_pack_weight", weight.data_ptr(), weight.stride(0), self.n, self.k, self.code, self.ptr,
+                     _native.stream_ptr(weight.device))
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor, act: int = 0, residual: torch.Tensor | None = None,
+                 bias: torch.Tensor | None = None, rows: int | None = None, x_stride: int | None = None,
+                 tile: tuple[int, int, int] | None = None) -> torch.Tensor:
+        """``tile`` = (block_n, block_k, num_stages) hint; None chooses by heuristic."""
+        m = x.shape[0] if rows is None else rows
+        cfg = None
+        if tile is not None:
+            cfg = ctypes.byref(_native.fml_tile_cfg(128, tile[0], tile[1], 6, tile[2]))
+        _native.call(
+            "fml_linear_packed", x.data_ptr(), x.stride(0) if x_stride is None else x_stride, self.ptr, self.n,
+            self.k, bias.data_ptr() if bias is not None else None, bias.stride(0) if bias is not None else 0,
+            residual.data_ptr() if residual is not None else None,
+            residual.stride(0) if residual is not None else 0, out.data_ptr(), out.stride(0), m, self.code, act,
+            cfg, _native.stream_ptr(x.device),
+        )
+        return out

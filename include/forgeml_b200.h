@@ -44,7 +44,9 @@ enum { FML_ACT_NONE = 0, FML_ACT_GELU_ERF = 1, FML_ACT_GELU_TANH = 2 };
 
 /* Tile hints; mirrors forgeml.kernels.KernelConfig(block_m, block_n, block_k,
  * num_warps, num_stages) (src/forgeml/kernels.py:12-18).  block_n selects the
- * UMMA N tile (16..256), num_stages the shared-memory pipeline depth.  NULL
+ * UMMA N tile (16..256), num_stages the shared-memory pipeline depth, and
+ * block_k the K elements carried per pipeline stage (one, two or four 128-byte
+ * slabs; 16-bit inputs only).  NULL
  * means "choose by heuristic".  block_m, block_k and num_warps are fixed by the
  * tcgen05 design (128-row UMMA tiles, 128-byte K slabs, 6 warps) and are only
  * range-checked. */
@@ -85,6 +87,27 @@ FML_API int fml_gemm(const void* a, int64_t lda_m, int64_t lda_k,
              int64_t m, int64_t n, int64_t k,
              int dtype, int act, const fml_tile_cfg* cfg,
              void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Constant-weight linear layer, y = x W^T (+ bias) (-> GELU) (+ residual),
+ * with the same epilogue contract as fml_gemm.  Replaces Nebula's
+ * F.linear(h, W) for the per-layer weights (src/nebula/runtime.py:131-133,
+ * 145,152-153,186), whose W is fixed for the engine's lifetime.
+ * fml_pack_weight rewrites W [N, K] (row stride ldw, K contiguous, 16-bit)
+ * once into 16 KB tiles of 128 rows x 128 bytes of K, each already in the
+ * swizzled shared-memory layout the tensor cores read, so a decode-step GEMM
+ * streams the weight as sequential bulk copies.  The packed buffer
+ * (fml_packed_weight_bytes bytes) must be 1024-byte aligned.  x is row-major
+ * [M, K] with row stride ldx (16-byte aligned rows).
+ * ------------------------------------------------------------------------- */
+FML_API size_t fml_packed_weight_bytes(int64_t n, int64_t k, int dtype);
+FML_API int fml_pack_weight(const void* w, int64_t ldw, int64_t n, int64_t k, int dtype,
+                            void* packed, void* stream);
+FML_API int fml_linear_packed(const void* x, int64_t ldx, const void* packed, int64_t n,
+                              int64_t k, const void* bias, int64_t bias_stride,
+                              const void* residual, int64_t ldr, void* out, int64_t ldo,
+                              int64_t m, int dtype, int act, const fml_tile_cfg* cfg,
+                              void* stream);
 
 /* ---------------------------------------------------------------------------
  * LayerNorm over the trailing `cols` elements of each of `rows` rows.

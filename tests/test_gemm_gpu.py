@@ -144,3 +144,26 @@ def test_device_status_clean(cuda):
     a = torch.randn(256, 256, device=cuda, dtype=torch.bfloat16)
     kernels.matmul(a, a)
     assert _native.device_status() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m,n,k", [(32, 6144, 2048), (32, 2048, 8192), (1, 300, 70), (5, 32000, 2048),
+                                   (130, 1000, 1000), (512, 2048, 2048)])
+@pytest.mark.parametrize("epi", ["plain", "gelu_tanh", "residual", "bias"])
+def test_packed_linear(cuda, dtype, m, n, k, epi):
+    """Pre-packed constant-weight GEMM (Nebula decode path) vs the oracle contract."""
+    from forgeml_b200.linear import PackedLinear
+
+    g = torch.Generator().manual_seed(m + n + k)
+    x = (torch.randn(m, k, generator=g) * 0.5).to(dtype)
+    w = (torch.randn(n, k, generator=g) * 0.05).to(dtype)
+    r = torch.randn(m, n, generator=g).to(dtype) if epi == "residual" else None
+    bias = torch.randn(n, generator=g).to(dtype) if epi == "bias" else None
+    lin = PackedLinear(w.to(cuda))
+    out = torch.empty(m, n, dtype=dtype, device=cuda)
+    act = 2 if epi == "gelu_tanh" else 0
+    lin(x.to(cuda), out, act=act, residual=r.to(cuda) if r is not None else None,
+        bias=bias.to(cuda) if bias is not None else None)
+    want = matmul_epilogue(x, w.t(), bias, activation="gelu" if act else "none",
+                           approximate="tanh" if act else "none", residual=r)
+    close(out, want, dtype)
