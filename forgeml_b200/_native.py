@@ -27,6 +27,9 @@ STATUS_NAMES = {
     5: "device-side error",
 }
 
+# Capacity of the library-owned scratch used by fml_gemm_noalloc (bytes).
+GEMM_NOALLOC_SCRATCH_BYTES = 16 * 1024 * 1024
+
 _DTYPE_CODE = {torch.float32: FML_F32, torch.float16: FML_F16, torch.bfloat16: FML_BF16}
 
 _lock = threading.Lock()
@@ -66,6 +69,11 @@ _SIGNATURES = {
         _I,
         [_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I, _I,
          ctypes.POINTER(fml_tile_cfg), _P, ctypes.c_size_t, _P],
+    ),
+    "fml_gemm_noalloc": (
+        _I,
+        [_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I, _I,
+         ctypes.POINTER(fml_tile_cfg), _P],
     ),
     "fml_packed_weight_bytes": (ctypes.c_size_t, [_I64, _I64, _I]),
     "fml_pack_weight": (_I, [_P, _I64, _I64, _I64, _I, _P, _P]),

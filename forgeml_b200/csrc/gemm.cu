@@ -1159,3 +1159,49 @@ extern "C" int fml_linear_packed(const void* x, int64_t ldx, const void* packed,
   return launch_plan(pl, mq, mq, dtype, act, bias, bias_stride, residual, ldr, out, ldo, m, n,
                      static_cast<const uint8_t*>(packed), sms, st);
 }
+
+// ---------------------------------------------------------------------------
+// fml_gemm_noalloc: the GEMM for callers that cannot allocate device memory.
+// Its packing scratch is this file-scope device array instead of a caller
+// workspace.  In host code the symbol is only a stand-in: the device address
+// is looked up once per device with cudaGetSymbolAddress (that device
+// current) and passed to the kernels like any workspace pointer.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) uint8_t g_noalloc_scratch[FML_GEMM_NOALLOC_SCRATCH_BYTES];
+
+static int noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return fail(FML_EUNSUPPORTED, "gemm_noalloc: device index out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    const int rc = check_cuda(cudaGetSymbolAddress(&p, g_noalloc_scratch), "gemm_noalloc: cudaGetSymbolAddress");
+    if (rc != FML_OK) return rc;
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return FML_OK;
+}
+
+extern "C" int fml_gemm_noalloc(const void* a, int64_t lda_m, int64_t lda_k, const void* b, int64_t ldb_k,
+                                int64_t ldb_n, const void* bias, int64_t bias_stride, const void* residual,
+                                int64_t ldr, void* c, int64_t ldc, int64_t m, int64_t n, int64_t k, int dtype,
+                                int act, const fml_tile_cfg* cfg, void* stream) {
+  int rc = validate_gemm(a, b, c, m, n, k, dtype);
+  if (rc) return rc;
+  const size_t need = fml_gemm_workspace_size(m, n, k, dtype, lda_m, lda_k, ldb_k, ldb_n, a, b, cfg);
+  if (need > (size_t)FML_GEMM_NOALLOC_SCRATCH_BYTES)
+    return fail(FML_EWORKSPACE, "gemm_noalloc: this problem needs " + std::to_string(need) +
+                                    " bytes of packing scratch, more than the " +
+                                    std::to_string((size_t)FML_GEMM_NOALLOC_SCRATCH_BYTES) +
+                                    "-byte static scratch; use fml_gemm with a caller workspace");
+  void* scratch = nullptr;
+  if (need > 0) {
+    rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+  }
+  return fml_gemm(a, lda_m, lda_k, b, ldb_k, ldb_n, bias, bias_stride, residual, ldr, c, ldc, m, n, k, dtype, act,
+                  cfg, scratch, need > 0 ? (size_t)FML_GEMM_NOALLOC_SCRATCH_BYTES : 0, stream);
+}

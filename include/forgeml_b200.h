@@ -89,6 +89,36 @@ FML_API int fml_gemm(const void* a, int64_t lda_m, int64_t lda_k,
              void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Allocation-free GEMM.  This entry point has no counterpart in the
+ * reference; it exists for callers that cannot allocate device memory at the
+ * call site -- for example a host runtime that reserves the GPU's memory up
+ * front through its own allocator and forbids any further cudaMalloc, or a
+ * latency-critical caller that must not go through cudaMalloc/cudaFree,
+ * which can synchronise the device.  Same arguments and results as fml_gemm,
+ * minus the workspace: the operand packing that fml_gemm stages in a caller
+ * workspace (the fp32 3xTF32 split, 16-bit operands TMA cannot address) goes
+ * to a scratch array of FML_GEMM_NOALLOC_SCRATCH_BYTES that the library
+ * keeps in device memory (every GPU that loads the library holds it until
+ * the process exits).  Problems whose packing needs more than that return
+ * FML_EWORKSPACE without launching.  The first call on a device looks up the
+ * scratch address (cudaGetSymbolAddress) with that device current; make that
+ * first call before any stream capture.  All calls share the one array:
+ * calls whose executions overlap on the GPU (different streams, or other
+ * host threads) race on it, so serialise them.  Everything the kernels read
+ * from the scratch is written earlier in the same call, so the contents left
+ * by a previous call never matter.  Nothing is allocated: no cudaMalloc,
+ * cudaFree or allocating library routine is called.
+ * ------------------------------------------------------------------------- */
+#define FML_GEMM_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+FML_API int fml_gemm_noalloc(const void* a, int64_t lda_m, int64_t lda_k,
+                             const void* b, int64_t ldb_k, int64_t ldb_n,
+                             const void* bias, int64_t bias_stride,
+                             const void* residual, int64_t ldr,
+                             void* c, int64_t ldc,
+                             int64_t m, int64_t n, int64_t k,
+                             int dtype, int act, const fml_tile_cfg* cfg, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Constant-weight linear layer, y = x W^T (+ bias) (-> GELU) (+ residual),
  * with the same epilogue contract as fml_gemm.  Replaces Nebula's
  * F.linear(h, W) for the per-layer weights (src/nebula/runtime.py:131-133,
