@@ -4,8 +4,13 @@ from forgeml_b200.nebula.cache import CacheError, KVCache
 from forgeml_b200.nebula.model import DecoderConfig, TinyDecoder
 from forgeml_b200.nebula.parallel import ParallelContext
 from forgeml_b200.nebula.runtime import Engine, EngineFailed, ShardedDecoder
+from forgeml_b200.nebula.scheduler import AsyncBatcher, QueueFull, RequestRouter, ServiceClosed
 
 __all__ = [
+    "AsyncBatcher",
+    "QueueFull",
+    "RequestRouter",
+    "ServiceClosed",
     "CacheError",
     "DecoderConfig",
     "Engine",

@@ -1,0 +1,195 @@
+"""Nebula host logic on the CPU (reference tests/test_nebula_cache.py and
+tests/test_nebula_runtime.py semantics): KV-cache bookkeeping, model config
+and init, the engine protocol, validation and failure poisoning.  The engine
+runs with the CPU sharded decoder harness; the product decoder itself is
+CUDA-only and refuses a CPU context."""
+
+import pytest
+import torch
+
+from forgeml_b200.nebula import (CacheError, DecoderConfig, Engine, EngineFailed, KVCache, ParallelContext,
+                                 ShardedDecoder, TinyDecoder)
+from tests.cpu_engine import CpuShardedDecoder
+from tests.golden_io import load_nebula_small
+
+
+def cache(**kw):
+    args = dict(layer_ids=(0, 1), num_heads=2, head_dim=4, max_seq_len=8, max_requests=4,
+                device=torch.device("cpu"), dtype=torch.float32)
+    args.update(kw)
+    return KVCache(**args)
+
+
+def kv(b, t, v=1.0):
+    return torch.full((b, 2, t, 4), v)
+
+
+def test_cache_append_returns_prefix():
+    c = cache()
+    c.reserve((7, 9))
+    k0, _ = c.append(0, (7, 9), kv(2, 3, 1.0), kv(2, 3, 2.0), 0)
+    assert k0.shape == (2, 2, 3, 4)
+    c.append(1, (7, 9), kv(2, 3), kv(2, 3), 0)
+    k1, v1 = c.append(0, (7, 9), kv(2, 1, 5.0), kv(2, 1, 6.0), 3)
+    assert k1.shape == (2, 2, 4, 4)
+    assert (k1[:, :, :3] == 1.0).all() and (k1[:, :, 3] == 5.0).all() and (v1[:, :, 3] == 6.0).all()
+
+
+def test_cache_reserve_rejects_without_mutation():
+    c = cache(max_requests=2)
+    with pytest.raises(CacheError):
+        c.reserve((1, 1))
+    assert c.active_requests == 0
+    c.reserve((1, 2))
+    with pytest.raises(CacheError):
+        c.reserve((3, 4))
+    assert c.active_requests == 2
+    with pytest.raises(CacheError):
+        c.reserve((1,))
+
+
+def test_cache_append_validation():
+    c = cache()
+    c.reserve((5,))
+    for args in (((5, 5), kv(2, 1), kv(2, 1), 0), ((5,), kv(2, 1), kv(2, 1), 1), ((5,), kv(1, 9), kv(1, 9), 0),
+                 ((5,), kv(1, 1), kv(1, 2), 0), ((99,), kv(1, 1), kv(1, 1), 0)):
+        with pytest.raises(CacheError):
+            c.append(0, *args)
+    with pytest.raises(CacheError):
+        c.append(2, (5,), kv(1, 1), kv(1, 1), 0)
+    c.append(0, (5,), kv(1, 2), kv(1, 2), 0)
+    with pytest.raises(CacheError):
+        c.append(0, (5,), kv(1, 1), kv(1, 1), 0)
+    with pytest.raises(CacheError):
+        c.append(0, (5,), kv(1, 7), kv(1, 7), 2)
+    k, _ = c.append(1, (5,), kv(1, 2, 3.0), kv(1, 2), 0)
+    assert k.shape == (1, 2, 2, 4)
+
+
+def test_cache_release_reuse_and_slots():
+    c = cache(max_requests=2)
+    c.reserve((3,))
+    c.reserve((4,))
+    assert c.slots((3, 4)) == [0, 1]
+    c.release((3,))
+    c.release((3,))
+    assert c.active_requests == 1
+    c.reserve((8,))
+    assert c.slots((8,)) == [0]  # lowest free slot is reused
+    c.clear()
+    assert c.active_requests == 0
+    # a request's per-layer buffer is a view with the reference layout [heads, max_seq, hd]
+    c.reserve((1,))
+    assert c._entries[1][0][0].shape == (2, 8, 4)
+
+
+def test_cache_validate_positions():
+    c = cache()
+    c.reserve((1,))
+    c.validate((1,), 0, 2)
+    c.append(0, (1,), kv(1, 2), kv(1, 2), 0)
+    with pytest.raises(CacheError):
+        c.validate((1,), 2, 1)
+    c.append(1, (1,), kv(1, 2), kv(1, 2), 0)
+    c.validate((1,), 2, 1)
+
+
+def test_config_validation_and_reference_init():
+    with pytest.raises(ValueError):
+        DecoderConfig(hidden_size=10, num_heads=3)
+    with pytest.raises(ValueError):
+        DecoderConfig(vocab_size=0)
+    gold = load_nebula_small()
+    sd = TinyDecoder(DecoderConfig(**gold["config"])).state_dict()
+    assert all(torch.equal(sd[k], v) for k, v in gold["state_dict"].items())
+
+
+def cfg():
+    return DecoderConfig(**load_nebula_small()["config"])
+
+
+def engine(**kw):
+    return Engine(cfg(), context=ParallelContext.from_env(), max_requests=4, decoder_factory=CpuShardedDecoder, **kw)
+
+
+def test_product_decoder_refuses_cpu():
+    with pytest.raises(ValueError, match="CUDA"):
+        ShardedDecoder(cfg(), ParallelContext.from_env())
+
+
+def test_engine_protocol_matches_reference_outputs():
+    gold = load_nebula_small()
+    e = engine()
+    got = e.forward(gold["prefill_tokens"], gold["prefill_ids"], 0)
+    torch.testing.assert_close(got, gold["prefill_logits"], rtol=1e-5, atol=1e-6)
+    got_d = e.forward(gold["decode_tokens"], gold["prefill_ids"], 3)
+    torch.testing.assert_close(got_d, gold["decode_logits"], rtol=1e-5, atol=1e-6)
+    e.release(gold["prefill_ids"])
+    assert e.generate(gold["generate_prompts"], 3) == gold["generate_tokens"]
+    assert e.decoder.cache.active_requests == 0
+    assert e.generate([[1, 2]], 0) == [[]]
+    e.close()
+
+
+def test_invalid_requests_do_not_poison():
+    e = engine()
+    for toks, ids, pos in ((torch.tensor([[1, 2]]), (1,), 15), (torch.tensor([[1, 99]]), (1,), 0),
+                           (torch.tensor([[1]]), (1, 2), 0), (torch.tensor([[1]]), (1 << 62,), 0)):
+        with pytest.raises(ValueError):
+            e.forward(toks, ids, pos)
+    with pytest.raises(TypeError):
+        e.forward(torch.tensor([[1]]), (1,), 0.0)
+    assert e.healthy
+    assert e.forward(torch.tensor([[1, 2]]), (3,), 0).shape == (1, 2, 32)
+    e.close()
+
+
+@pytest.mark.parametrize("failure", [RuntimeError, KeyError, AssertionError])
+def test_failed_forward_poisons_engine(monkeypatch, failure):
+    e = engine()
+    e.forward(torch.tensor([[1, 2]]), (8,), 0)
+
+    def boom(*a, **k):
+        raise failure("simulated failure")
+
+    monkeypatch.setattr(e.decoder, "forward", boom)
+    with pytest.raises(EngineFailed):
+        e.forward(torch.tensor([[3]]), (8,), 2)
+    assert not e.healthy and e.decoder.cache.active_requests == 0
+    with pytest.raises(EngineFailed):
+        e.forward(torch.tensor([[1]]), (9,), 0)
+    e.close()
+
+
+def test_broadcast_failure_poisons_and_close_skips(monkeypatch):
+    e = engine()
+    calls = []
+
+    def boom(t):
+        calls.append(t)
+        raise RuntimeError("transport dead")
+
+    monkeypatch.setattr(e, "_world", lambda: True)
+    monkeypatch.setattr(e, "_bcast", boom)
+    with pytest.raises(EngineFailed):
+        e.forward(torch.tensor([[1]]), (1,), 0)
+    assert not e.healthy and e.decoder.cache.active_requests == 0
+    e.close()
+    assert len(calls) == 1
+    # the header that failed to go out is the reference's int64 STEP header
+    assert calls[0].dtype == torch.int64 and calls[0].tolist() == [1, 1, 1, 0]
+
+
+def test_closed_engine_and_release_checks():
+    e = engine()
+    with pytest.raises(ValueError):
+        e.release((1 << 63,))
+    assert e.healthy
+    e.forward(torch.tensor([[1, 2]]), (1,), 0)
+    e.release((1,))
+    assert e.decoder.cache.active_requests == 0
+    e.close()
+    with pytest.raises(EngineFailed):
+        e.forward(torch.tensor([[1]]), (1,), 0)
+    with pytest.raises(EngineFailed):
+        e.generate([[1]], 1)
