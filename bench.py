@@ -276,7 +276,7 @@ def run_native(args) -> None:
             sync_all()
         ms = ev0.elapsed_time(ev1)
         # native launches per step: a captured step replays the kernels counted at capture
-        graphed = world == 1 and dec.use_cuda_graphs
+        graphed = dec.use_cuda_graphs and ctx.pp_size == 1
         if graphed:
             n0 = _native.launch_count()
             dec._graphs.clear()
@@ -299,8 +299,10 @@ def run_native(args) -> None:
         torch.cuda.synchronize(dev)
 
     # ---- end-to-end through the public Engine API (host tokens in, ids out) ----
+    # Rank 0 drives the engine (it broadcasts the reference command protocol);
+    # the other ranks serve until the leader's STOP at engine.close().
     e2e = None
-    if world == 1:
+    if rank == 0:
         with torch.inference_mode():
             host_tok = torch.empty(BATCH, 1, dtype=torch.long).pin_memory()
             host_out = torch.empty(BATCH, dtype=torch.long).pin_memory()
@@ -324,7 +326,10 @@ def run_native(args) -> None:
             engine.release(ids)
         e2e = {"value": BATCH * K / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": BATCH * 8,
                "d2h_bytes_per_step": BATCH * 8,
-               "path": "Engine.forward(host int64 tokens) + native argmax + D2H ids, per step"}
+               "path": "Engine.forward(host int64 tokens) + native argmax + D2H ids, per step"
+                       + ("" if world == 1 else "; leader drives workers through the command protocol")}
+    else:
+        engine.serve()
 
     extra = {}
     if rank == 0:
@@ -342,14 +347,18 @@ def run_native(args) -> None:
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "nebula_c4_greedy_decode", "model": "12L d2048 h16x128 ffn8192 v32000",
                        "global_batch": BATCH, "prompt_len": PROMPT, "context": [PROMPT + W + 1, PROMPT + W + K],
-                       "parallelism": f"tp{world}", "cuda_graph": bool(world == 1 and dec.use_cuda_graphs),
+                       "parallelism": f"tp{world}", "cuda_graph": bool(dec.use_cuda_graphs and ctx.pp_size == 1),
                        "l2": "inputs larger than L2 (>3 GB streamed per step)"},
             "e2e": e2e, "gpu_launches": int(per_step_launches * K), "clocks": clk.summary(),
             "cpu_baseline": cpu, **extra,
         }
         print(json.dumps(line), flush=True)
-    engine.close()
+    if rank == 0:
+        engine.close()  # sends STOP to the serving workers
+    else:
+        engine.close()
     if world > 1:
+        torch.cuda.synchronize(dev)
         dist.barrier()
         ctx.close()
 

@@ -92,6 +92,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3)
   __shared__ float res_o[kMaxD];
   __shared__ float res_ml[2];
 
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int group = lane / G, gl = lane % G;
   const long long qidx = blockIdx.x / nsplit;
@@ -260,22 +262,10 @@ static int launch_neb(const void* q, const int64_t* qs, const void* kp, const vo
                       long long tq, long long H, long long D, long long max_seq, float scale,
                       int nsplit, cudaStream_t st) {
   const long long nq = B * tq * H;
-  cudaLaunchConfig_t lc = {};
-  lc.gridDim = dim3((unsigned)(nq * nsplit));
-  lc.blockDim = dim3(kAttnWarps * 32);
-  lc.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = nsplit;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  lc.attrs = attr;
-  lc.numAttrs = nsplit > 1 ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&lc, neb_attn_kernel<T, G, VEC>, static_cast<const T*>(q),
-                                     (long long)qs[0], (long long)qs[1], (long long)qs[2],
-                                     static_cast<const T*>(kp), static_cast<const T*>(vp), slot_of,
-                                     start_pos, static_cast<T*>(out), (int)tq, (int)H, (int)D,
-                                     (int)max_seq, scale, nsplit);
+  cudaError_t e = launch_pdl(neb_attn_kernel<T, G, VEC>, dim3((unsigned)(nq * nsplit)), dim3(kAttnWarps * 32), 0,
+                             st, nsplit, static_cast<const T*>(q), (long long)qs[0], (long long)qs[1],
+                             (long long)qs[2], static_cast<const T*>(kp), static_cast<const T*>(vp), slot_of,
+                             start_pos, static_cast<T*>(out), (int)tq, (int)H, (int)D, (int)max_seq, scale, nsplit);
   count_launch();
   return check_cuda(e, "neb_attention launch");
 }
@@ -322,6 +312,8 @@ struct SdpaParams {
 // s, s+TPQ, s+2*TPQ, ... (interleaved so the TPQ threads hit distinct banks).
 template <typename T, int TPQ>
 __global__ void __launch_bounds__(kSdpaThreads) sdpa_kernel(const SdpaParams p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int QB = kSdpaThreads / TPQ;  // queries per CTA
   extern __shared__ float sm[];
   const int D = p.D;
@@ -425,13 +417,13 @@ static int launch_sdpa(const SdpaParams& p, cudaStream_t st) {
   cudaError_t e;
   switch (t2) {
     case 1: e = cudaFuncSetAttribute(sdpa_kernel<T, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      sdpa_kernel<T, 1><<<grid, kSdpaThreads, smem, st>>>(p); break;
+      launch_pdl(sdpa_kernel<T, 1>, dim3(grid), dim3(kSdpaThreads), smem, st, 1, p); break;
     case 2: e = cudaFuncSetAttribute(sdpa_kernel<T, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      sdpa_kernel<T, 2><<<grid, kSdpaThreads, smem, st>>>(p); break;
+      launch_pdl(sdpa_kernel<T, 2>, dim3(grid), dim3(kSdpaThreads), smem, st, 1, p); break;
     case 4: e = cudaFuncSetAttribute(sdpa_kernel<T, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      sdpa_kernel<T, 4><<<grid, kSdpaThreads, smem, st>>>(p); break;
+      launch_pdl(sdpa_kernel<T, 4>, dim3(grid), dim3(kSdpaThreads), smem, st, 1, p); break;
     default: e = cudaFuncSetAttribute(sdpa_kernel<T, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      sdpa_kernel<T, 8><<<grid, kSdpaThreads, smem, st>>>(p); break;
+      launch_pdl(sdpa_kernel<T, 8>, dim3(grid), dim3(kSdpaThreads), smem, st, 1, p); break;
   }
   if (e != cudaSuccess) return check_cuda(e, "sdpa attribute");
   count_launch();

@@ -11,6 +11,7 @@
 
 #include <atomic>
 #include <string>
+#include <utility>
 
 #include "../../include/forgeml_b200.h"
 
@@ -45,6 +46,46 @@ extern __device__ int g_device_error;
 
 __device__ __forceinline__ void raise_device_error(int code) {
   atomicOr(&g_device_error, code);
+}
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  Every kernel of this library is launched
+// with programmatic stream serialization, so it may start while the previous
+// kernel in the stream is finishing.  Before touching anything an earlier
+// kernel may write (or read), a kernel executes pdl_wait(), which returns once
+// the preceding grid has completed and its memory is visible; it then calls
+// pdl_trigger() so the next kernel can begin launching.  Both are no-ops for a
+// kernel launched without the attribute.  Only constant data (weights) may be
+// read before pdl_wait().
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Host: launch with programmatic stream serialization (and an optional
+// cluster shape along x).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              int cluster_x, Args&&... args) {
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = grid;
+  lc.blockDim = block;
+  lc.dynamicSmemBytes = smem;
+  lc.stream = st;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[na].val.programmaticStreamSerializationAllowed = 1;
+  ++na;
+  if (cluster_x > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = cluster_x;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  lc.attrs = attr;
+  lc.numAttrs = na;
+  return cudaLaunchKernelEx(&lc, kernel, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------------------

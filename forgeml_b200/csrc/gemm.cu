@@ -287,21 +287,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;
       bool ok = true;
+      // Constant (pre-packed) weights do not depend on the previous kernel:
+      // start streaming the first tile's weight slabs into the free stages
+      // before waiting for the previous grid (programmatic dependent launch).
+      int pre = 0;
+      if (p.p_packed != nullptr && cluster_id < p.num_tiles) {
+        int ti0, tj0;
+        tile_coords(p, cluster_id, ti0, tj0);
+        for (int kb = kb_begin; kb < kb_end && pre < p.stages; kb += S, ++pre) {
+          const int nsl = min(S, kb_end - kb);
+          const uint32_t fb = bar_full(s, pre);
+          mbar_arrive_expect_tx(fb, (uint32_t)nsl * (kBM + BN) * kSlab);
+          const uint32_t sp0 = s.stage_base + pre * s.stage_bytes;
+          for (int sl = 0; sl < nsl; ++sl)
+            bulk_load(sp0 + sl * (kBM * kSlab),
+                      p.p_packed + ((size_t)ti0 * p.num_kb + kb + sl) * (size_t)(kBM * kSlab), kBM * kSlab, fb);
+        }
+      }
+      pdl_wait();
+      pdl_trigger();
+      int step = 0;
       for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
         int ti, tj;
         tile_coords(p, t, ti, tj);
-        for (int kb = kb_begin; kb < kb_end; kb += S) {
-          if (!mbar_wait(bar_empty(s, stage), phase ^ 1u, DEV_ERR_GEMM_TIMEOUT)) { ok = false; break; }
+        for (int kb = kb_begin; kb < kb_end; kb += S, ++step) {
+          const bool prefetched = step < pre;  // weights already in flight, barrier armed
+          if (!prefetched && !mbar_wait(bar_empty(s, stage), phase ^ 1u, DEV_ERR_GEMM_TIMEOUT)) { ok = false; break; }
           const int nsl = min(S, kb_end - kb);
           const uint32_t fb = bar_full(s, stage);
-          mbar_arrive_expect_tx(fb, (uint32_t)nsl * (kBM + BN) * kSlab);
+          if (!prefetched) mbar_arrive_expect_tx(fb, (uint32_t)nsl * (kBM + BN) * kSlab);
           const uint32_t sp0 = s.stage_base + stage * s.stage_bytes;
           const uint32_t sq0 = sp0 + s.p_bytes;
           for (int sl = 0; sl < nsl; ++sl) {
             const int kk = kb + sl;
             const uint32_t sp = sp0 + sl * (kBM * kSlab);
             const uint32_t sq = sq0 + sl * (BN * kSlab);
-            if (p.p_packed != nullptr) {
+            if (prefetched) {
+              // P slab issued before the dependency wait
+            } else if (p.p_packed != nullptr) {
               // One sequential 16 KB copy: the tile is stored pre-swizzled.
               bulk_load(sp, p.p_packed + ((size_t)ti * p.num_kb + kk) * (size_t)(kBM * kSlab),
                         kBM * kSlab, fb);
@@ -333,6 +356,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ UMMA issuer
+    pdl_wait();
+    pdl_trigger();
     if (lane == 0) {
       const uint32_t idesc = umma_idesc(p.fmt, p.p_mn, p.q_mn, BN);
       const uint32_t p_lbo = p.p_mn ? slab_box_bytes : 16u;
@@ -391,6 +416,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
+    pdl_wait();  // bias / residual / output may belong to the previous grid
+    pdl_trigger();
     const int quad = warp & 3;              // TMEM lane quadrant of this warp
     const int row = quad * 32 + lane;       // MMA row within the tile
     const int ep_tid = threadIdx.x - 64;    // 0..127
@@ -547,6 +574,8 @@ __device__ __forceinline__ float tf32_round(float x) {
 template <typename T>
 __global__ void pack_kernel(const T* __restrict__ x, long long s_r, long long s_k, int R, int K,
                             int Kp, int mode, T* __restrict__ dst) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float tile[32][33];
   const int r0 = blockIdx.y * 32, k0 = blockIdx.x * 32;
   const bool r_contig = (s_r == 1 && s_k != 1);
@@ -587,6 +616,8 @@ __global__ void pack_kernel(const T* __restrict__ x, long long s_r, long long s_
 template <typename T>
 __global__ void pack_weight_kernel(const T* __restrict__ w, long long ldw, int n, int k, int num_kb,
                                    long long total_chunks, uint8_t* __restrict__ dst) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int E = 16 / sizeof(T);  // elements per 16-byte chunk
   for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total_chunks;
        idx += (long long)gridDim.x * blockDim.x) {
@@ -911,14 +942,17 @@ static int launch_bn(const CUtensorMap& mp, const CUtensorMap& mq, const Params&
   lc.blockDim = dim3(kThreads);
   lc.dynamicSmemBytes = smem;
   lc.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   int na = 0;
+  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[na].val.programmaticStreamSerializationAllowed = 1;
+  ++na;
   if (prm.ksplit > 1) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = prm.ksplit;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    na = 1;
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = prm.ksplit;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
   }
   lc.attrs = attr;
   lc.numAttrs = na;
@@ -996,15 +1030,15 @@ static int pack_operand(const Operand& o, int dtype, int mode, void* ws, cudaStr
   if (grd.y > 65535) return fail(FML_EUNSUPPORTED, "pack: too many rows");
   void* dst = static_cast<uint8_t*>(ws) + o.ws_off;
   if (dtype == FML_F32)
-    pack_kernel<float><<<grd, blk, 0, st>>>(static_cast<const float*>(o.ptr), o.s_r, o.s_k,
+    launch_pdl(pack_kernel<float>, dim3(grd), dim3(blk), 0, st, 1, static_cast<const float*>(o.ptr), o.s_r, o.s_k,
                                             (int)o.rows, (int)o.k, (int)o.kp, mode,
                                             static_cast<float*>(dst));
   else if (dtype == FML_BF16)
-    pack_kernel<__nv_bfloat16><<<grd, blk, 0, st>>>(
+    launch_pdl(pack_kernel<__nv_bfloat16>, dim3(grd), dim3(blk), 0, st, 1, 
         static_cast<const __nv_bfloat16*>(o.ptr), o.s_r, o.s_k, (int)o.rows, (int)o.k,
         (int)o.kp, 0, static_cast<__nv_bfloat16*>(dst));
   else
-    pack_kernel<__half><<<grd, blk, 0, st>>>(static_cast<const __half*>(o.ptr), o.s_r, o.s_k,
+    launch_pdl(pack_kernel<__half>, dim3(grd), dim3(blk), 0, st, 1, static_cast<const __half*>(o.ptr), o.s_r, o.s_k,
                                              (int)o.rows, (int)o.k, (int)o.kp, 0,
                                              static_cast<__half*>(dst));
   count_launch();
@@ -1115,10 +1149,10 @@ extern "C" int fml_pack_weight(const void* w, int64_t ldw, int64_t n, int64_t k,
   const unsigned grid = (unsigned)std::min<long long>((total + 255) / 256, 148LL * 64);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == FML_BF16)
-    pack_weight_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(w), ldw, (int)n,
+    launch_pdl(pack_weight_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, st, 1, static_cast<const __nv_bfloat16*>(w), ldw, (int)n,
                                                             (int)k, (int)nkb, total, static_cast<uint8_t*>(packed));
   else
-    pack_weight_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(w), ldw, (int)n, (int)k, (int)nkb,
+    launch_pdl(pack_weight_kernel<__half>, dim3(grid), dim3(256), 0, st, 1, static_cast<const __half*>(w), ldw, (int)n, (int)k, (int)nkb,
                                                      total, static_cast<uint8_t*>(packed));
   count_launch();
   return check_cuda(cudaGetLastError(), "pack_weight launch");

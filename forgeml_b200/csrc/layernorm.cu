@@ -52,6 +52,8 @@ __global__ void __launch_bounds__(kWarps * 32)
     ln_vec_kernel(const T* __restrict__ x, long long xs, const T* __restrict__ g,
                   const T* __restrict__ b, float eps, T* __restrict__ y, long long ys, long long rows,
                   int cols) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int W = Vec<T>::N;
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * kWarps + threadIdx.x / 32;
@@ -113,6 +115,8 @@ __global__ void __launch_bounds__(kWarps * 32)
     ln_generic_kernel(const T* __restrict__ x, long long xs, const T* __restrict__ g,
                       const T* __restrict__ b, float eps, T* __restrict__ y, long long ys,
                       long long rows, int cols) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * kWarps + threadIdx.x / 32;
   if (row >= rows) return;
@@ -151,15 +155,15 @@ static int launch(const void* x, long long xs, const void* g, const void* b, flo
   const T* bp = static_cast<const T*>(b);
   T* yp = static_cast<T*>(y);
   if (aligned && vpl <= 2)
-    ln_vec_kernel<T, 2><<<grid, kWarps * 32, 0, st>>>(xp, xs, gp, bp, eps, yp, ys, rows, (int)cols);
+    launch_pdl(ln_vec_kernel<T, 2>, dim3(grid), dim3(kWarps * 32), 0, st, 1, xp, xs, gp, bp, eps, yp, ys, rows, (int)cols);
   else if (aligned && vpl <= 4)
-    ln_vec_kernel<T, 4><<<grid, kWarps * 32, 0, st>>>(xp, xs, gp, bp, eps, yp, ys, rows, (int)cols);
+    launch_pdl(ln_vec_kernel<T, 4>, dim3(grid), dim3(kWarps * 32), 0, st, 1, xp, xs, gp, bp, eps, yp, ys, rows, (int)cols);
   else if (aligned && vpl <= 8)
-    ln_vec_kernel<T, 8><<<grid, kWarps * 32, 0, st>>>(xp, xs, gp, bp, eps, yp, ys, rows, (int)cols);
+    launch_pdl(ln_vec_kernel<T, 8>, dim3(grid), dim3(kWarps * 32), 0, st, 1, xp, xs, gp, bp, eps, yp, ys, rows, (int)cols);
   else if (aligned && vpl <= 16)
-    ln_vec_kernel<T, 16><<<grid, kWarps * 32, 0, st>>>(xp, xs, gp, bp, eps, yp, ys, rows, (int)cols);
+    launch_pdl(ln_vec_kernel<T, 16>, dim3(grid), dim3(kWarps * 32), 0, st, 1, xp, xs, gp, bp, eps, yp, ys, rows, (int)cols);
   else
-    ln_generic_kernel<T><<<grid, kWarps * 32, 0, st>>>(xp, xs, gp, bp, eps, yp, ys, rows, (int)cols);
+    launch_pdl(ln_generic_kernel<T>, dim3(grid), dim3(kWarps * 32), 0, st, 1, xp, xs, gp, bp, eps, yp, ys, rows, (int)cols);
   count_launch();
   return check_cuda(cudaGetLastError(), "layernorm launch");
 }

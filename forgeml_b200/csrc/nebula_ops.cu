@@ -19,6 +19,8 @@ __global__ void kv_append_kernel(const T* __restrict__ k, long long ks0, long lo
                                  const int32_t* __restrict__ slot_of,
                                  const int32_t* __restrict__ start_pos, int tq, int H, int D,
                                  int max_seq, long long total) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int W = VEC ? (int)(16 / sizeof(T)) : 1;
   const int per_row = D / W;
   for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
@@ -53,6 +55,8 @@ template <typename T>
 __global__ void embed_kernel(const int64_t* __restrict__ tokens, const int32_t* __restrict__ start_pos,
                              const T* __restrict__ te, const T* __restrict__ pe, T* __restrict__ x,
                              int tq, int hidden, long long vocab, int max_seq) {
+  pdl_wait();
+  pdl_trigger();
   const long long row = blockIdx.x;  // b * tq + t
   const int b = (int)(row / tq), t = (int)(row % tq);
   const long long tok = tokens[row];
@@ -101,6 +105,8 @@ __device__ __forceinline__ bool better(float v, long long i, float bv, long long
 template <typename T>
 __global__ void __launch_bounds__(1024)
     argmax_kernel(const T* __restrict__ logits, long long rs, long long cols, int64_t* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const T* row = logits + (long long)blockIdx.x * rs;
   float bv = -INFINITY;
   long long bi = cols;  // sentinel (worse than any real index once a value is seen)
@@ -135,6 +141,8 @@ __global__ void __launch_bounds__(1024)
 
 template <typename T>
 __global__ void add_kernel(const T* __restrict__ a, const T* __restrict__ b, T* __restrict__ y, long long n) {
+  pdl_wait();
+  pdl_trigger();
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x)
     y[i] = from_f32<T>(to_f32<T>(a[i]) + to_f32<T>(b[i]));
@@ -173,7 +181,7 @@ extern "C" int neb_kv_append(const void* k, const int64_t k_strides[4], const vo
   const long long total = batch * t * heads * (vec ? head_dim / W : head_dim);
   const unsigned grid = neb::grid_for(total, 256);
 #define KV_LAUNCH(TT, VV)                                                                         \
-  neb::kv_append_kernel<TT, VV><<<grid, 256, 0, st>>>(                                           \
+  launch_pdl(neb::kv_append_kernel<TT, VV>, dim3(grid), dim3(256), 0, st, 1,                                            \
       static_cast<const TT*>(k), k_strides[0], k_strides[1], k_strides[2],                        \
       static_cast<const TT*>(v), v_strides[0], v_strides[1], v_strides[2],                        \
       static_cast<TT*>(k_pool), static_cast<TT*>(v_pool), slot_of, start_pos, (int)t, (int)heads, \
@@ -200,14 +208,14 @@ extern "C" int neb_embed(const int64_t* tokens, const int32_t* start_pos, const 
                   reinterpret_cast<uintptr_t>(pos_emb) % 16 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0;
   if (!al) return fail(FML_EUNSUPPORTED, "neb_embed: tables and output must be 16-byte aligned");
   if (dtype == FML_F32)
-    neb::embed_kernel<float><<<grid, 256, 0, st>>>(tokens, start_pos, static_cast<const float*>(tok_emb),
+    launch_pdl(neb::embed_kernel<float>, dim3(grid), dim3(256), 0, st, 1, tokens, start_pos, static_cast<const float*>(tok_emb),
         static_cast<const float*>(pos_emb), static_cast<float*>(x), (int)t, (int)hidden, vocab, (int)max_seq);
   else if (dtype == FML_BF16)
-    neb::embed_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(tokens, start_pos,
+    launch_pdl(neb::embed_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, st, 1, tokens, start_pos,
         static_cast<const __nv_bfloat16*>(tok_emb), static_cast<const __nv_bfloat16*>(pos_emb),
         static_cast<__nv_bfloat16*>(x), (int)t, (int)hidden, vocab, (int)max_seq);
   else
-    neb::embed_kernel<__half><<<grid, 256, 0, st>>>(tokens, start_pos, static_cast<const __half*>(tok_emb),
+    launch_pdl(neb::embed_kernel<__half>, dim3(grid), dim3(256), 0, st, 1, tokens, start_pos, static_cast<const __half*>(tok_emb),
         static_cast<const __half*>(pos_emb), static_cast<__half*>(x), (int)t, (int)hidden, vocab, (int)max_seq);
   count_launch();
   return check_cuda(cudaGetLastError(), "neb_embed launch");
@@ -221,12 +229,12 @@ extern "C" int neb_argmax(const void* logits, int64_t row_stride, int64_t rows, 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int threads = cols >= 1024 ? 1024 : 256;
   if (dtype == FML_F32)
-    neb::argmax_kernel<float><<<(unsigned)rows, threads, 0, st>>>(static_cast<const float*>(logits), row_stride, cols, out);
+    launch_pdl(neb::argmax_kernel<float>, dim3((unsigned)rows), dim3(threads), 0, st, 1, static_cast<const float*>(logits), row_stride, cols, out);
   else if (dtype == FML_BF16)
-    neb::argmax_kernel<__nv_bfloat16><<<(unsigned)rows, threads, 0, st>>>(
+    launch_pdl(neb::argmax_kernel<__nv_bfloat16>, dim3((unsigned)rows), dim3(threads), 0, st, 1, 
         static_cast<const __nv_bfloat16*>(logits), row_stride, cols, out);
   else
-    neb::argmax_kernel<__half><<<(unsigned)rows, threads, 0, st>>>(static_cast<const __half*>(logits), row_stride, cols, out);
+    launch_pdl(neb::argmax_kernel<__half>, dim3((unsigned)rows), dim3(threads), 0, st, 1, static_cast<const __half*>(logits), row_stride, cols, out);
   count_launch();
   return check_cuda(cudaGetLastError(), "neb_argmax launch");
 }
@@ -237,12 +245,12 @@ extern "C" int neb_add(const void* a, const void* b, void* y, int64_t n, int dty
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const unsigned grid = neb::grid_for(n, 256);
   if (dtype == FML_F32)
-    neb::add_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(a), static_cast<const float*>(b), static_cast<float*>(y), n);
+    launch_pdl(neb::add_kernel<float>, dim3(grid), dim3(256), 0, st, 1, static_cast<const float*>(a), static_cast<const float*>(b), static_cast<float*>(y), n);
   else if (dtype == FML_BF16)
-    neb::add_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(a),
+    launch_pdl(neb::add_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, st, 1, static_cast<const __nv_bfloat16*>(a),
         static_cast<const __nv_bfloat16*>(b), static_cast<__nv_bfloat16*>(y), n);
   else
-    neb::add_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(a), static_cast<const __half*>(b), static_cast<__half*>(y), n);
+    launch_pdl(neb::add_kernel<__half>, dim3(grid), dim3(256), 0, st, 1, static_cast<const __half*>(a), static_cast<const __half*>(b), static_cast<__half*>(y), n);
   count_launch();
   return check_cuda(cudaGetLastError(), "neb_add launch");
 }

@@ -285,8 +285,12 @@ class ShardedDecoder(nn.Module):
         slots_host = torch.tensor(self.cache.slots(request_ids), dtype=torch.int32)
         if tokens.device != ctx.device:
             tokens = tokens.to(ctx.device)
-        graphable = (t == 1 and last_only and ctx.world_size == 1 and self.use_cuda_graphs
-                     and not torch.cuda.is_current_stream_capturing())
+        # Single-token steps replay a captured graph.  With tensor parallelism the
+        # graph also holds the NCCL all-reduces (every TP rank captures and
+        # replays the same step in lockstep); pipeline stages run eagerly.
+        graphable = (t == 1 and ctx.pp_size == 1 and self.use_cuda_graphs
+                     and not torch.cuda.is_current_stream_capturing()
+                     and (last_only or ctx.world_size > 1))
         if graphable:
             logits = self._replay(tokens, slots_host, start_pos, b)
         else:

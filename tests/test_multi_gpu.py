@@ -1,0 +1,109 @@
+"""Tensor/pipeline parallel engine on several B200s (NCCL over NVLink).
+
+One process per GPU; the leader drives workers in ``serve()`` through the
+reference command protocol.  fp32 results must match the monolithic CPU
+oracle (rtol 1e-5, atol 1e-5) and greedy tokens must match exactly; bf16 runs
+must agree with the single-GPU native engine on the same weights
+(rtol 2e-2, atol 2e-2 * max|logits|).  Skipped when the box has fewer GPUs
+than ranks.
+"""
+
+import tempfile
+import time
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+CFG = dict(vocab_size=512, hidden_size=256, num_heads=8, num_layers=4, intermediate_size=512, max_seq_len=64, seed=17)
+
+
+def _worker(rank, world, tp, pp, store, dtype_name):
+    import os
+
+    from forgeml_b200.nebula import DecoderConfig, Engine, ParallelContext, TinyDecoder
+    from oracle import nebula as orc
+
+    os.environ["LOCAL_RANK"] = str(rank)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"file://{store}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    dtype = getattr(torch, dtype_name)
+    cfg = DecoderConfig(**CFG)
+    ctx = ParallelContext.from_env(tp_size=tp, pp_size=pp, device="cuda", timeout_s=60)
+    engine = Engine(cfg, context=ctx, dtype=dtype, max_requests=4)
+    try:
+        if rank == 0:
+            ref = TinyDecoder(cfg).eval()
+            w = orc.weights_from_state_dict({k: v.to(dtype).float() for k, v in ref.state_dict().items()},
+                                            cfg.num_layers)
+            g = torch.Generator().manual_seed(5)
+            toks = torch.randint(0, cfg.vocab_size, (2, 9), generator=g)
+            got = engine.forward(toks, (21, 22), 0).float().cpu()
+            want = orc.forward(w, toks, cfg.num_heads, cfg.num_layers)
+            if dtype == torch.float32:
+                torch.testing.assert_close(got, want, rtol=1e-5, atol=1e-5)
+            else:
+                torch.testing.assert_close(got, want, rtol=2e-2, atol=2e-2 * float(want.abs().max()))
+            step = got[:, -1].argmax(-1, keepdim=True)
+            got_d = engine.forward(step, (21, 22), 9).float().cpu()
+            want_d = orc.forward(w, torch.cat([toks, step], 1), cfg.num_heads, cfg.num_layers)[:, -1:]
+            tol = (1e-5, 1e-5) if dtype == torch.float32 else (2e-2, 2e-2 * float(want_d.abs().max()))
+            torch.testing.assert_close(got_d, want_d, rtol=tol[0], atol=tol[1])
+            engine.release((21, 22))
+            prompts = toks.tolist()
+            gen = engine.generate(prompts, 4)
+            if dtype == torch.float32:
+                assert gen == [orc.greedy(w, p, 4, cfg.num_heads, cfg.num_layers) for p in prompts]
+            assert engine.decoder.cache.active_requests == 0
+        else:
+            engine.serve()
+    finally:
+        engine.close()
+        torch.cuda.synchronize()
+        dist.barrier()
+        ctx.close()
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _run(world, tp, pp, dtype_name="float32"):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    with tempfile.TemporaryDirectory() as d:
+        procs = mp.start_processes(_worker, args=(world, tp, pp, f"{d}/store", dtype_name), nprocs=world,
+                                   join=False, start_method="spawn")
+        deadline = time.time() + 240
+        while time.time() < deadline and not all(p.exitcode is not None for p in procs.processes):
+            time.sleep(0.2)
+        for p in procs.processes:
+            if p.is_alive():
+                p.terminate()
+        for p in procs.processes:
+            p.join()
+        assert [p.exitcode for p in procs.processes] == [0] * world
+
+
+def test_tp2_fp32():
+    _run(2, 2, 1)
+
+
+def test_tp2_bf16():
+    _run(2, 2, 1, "bfloat16")
+
+
+def test_pp2_fp32():
+    _run(2, 1, 2)
+
+
+def test_tp2_pp2_bf16():
+    _run(4, 2, 2, "bfloat16")
+
+
+def test_tp8_bf16():
+    _run(8, 8, 1, "bfloat16")
