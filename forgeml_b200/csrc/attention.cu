@@ -256,6 +256,255 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3)
   cluster_sync_all();  // keep every CTA's shared memory alive until rank 0 has read it
 }
 
+// ---------------------------------------------------------------------------
+// Bulk-copy pipelined variant (16-byte aligned rows).  The keys [lo, hi) of
+// one (request, head) are one contiguous run of the pool, so a producer warp
+// streams them into shared memory with cp.async.bulk, kBulkStages stages of
+// NK keys (a 16 KB K tile plus a 16 KB V tile each) in flight, completion
+// signalled as transaction bytes on a per-stage mbarrier.  The K and V copies
+// of a stage are issued by two different lanes, and successive stages by
+// different lane pairs: one thread's bulk copies complete one after another,
+// copies from different threads overlap.  Four consumer warps read the tiles
+// with conflict-free 16-byte shared loads (a G-lane group per row, 32/G rows
+// per warp-wide load) and run the same online softmax as above; each
+// releases a stage back to the producer with one arrive.  Nothing but the
+// valid keys is copied, so a ragged final stage needs no bounds on the
+// global side.
+// ---------------------------------------------------------------------------
+constexpr int kBulkConsumers = 4;
+constexpr int kBulkStages = 3;
+constexpr int kBulkTile = 16384;  // bytes of one K (or V) tile
+constexpr int kBulkSmem = kBulkStages * 2 * kBulkTile;
+
+template <typename T, int G>
+__global__ void __launch_bounds__(32 * (kBulkConsumers + 1))
+    neb_attn_bulk_kernel(const T* __restrict__ q, long long qs0, long long qs1, long long qs2,
+                         const T* __restrict__ kpool, const T* __restrict__ vpool,
+                         const int32_t* __restrict__ slot_of, const int32_t* __restrict__ start_pos,
+                         T* __restrict__ out, int tq, int H, int D, int max_seq, float scale, int nsplit) {
+  constexpr int VE = 16 / (int)sizeof(T);
+  constexpr int RB = 16 * G;                    // bytes of one K/V row (= D * sizeof(T))
+  constexpr int NK = kBulkTile / RB;            // keys per stage
+  constexpr int KPW = 32 / G;                   // rows per warp-wide 16-byte load
+  constexpr int KW = NK / kBulkConsumers;       // keys per consumer warp per stage
+  constexpr int R = KW / KPW;                   // warp-wide loads per stage (= 8)
+  static_assert(R * KPW * kBulkConsumers == NK, "stage split");
+  extern __shared__ __align__(1024) uint8_t tiles[];
+  __shared__ __align__(8) uint64_t full_bar[kBulkStages], empty_bar[kBulkStages];
+  __shared__ float sm_o[kBulkConsumers][kMaxD];
+  __shared__ float sm_ml[kBulkConsumers][2];
+  __shared__ float res_o[kMaxD];
+  __shared__ float res_ml[2];
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kBulkStages; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), kBulkConsumers);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+
+  const long long qidx = blockIdx.x / nsplit;
+  const int split = (int)(blockIdx.x % nsplit);
+  const int h = (int)(qidx % H);
+  const int t = (int)((qidx / H) % tq);
+  const int b = (int)(qidx / ((long long)H * tq));
+  const int slot = slot_of[b];
+  const int pos = start_pos[b] + t;
+  const bool bad = (slot < 0) || (pos < 0) || (pos >= max_seq);
+  const int len = bad ? 0 : pos + 1;
+  if (bad && split == 0 && threadIdx.x == 0) raise_device_error(DEV_ERR_ATTN_RANGE);
+  const int lo = (int)((long long)split * len / nsplit);
+  const int hi = (int)((long long)(split + 1) * len / nsplit);
+  const int nst = (hi - lo + NK - 1) / NK;
+  const long long head_off = ((long long)(bad ? 0 : slot) * H + h) * (long long)max_seq * D;
+  const uint32_t tiles_u32 = smem_u32(tiles);
+
+  float m = -INFINITY, l = 0.f;
+  float o[VE];
+#pragma unroll
+  for (int i = 0; i < VE; ++i) o[i] = 0.f;
+  const int group = lane / G, gl = lane % G;
+
+  if (warp == kBulkConsumers) {
+    // Producer warp: lane 0 waits for a free stage and arms its barrier; the
+    // stage's K tile is copied by lane 2r and its V tile by lane 2r+1
+    // (r = stage index mod 16).  Stage s is reused once all four consumer
+    // warps have arrived on empty_bar[s].
+    const uint8_t* src = reinterpret_cast<const uint8_t*>((lane & 1) ? vpool : kpool) +
+                         (head_off + (long long)lo * D) * (long long)sizeof(T);
+    int issued = 0;
+    for (int j = 0; j < nst; ++j) {
+      const int s = j % kBulkStages;
+      const uint32_t bytes = (uint32_t)min(NK, hi - lo - j * NK) * RB;
+      const uint32_t fb = smem_u32(&full_bar[s]);
+      bool got = true;
+      if (lane == 0) {
+        if (j >= kBulkStages)
+          got = mbar_wait(smem_u32(&empty_bar[s]), ((j / kBulkStages) - 1) & 1, DEV_ERR_ATTN_TIMEOUT);
+        if (got) mbar_arrive_expect_tx(fb, 2 * bytes);
+      }
+      if (!__shfl_sync(0xffffffffu, got ? 1 : 0, 0)) break;
+      if ((lane >> 1) == (j & 15))
+        bulk_load(tiles_u32 + s * 2 * kBulkTile + (lane & 1) * kBulkTile, src + (long long)j * kBulkTile, bytes, fb);
+      __syncwarp();
+      ++issued;
+    }
+    // Drain: every copy this CTA issued has landed before it may exit (a
+    // no-op unless a wait above gave up).
+    if (lane == 0)
+      for (int j = max(0, issued - kBulkStages); j < issued; ++j)
+        mbar_wait(smem_u32(&full_bar[j % kBulkStages]), (j / kBulkStages) & 1, DEV_ERR_ATTN_TIMEOUT);
+  } else {
+    // Query slice of this lane, pre-scaled.
+    float qv[VE];
+    {
+      const T* qp = q + b * qs0 + (long long)t * qs1 + (long long)h * qs2;
+      uint4 raw = *reinterpret_cast<const uint4*>(qp + gl * VE);
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int i = 0; i < VE; ++i) qv[i] = to_f32<T>(e[i]) * scale;
+    }
+    const uint32_t row0 = (uint32_t)(warp * KW + group) * RB + gl * 16;
+    for (int j = 0; j < nst; ++j) {
+      const int s = j % kBulkStages;
+      if (!mbar_wait(smem_u32(&full_bar[s]), (j / kBulkStages) & 1, DEV_ERR_ATTN_TIMEOUT)) break;
+      const int nk = min(NK, hi - lo - j * NK);
+      const uint8_t* kt = tiles + s * 2 * kBulkTile + row0;
+      const uint8_t* vt = kt + kBulkTile;
+      uint4 kr[R];
+#pragma unroll
+      for (int u = 0; u < R; ++u) kr[u] = *reinterpret_cast<const uint4*>(kt + u * KPW * RB);
+      float sc[R];
+      float bmax = -INFINITY;
+#pragma unroll
+      for (int u = 0; u < R; ++u) {
+        const T* e = reinterpret_cast<const T*>(&kr[u]);
+        float d = 0.f;
+#pragma unroll
+        for (int i = 0; i < VE; ++i) d = fmaf(qv[i], to_f32<T>(e[i]), d);
+#pragma unroll
+        for (int off = G / 2; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+        const bool valid = warp * KW + u * KPW + group < nk;
+        sc[u] = valid ? d : -INFINITY;
+        bmax = fmaxf(bmax, sc[u]);
+      }
+      uint4 vr[R];
+#pragma unroll
+      for (int u = 0; u < R; ++u) {
+        const bool valid = warp * KW + u * KPW + group < nk;
+        vr[u] = valid ? *reinterpret_cast<const uint4*>(vt + u * KPW * RB) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, off));
+      const float m_new = fmaxf(m, bmax);
+      // A warp whose keys of this stage are all past the end keeps m at -inf.
+      const float alpha = (m_new == -INFINITY) ? 1.f : expf(m - m_new);
+      l *= alpha;
+#pragma unroll
+      for (int i = 0; i < VE; ++i) o[i] *= alpha;
+#pragma unroll
+      for (int u = 0; u < R; ++u) {
+        const float pr = (sc[u] == -INFINITY) ? 0.f : expf(sc[u] - m_new);
+        l += pr;
+        const T* e = reinterpret_cast<const T*>(&vr[u]);
+#pragma unroll
+        for (int i = 0; i < VE; ++i) o[i] = fmaf(pr, to_f32<T>(e[i]), o[i]);
+      }
+      m = m_new;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
+    }
+    // Sum the row groups of this warp (each group holds distinct keys).
+#pragma unroll
+    for (int off = 16; off >= G; off >>= 1) {
+      l += __shfl_xor_sync(0xffffffffu, l, off);
+#pragma unroll
+      for (int i = 0; i < VE; ++i) o[i] += __shfl_xor_sync(0xffffffffu, o[i], off);
+    }
+    if (group == 0) {
+#pragma unroll
+      for (int i = 0; i < VE; ++i) sm_o[warp][gl * VE + i] = o[i];
+      if (gl == 0) { sm_ml[warp][0] = m; sm_ml[warp][1] = l; }
+    }
+  }
+  __syncthreads();
+  // Combine the consumer warps of this CTA.
+  float mc = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kBulkConsumers; ++w) mc = fmaxf(mc, sm_ml[w][0]);
+  float lc = 0.f;
+  float wgt[kBulkConsumers];
+#pragma unroll
+  for (int w = 0; w < kBulkConsumers; ++w) {
+    wgt[w] = (sm_ml[w][0] == -INFINITY) ? 0.f : expf(sm_ml[w][0] - mc);
+    lc += wgt[w] * sm_ml[w][1];
+  }
+  T* op = out + ((long long)b * tq + t) * (long long)H * D + (long long)h * D;
+  if (nsplit == 1) {
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+      float acc = 0.f;
+#pragma unroll
+      for (int w = 0; w < kBulkConsumers; ++w) acc += wgt[w] * sm_o[w][d];
+      op[d] = from_f32<T>(bad ? 0.f : acc / lc);
+    }
+    return;
+  }
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kBulkConsumers; ++w) acc += wgt[w] * sm_o[w][d];
+    res_o[d] = acc;
+  }
+  if (threadIdx.x == 0) { res_ml[0] = mc; res_ml[1] = lc; }
+  cluster_sync_all();
+  if (split == 0) {
+    const uint32_t a_ml = smem_u32(res_ml), a_o = smem_u32(res_o);
+    float mm = -INFINITY;
+    for (int r = 0; r < nsplit; ++r) mm = fmaxf(mm, ld_cluster_f32(mapa(a_ml, r)));
+    float ww[8];
+    float lt = 0.f;
+    for (int r = 0; r < nsplit; ++r) {
+      const float mr = ld_cluster_f32(mapa(a_ml, r));
+      ww[r] = (mr == -INFINITY) ? 0.f : expf(mr - mm);
+      lt += ww[r] * ld_cluster_f32(mapa(a_ml + 4, r));
+    }
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+      float acc = 0.f;
+      for (int r = 0; r < nsplit; ++r) acc += ww[r] * ld_cluster_f32(mapa(a_o + 4 * d, r));
+      op[d] = from_f32<T>(bad ? 0.f : acc / lt);
+    }
+  }
+  cluster_sync_all();
+}
+
+template <typename T, int G>
+static int launch_neb_bulk(const void* q, const int64_t* qs, const void* kp, const void* vp,
+                           const int32_t* slot_of, const int32_t* start_pos, void* out, long long B,
+                           long long tq, long long H, long long D, long long max_seq, float scale,
+                           int nsplit, cudaStream_t st) {
+  static bool attr_set[64] = {};
+  const int dev = current_device();
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(neb_attn_bulk_kernel<T, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kBulkSmem);
+    if (e != cudaSuccess) return check_cuda(e, "neb_attention smem attribute");
+    attr_set[dev] = true;
+  }
+  const long long nq = B * tq * H;
+  cudaError_t e = launch_pdl(neb_attn_bulk_kernel<T, G>, dim3((unsigned)(nq * nsplit)),
+                             dim3(32 * (kBulkConsumers + 1)), kBulkSmem, st, nsplit, static_cast<const T*>(q),
+                             (long long)qs[0], (long long)qs[1], (long long)qs[2], static_cast<const T*>(kp),
+                             static_cast<const T*>(vp), slot_of, start_pos, static_cast<T*>(out), (int)tq,
+                             (int)H, (int)D, (int)max_seq, scale, nsplit);
+  count_launch();
+  return check_cuda(e, "neb_attention launch");
+}
+
 template <typename T, int G, bool VEC>
 static int launch_neb(const void* q, const int64_t* qs, const void* kp, const void* vp,
                       const int32_t* slot_of, const int32_t* start_pos, void* out, long long B,
@@ -282,6 +531,11 @@ static int dispatch_neb(const void* q, const int64_t* qs, const void* kp, const 
                       (reinterpret_cast<uintptr_t>(vp) % 16 == 0);
   if (vec_ok) {
     const long long nv = D / VE;  // 16-byte slices per row
+    // Rows of exactly 16*G bytes stream through the bulk-copy pipeline.
+#define NEB_BULK(GG) \
+  if (nv == GG) return launch_neb_bulk<T, GG>(q, qs, kp, vp, so, sp, out, B, tq, H, D, ms, scale, nsplit, st);
+    NEB_BULK(1) NEB_BULK(2) NEB_BULK(4) NEB_BULK(8) NEB_BULK(16) NEB_BULK(32)
+#undef NEB_BULK
 #define NEB_CASE(GG) \
   if (nv <= GG) return launch_neb<T, GG, true>(q, qs, kp, vp, so, sp, out, B, tq, H, D, ms, scale, nsplit, st);
     NEB_CASE(1) NEB_CASE(2) NEB_CASE(4) NEB_CASE(8) NEB_CASE(16) NEB_CASE(32)
@@ -452,7 +706,9 @@ extern "C" int neb_attention(const void* q, const int64_t q_strides[4], const vo
   // long run of keys.  Depends only on the launch shape (not on the device-side
   // positions), so a captured decode step keeps a valid split.
   const long long nq = batch * t * heads;
-  const long long target = 8LL * num_sms(current_device());
+  const char* tune = getenv("FORGEML_NEB_ATTN_CTAS_PER_SM");  // tuning override
+  const long long target_per_sm = (tune && atoll(tune) > 0) ? atoll(tune) : 8LL;
+  const long long target = target_per_sm * num_sms(current_device());
   int nsplit = (int)std::min<long long>(8, std::max<long long>(1, (target + nq - 1) / nq));
   nsplit = (int)std::min<long long>(nsplit, std::max<long long>(1, max_seq / 64));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);

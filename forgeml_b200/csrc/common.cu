@@ -3,6 +3,8 @@
 #include <mutex>
 #include <string>
 
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace fml {
@@ -45,6 +47,11 @@ int num_sms(int device) {
     cache[device] = v;
   }
   return cache[device];
+}
+
+bool pdl_enabled() {
+  const char* e = getenv("FORGEML_PDL");
+  return !(e && e[0] == '0');
 }
 
 }  // namespace fml

@@ -41,6 +41,7 @@ enum : int {
   DEV_ERR_TOKEN_RANGE = 1 << 1,
   DEV_ERR_ATTN_RANGE = 1 << 2,
   DEV_ERR_REDUCE_TIMEOUT = 1 << 3,
+  DEV_ERR_ATTN_TIMEOUT = 1 << 4,
 };
 extern __device__ int g_device_error;
 
@@ -61,6 +62,10 @@ __device__ __forceinline__ void raise_device_error(int code) {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Programmatic dependent launch is on unless FORGEML_PDL=0 (a diagnostic
+// switch: every kernel stays correct either way).
+bool pdl_enabled();
+
 // Host: launch with programmatic stream serialization (and an optional
 // cluster shape along x).
 template <typename... KArgs, typename... Args>
@@ -74,7 +79,7 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   cudaLaunchAttribute attr[2];
   int na = 0;
   attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[na].val.programmaticStreamSerializationAllowed = 1;
+  attr[na].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   ++na;
   if (cluster_x > 1) {
     attr[na].id = cudaLaunchAttributeClusterDimension;

@@ -40,7 +40,11 @@ namespace gemm {
 
 constexpr int kBM = 128;        // UMMA M
 constexpr int kSlab = 128;      // bytes of K per smem row (one swizzle row)
-constexpr int kThreads = 192;   // 6 warps
+// Warp roles: 0-3 epilogue (TMEM lane quadrant = warp), 4 UMMA issuer,
+// 5-8 TMA producers.
+constexpr int kMmaWarp = 4;
+constexpr int kProducerWarp0 = 5;
+constexpr int kThreads = 288;   // 9 warps
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in per block
 constexpr int kMaxStages = 8;
 constexpr int kPromoteKb = 2;  // K slabs per promoted chunk (fp32 path)
@@ -88,11 +92,10 @@ __device__ __forceinline__ uint32_t bar_tfull(const Smem& s, int a) {
 __device__ __forceinline__ uint32_t bar_tempty(const Smem& s, int a) {
   return s.bars + 8 * (2 * kMaxStages + 2 + a);
 }
-__device__ __forceinline__ uint32_t bar_red_ready(const Smem& s) {
+// Split-K: completes once every other CTA of the cluster has pushed its
+// partial rows of this CTA's output slice (transaction bytes of st.async).
+__device__ __forceinline__ uint32_t bar_recv(const Smem& s) {
   return s.bars + 8 * (2 * kMaxStages + 4);
-}
-__device__ __forceinline__ uint32_t bar_red_done(const Smem& s) {
-  return s.bars + 8 * (2 * kMaxStages + 5);
 }
 __device__ __forceinline__ uint32_t bar_drain(const Smem& s) {
   return s.bars + 8 * (2 * kMaxStages + 6);
@@ -133,6 +136,16 @@ __device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t addr) {
                : "memory");
   return v;
 }
+// Asynchronous store of 16 bytes into another CTA's shared memory; the
+// bytes are reported as transactions on that CTA's mbarrier `mbar`.
+__device__ __forceinline__ void st_async_v4(uint32_t addr, float a, float b, float c, float d, uint32_t mbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
+               "f"(a), "f"(b), "f"(c), "f"(d), "r"(mbar)
+               : "memory");
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
                    : "memory");
@@ -144,6 +157,15 @@ __device__ __forceinline__ void fence_cluster() {
   asm volatile("fence.acq_rel.cluster;" ::: "memory");
 }
 
+// ---------------------------------------------------------------------------
+// Epilogue, per output element (m, n) with fp32 accumulator v: the reference
+// template's rounding contract (src/forgeml/_triton.py:43-57), round to the
+// output dtype, add bias and round, apply GELU, then (Nebula's residual
+// extension) round and add residual.  Callers loop over elements without
+// unrolling (one inlined copy of the GELU code): unrolled copies per element
+// overflow the instruction cache and stall every warp of the CTA.  The
+// vectorised row path below is the exception, 32 elements in pairs.
+// ---------------------------------------------------------------------------
 // Epilogue for one output element at MMA coordinates (i, j) with fp32 value v.
 __device__ __forceinline__ void epilogue_store(const Params& p, int i, int j, float v) {
   int m, n;
@@ -251,21 +273,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < p.stages; ++i) {
-      mbar_init(bar_full(s, i), 1);
+      mbar_init(bar_full(s, i), 2);  // one arrive from the P producer, one from the Q producer
       mbar_init(bar_empty(s, i), 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(bar_tfull(s, a), 1);
       mbar_init(bar_tempty(s, a), 4);
     }
-    mbar_init(bar_red_ready(s), ksplit);
-    mbar_init(bar_red_done(s), ksplit);
+    mbar_init(bar_recv(s), 1);
     mbar_init(bar_drain(s), 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmP);
     tma_prefetch_desc(&tmQ);
   }
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_holder, kTmemCols);
     tmem_relinquish();
   }
@@ -280,81 +301,93 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int mn_box = kSlab / p.esize;         // MN elements per MN-major box
   const uint32_t slab_box_bytes = (uint32_t)bke * kSlab;  // bytes of one MN-major box
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t issued_mask = 0, issued_parity = 0;
-      bool ok = true;
-      // Constant (pre-packed) weights do not depend on the previous kernel:
-      // start streaming the first tile's weight slabs into the free stages
-      // before waiting for the previous grid (programmatic dependent launch).
-      int pre = 0;
-      if (p.p_packed != nullptr && cluster_id < p.num_tiles) {
-        int ti0, tj0;
-        tile_coords(p, cluster_id, ti0, tj0);
-        for (int kb = kb_begin; kb < kb_end && pre < p.stages; kb += S, ++pre) {
-          const int nsl = min(S, kb_end - kb);
-          const uint32_t fb = bar_full(s, pre);
-          mbar_arrive_expect_tx(fb, (uint32_t)nsl * (kBM + BN) * kSlab);
-          const uint32_t sp0 = s.stage_base + pre * s.stage_bytes;
-          for (int sl = 0; sl < nsl; ++sl)
-            bulk_load(sp0 + sl * (kBM * kSlab),
-                      p.p_packed + ((size_t)ti0 * p.num_kb + kb + sl) * (size_t)(kBM * kSlab), kBM * kSlab, fb);
-        }
-      }
-      pdl_wait();
-      pdl_trigger();
-      int step = 0;
-      for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
-        int ti, tj;
-        tile_coords(p, t, ti, tj);
-        for (int kb = kb_begin; kb < kb_end; kb += S, ++step) {
-          const bool prefetched = step < pre;  // weights already in flight, barrier armed
-          if (!prefetched && !mbar_wait(bar_empty(s, stage), phase ^ 1u, DEV_ERR_GEMM_TIMEOUT)) { ok = false; break; }
-          const int nsl = min(S, kb_end - kb);
-          const uint32_t fb = bar_full(s, stage);
-          if (!prefetched) mbar_arrive_expect_tx(fb, (uint32_t)nsl * (kBM + BN) * kSlab);
-          const uint32_t sp0 = s.stage_base + stage * s.stage_bytes;
-          const uint32_t sq0 = sp0 + s.p_bytes;
-          for (int sl = 0; sl < nsl; ++sl) {
-            const int kk = kb + sl;
-            const uint32_t sp = sp0 + sl * (kBM * kSlab);
-            const uint32_t sq = sq0 + sl * (BN * kSlab);
-            if (prefetched) {
-              // P slab issued before the dependency wait
-            } else if (p.p_packed != nullptr) {
-              // One sequential 16 KB copy: the tile is stored pre-swizzled.
-              bulk_load(sp, p.p_packed + ((size_t)ti * p.num_kb + kk) * (size_t)(kBM * kSlab),
-                        kBM * kSlab, fb);
-            } else if (!p.p_mn) {
-              tma_load_2d(&tmP, fb, sp, kk * bke, ti * kBM);
-            } else {
-              for (int b = 0; b < kBM / mn_box; ++b)
-                tma_load_2d(&tmP, fb, sp + b * slab_box_bytes, ti * kBM + b * mn_box, kk * bke);
-            }
-            if (!p.q_mn) {
-              tma_load_2d(&tmQ, fb, sq, kk * bke, tj * BN);
-            } else {
-              for (int b = 0; b < BN / mn_box; ++b)
-                tma_load_2d(&tmQ, fb, sq + b * slab_box_bytes, tj * BN + b * mn_box, kk * bke);
-            }
-          }
-          issued_mask |= 1u << stage;
-          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-          if (++stage == p.stages) { stage = 0; phase ^= 1u; }
-        }
-      }
-      if (!ok) {
-        // Unwind: let every load we issued land before the CTA can exit.
-        for (int i = 0; i < p.stages; ++i)
-          if (issued_mask & (1u << i))
-            mbar_wait(bar_full(s, i), (issued_parity >> i) & 1u, DEV_ERR_GEMM_TIMEOUT);
+  if (warp >= kProducerWarp0) {
+    // ------------------------------------------------------------ producers
+    // Four warps: P or Q operand x even or odd pipeline steps.  A warp's
+    // bulk/TMA copies are processed one after another (about a memory
+    // latency each), while copies issued by different warps, or by several
+    // lanes of one instruction, are in flight together.  So every copy of
+    // a stage's operand (one per slab, or per box for MN-major operands)
+    // goes out in a single instruction across lanes, and consecutive steps
+    // alternate between two warps.  Lane 0 waits for the free stage and arms
+    // the full barrier with this operand's bytes.
+    const int pw = warp - kProducerWarp0;
+    const bool is_q = pw >= 2;
+    const int parity = pw & 1;
+    const CUtensorMap* tm = is_q ? &tmQ : &tmP;
+    const int mn = is_q ? p.q_mn : p.p_mn;
+    const int rows = is_q ? BN : kBM;
+    const uint32_t op_off = is_q ? s.p_bytes : 0u;
+    const uint32_t slab_bytes = (uint32_t)rows * kSlab;
+    const bool packed = !is_q && p.p_packed != nullptr;
+    const int nbox = mn ? rows / mn_box : 1;
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued_mask = 0, issued_parity = 0;
+    bool ok = true;
+    // Constant (pre-packed) weights do not depend on the previous kernel:
+    // start streaming the first tile's weight slabs into the free stages
+    // before waiting for the previous grid (programmatic dependent launch).
+    const int steps_first = cluster_id < p.num_tiles ? (kb_end - kb_begin + S - 1) / S : 0;
+    const int pre_limit = packed ? min(p.stages, steps_first) : 0;
+    if (pre_limit > 0 && lane == 0) {
+      int ti0, tj0;
+      tile_coords(p, cluster_id, ti0, tj0);
+      for (int st = parity; st < pre_limit; st += 2) {
+        const int kb = kb_begin + st * S;
+        const int nsl = min(S, kb_end - kb);
+        const uint32_t fb = bar_full(s, st);
+        mbar_arrive_expect_tx(fb, (uint32_t)nsl * slab_bytes);
+        bulk_load(s.stage_base + st * s.stage_bytes,
+                  p.p_packed + ((size_t)ti0 * p.num_kb + kb) * (size_t)(kBM * kSlab), (uint32_t)nsl * slab_bytes, fb);
+        issued_mask |= 1u << st;
       }
     }
     __syncwarp();
-  } else if (warp == 1) {
+    pdl_wait();
+    pdl_trigger();
+    int step = 0;
+    for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
+      int ti, tj;
+      tile_coords(p, t, ti, tj);
+      const int rbase = is_q ? tj * BN : ti * kBM;
+      for (int kb = kb_begin; kb < kb_end; kb += S, ++step) {
+        if ((step & 1) == parity && step >= pre_limit) {
+          const int nsl = min(S, kb_end - kb);
+          const uint32_t fb = bar_full(s, stage);
+          bool got = true;
+          if (lane == 0) {
+            got = mbar_wait(bar_empty(s, stage), phase ^ 1u, DEV_ERR_GEMM_TIMEOUT);
+            if (got) mbar_arrive_expect_tx(fb, (uint32_t)nsl * slab_bytes);
+          }
+          if (!__shfl_sync(0xffffffffu, got ? 1 : 0, 0)) { ok = false; break; }
+          const uint32_t dst0 = s.stage_base + stage * s.stage_bytes + op_off;
+          if (packed) {
+            // The tile's slabs are stored pre-swizzled and consecutive.
+            if (lane == 0)
+              bulk_load(dst0, p.p_packed + ((size_t)ti * p.num_kb + kb) * (size_t)(kBM * kSlab),
+                        (uint32_t)nsl * slab_bytes, fb);
+          } else if (lane < nsl * nbox) {
+            const int sl = lane / nbox, b = lane % nbox;
+            const uint32_t dst = dst0 + sl * slab_bytes + b * slab_box_bytes;
+            if (!mn) tma_load_2d(tm, fb, dst, (kb + sl) * bke, rbase);
+            else tma_load_2d(tm, fb, dst, rbase + b * mn_box, (kb + sl) * bke);
+          }
+          __syncwarp();
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        }
+        if (++stage == p.stages) { stage = 0; phase ^= 1u; }
+      }
+    }
+    if (!ok && lane == 0) {
+      // Unwind: let every load we issued land before the CTA can exit.
+      for (int i = 0; i < p.stages; ++i)
+        if (issued_mask & (1u << i))
+          mbar_wait(bar_full(s, i), (issued_parity >> i) & 1u, DEV_ERR_GEMM_TIMEOUT);
+    }
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ UMMA issuer
     pdl_wait();
     pdl_trigger();
@@ -362,10 +395,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc = umma_idesc(p.fmt, p.p_mn, p.q_mn, BN);
       const uint32_t p_lbo = p.p_mn ? slab_box_bytes : 16u;
       const uint32_t q_lbo = p.q_mn ? slab_box_bytes : 16u;
-      // Advance per UMMA K step (32 bytes of K): within the swizzle row for
-      // K-major, by (32/esize) rows of 128 B for MN-major.
-      const uint32_t p_kstep = p.p_mn ? (uint32_t)(32 / p.esize) * kSlab : 32u;
-      const uint32_t q_kstep = p.q_mn ? (uint32_t)(32 / p.esize) * kSlab : 32u;
+      // Descriptors of stage 0 / slab 0 / K step 0; everything else is a
+      // constant offset added to the start-address field (address >> 4).
+      // Per UMMA K step (32 bytes of K): within the swizzle row for K-major,
+      // (32/esize) rows of 128 B for MN-major.
+      const uint64_t dp0 = umma_desc_sw128(s.stage_base, p_lbo, 1024u);
+      const uint64_t dq0 = umma_desc_sw128(s.stage_base + s.p_bytes, q_lbo, 1024u);
+      const uint32_t d_stage = s.stage_bytes >> 4;
+      const uint32_t dp_slab = (kBM * kSlab) >> 4, dq_slab = (BN * kSlab) >> 4;
+      const uint32_t dp_k = (p.p_mn ? (uint32_t)(32 / p.esize) * kSlab : 32u) >> 4;
+      const uint32_t dq_k = (p.q_mn ? (uint32_t)(32 / p.esize) * kSlab : 32u) >> 4;
+      const bool tf32 = p.fmt == 2;
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -379,26 +419,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         int kb = kb_begin;
         while (kb < kb_end && ok) {
           const int kb_stop = PROMOTE ? min(kb + p.promote_kb, kb_end) : kb_end;
-          const int chunk_begin = kb;
           if (!mbar_wait(bar_tempty(s, acc), acc_phase ^ 1u, DEV_ERR_GEMM_TIMEOUT)) { ok = false; break; }
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + acc * kAccStride;
+          uint32_t accum = 0u;
           for (; kb < kb_stop; kb += S) {
             if (!mbar_wait(bar_full(s, stage), phase, DEV_ERR_GEMM_TIMEOUT)) { ok = false; break; }
             tc_fence_after();
             const int nsl = min(S, kb_end - kb);
-            const uint32_t sp0 = s.stage_base + stage * s.stage_bytes;
-            const uint32_t sq0 = sp0 + s.p_bytes;
+            const uint64_t dp = dp0 + stage * d_stage, dq = dq0 + stage * d_stage;
             for (int sl = 0; sl < nsl; ++sl) {
-              const uint32_t sp = sp0 + sl * (kBM * kSlab);
-              const uint32_t sq = sq0 + sl * (BN * kSlab);
+              const uint64_t ap = dp + sl * dp_slab, bq = dq + sl * dq_slab;
+              if (tf32) {
 #pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const uint64_t ad = umma_desc_sw128(sp + k * p_kstep, p_lbo, 1024u);
-                const uint64_t bd = umma_desc_sw128(sq + k * q_kstep, q_lbo, 1024u);
-                const uint32_t accum = (kb > chunk_begin || sl > 0 || k > 0) ? 1u : 0u;
-                if (p.fmt == 2) umma_tf32(d_tmem, ad, bd, idesc, accum);
-                else umma_f16(d_tmem, ad, bd, idesc, accum);
+                for (int k = 0; k < 4; ++k) { umma_tf32(d_tmem, ap + k * dp_k, bq + k * dq_k, idesc, accum); accum = 1u; }
+              } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) { umma_f16(d_tmem, ap + k * dp_k, bq + k * dq_k, idesc, accum); accum = 1u; }
               }
             }
             umma_commit(bar_empty(s, stage));
@@ -418,18 +455,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     pdl_wait();  // bias / residual / output may belong to the previous grid
     pdl_trigger();
-    const int quad = warp & 3;              // TMEM lane quadrant of this warp
+    const int quad = warp;                  // TMEM lane quadrant of this warp
     const int row = quad * 32 + lane;       // MMA row within the tile
-    const int ep_tid = threadIdx.x - 64;    // 0..127
+    const int ep_tid = threadIdx.x;         // 0..127
     int acc = 0;
-    uint32_t acc_phase = 0, red_phase = 0;
+    uint32_t acc_phase = 0;
     bool ok = true;
     constexpr int kChunks = (BN + 31) / 32;
     float* red = reinterpret_cast<float*>(smem_raw + (s.red - smem_u32(smem_raw)));
+    // Split-K (one tile per cluster): rows [crank*rows_per, +rows_per) of the
+    // tile are owned by this CTA.  Every CTA pushes its partial of each row
+    // to the row's owner (st.async into recv[src][row], own rows with plain
+    // stores), so the owner needs no round trip: it waits on bar_recv for the
+    // other CTAs' bytes and sums the ksplit partials of its slice.
+    const int rows_per = kBM / ksplit;
+    const int owner = row / rows_per, orow = row % rows_per;
+    const uint32_t push_local = s.red + (uint32_t)(((crank * rows_per + orow) * p.red_stride) * 4);
+    const uint32_t push_dst = (ksplit > 1 && owner != (int)crank) ? mapa(push_local, owner) : push_local;
+    const uint32_t push_bar = ksplit > 1 ? mapa(bar_recv(s), owner) : 0u;
+    auto push4 = [&](int col, float a, float b, float c, float d) {
+      if (owner == (int)crank) st_shared_v4(push_local + col * 4, a, b, c, d);
+      else st_async_v4(push_dst + col * 4, a, b, c, d, push_bar);
+    };
     for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
       int ti, tj;
       tile_coords(p, t, ti, tj);
       const int i = ti * kBM + row;
+      if (ksplit > 1 && ep_tid == 0)
+        mbar_arrive_expect_tx(bar_recv(s), (uint32_t)((ksplit - 1) * rows_per * BN * 4));
       float racc[PROMOTE ? BN : 1];
 #pragma unroll
       for (int e = 0; e < (PROMOTE ? BN : 1); ++e) racc[e] = 0.f;
@@ -450,23 +503,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(bar_tempty(s, acc));
-        } else if (ksplit == 1) {
-#pragma unroll 1
-          for (int c = 0; c < kChunks; ++c) {
-            float v[32];
-            tmem_ld32(tbase + c * 32, v);
-            if (c == kChunks - 1) {
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(bar_tempty(s, acc));
-            }
-            const int j0 = tj * BN + c * 32;
-            const int nvalid = min(32, BN - c * 32);
-            if (nvalid == 32 && epilogue_row32_fast(p, i, j0, v)) continue;
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (e < nvalid) epilogue_store(p, i, j0 + e, v[e]);
-          }
         } else {
 #pragma unroll 1
           for (int c = 0; c < kChunks; ++c) {
@@ -478,15 +514,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (lane == 0) mbar_arrive(bar_tempty(s, acc));
             }
             const int nvalid = min(32, BN - c * 32);
-            float4* dst = reinterpret_cast<float4*>(red + row * p.red_stride + c * 32);
-            if (nvalid == 32) {
-#pragma unroll
-              for (int q = 0; q < 8; ++q)
-                dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            if (ksplit == 1) {
+              const int j0 = tj * BN + c * 32;
+              if (nvalid == 32 && epilogue_row32_fast(p, i, j0, v)) continue;
+#pragma unroll 1
+              for (int e = 0; e < nvalid; ++e) epilogue_store(p, i, j0 + e, v[e]);
             } else {
 #pragma unroll
-              for (int e = 0; e < 32; ++e)
-                if (e < nvalid) red[row * p.red_stride + c * 32 + e] = v[e];
+              for (int q = 0; q < 8; ++q)
+                if (4 * q < nvalid) push4(c * 32 + 4 * q, v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
             }
           }
         }
@@ -495,23 +531,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       if (PROMOTE) {
         if (ksplit == 1) {
-#pragma unroll
+#pragma unroll 1
           for (int e = 0; e < BN; ++e) epilogue_store(p, i, tj * BN + e, racc[e]);
         } else {
 #pragma unroll
-          for (int e = 0; e < BN; ++e) red[row * p.red_stride + e] = racc[e];
+          for (int q = 0; q < BN / 4; ++q)
+            push4(4 * q, racc[4 * q], racc[4 * q + 1], racc[4 * q + 2], racc[4 * q + 3]);
         }
       }
       if (ksplit > 1) {
-        // Split-K: the partial tile is parked in this CTA's smem; reduce a
-        // slice of rows across the cluster through distributed shared memory.
-        epi_bar_sync();
-        if (ep_tid == 0) {
-          fence_cluster();
-          for (int r = 0; r < ksplit; ++r) mbar_arrive_remote(mapa(bar_red_ready(s), r));
-        }
-        if (!mbar_wait_cluster(bar_red_ready(s), red_phase, DEV_ERR_REDUCE_TIMEOUT)) { ok = false; break; }
-        const int rows_per = kBM / ksplit;
+        epi_bar_sync();  // own rows' plain stores visible to every epilogue thread
+        if (!mbar_wait_cluster(bar_recv(s), 0, DEV_ERR_REDUCE_TIMEOUT)) { ok = false; break; }
         const int r0 = crank * rows_per;
         constexpr int kGroups = BN / 4 > 0 ? BN / 4 : 1;  // 4-column groups per row
         const int items = rows_per * kGroups;
@@ -521,35 +551,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           int rr, cg;
           if (p.swap) { rr = idx % rows_per; cg = idx / rows_per; }
           else { rr = idx / kGroups; cg = idx % kGroups; }
-          const uint32_t local = s.red + (uint32_t)(((r0 + rr) * p.red_stride + 4 * cg) * 4);
-          float4 part[8];
-#pragma unroll
-          for (int r = 0; r < 8; ++r)  // all remote loads in flight before any use
-            if (r < ksplit) part[r] = ld_cluster_f32x4(mapa(local, r));
           float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-          for (int r = 0; r < 8; ++r)
-            if (r < ksplit) { sum.x += part[r].x; sum.y += part[r].y; sum.z += part[r].z; sum.w += part[r].w; }
-          const int i = ti * kBM + r0 + rr, j = tj * BN + 4 * cg;
-          epilogue_store(p, i, j, sum.x);
-          epilogue_store(p, i, j + 1, sum.y);
-          epilogue_store(p, i, j + 2, sum.z);
-          epilogue_store(p, i, j + 3, sum.w);
+          for (int r = 0; r < ksplit; ++r) {
+            const float4 v = *reinterpret_cast<const float4*>(red + (r * rows_per + rr) * p.red_stride + 4 * cg);
+            sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+          }
+          const float quad4[4] = {sum.x, sum.y, sum.z, sum.w};
+#pragma unroll 1
+          for (int e = 0; e < 4; ++e) epilogue_store(p, ti * kBM + r0 + rr, tj * BN + 4 * cg + e, quad4[e]);
         }
-        epi_bar_sync();
-        if (ep_tid == 0) {
-          fence_cluster();
-          for (int r = 0; r < ksplit; ++r) mbar_arrive_remote(mapa(bar_red_done(s), r));
-        }
-        if (!mbar_wait_cluster(bar_red_done(s), red_phase, DEV_ERR_REDUCE_TIMEOUT)) { ok = false; break; }
-        red_phase ^= 1u;
       }
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
@@ -858,6 +875,11 @@ static void choose_split(Plan& pl, long long tiles, long long num_kb, const fml_
     const double cost = rounds * per_cta + (ks > 1 ? 4.0 : 0.0);
     if (cost < best_cost - 1e-9) { best_cost = cost; best_ks = ks; }
   }
+  const char* tune = getenv("FORGEML_GEMM_KSPLIT");  // tuning override: 1, 2, 4 or 8
+  if (tune) {
+    const int ks = atoi(tune);
+    if ((ks == 1 || ks == 2 || ks == 4 || ks == 8) && (ks == 1 || (pl.bn <= 128 && num_kb >= 2LL * ks))) best_ks = ks;
+  }
   pl.ksplit = best_ks;
   pl.stages = stages_for(pl.bn, best_ks, cfg, pl.slabs);
 }
@@ -945,7 +967,7 @@ static int launch_bn(const CUtensorMap& mp, const CUtensorMap& mq, const Params&
   cudaLaunchAttribute attr[2];
   int na = 0;
   attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[na].val.programmaticStreamSerializationAllowed = 1;
+  attr[na].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   ++na;
   if (prm.ksplit > 1) {
     attr[na].id = cudaLaunchAttributeClusterDimension;
@@ -999,12 +1021,19 @@ static int launch_plan(const Plan& pl, const CUtensorMap& mp, const CUtensorMap&
   const int smem = smem_bytes_for(pl.bn, pl.stages, pl.ksplit, &red_stride, pl.slabs);
   prm.red_stride = red_stride;
   prm.promote_kb = kPromoteKb;
-  // Persistent grid: as many CTAs (whole clusters) as are co-resident.
+  // Persistent grid (as many CTAs as are co-resident) without split-K; with
+  // split-K one cluster per tile (the push reduction uses its receive
+  // buffer once).
   const long long want = (long long)prm.num_tiles * prm.ksplit;
-  int res = resident_ctas(pl.bn, pl.promote, pl.ksplit, smem, sms);
-  if (res <= 0) res = std::max(sms / prm.ksplit, 1) * prm.ksplit;
-  int grid = (int)std::min<long long>(want, res);
-  grid = std::max(grid / prm.ksplit, 1) * prm.ksplit;
+  int grid;
+  if (prm.ksplit > 1) {
+    if (want > 0x7fffffffLL) return fail(FML_EUNSUPPORTED, "gemm: too many split-K tiles");
+    grid = (int)want;
+  } else {
+    int res = resident_ctas(pl.bn, pl.promote, pl.ksplit, smem, sms);
+    if (res <= 0) res = sms;
+    grid = (int)std::min<long long>(want, res);
+  }
   if (pl.promote) {
     switch (pl.bn) {
       case 16: return launch_bn<16, true>(mp, mq, prm, grid, smem, st);

@@ -229,6 +229,9 @@ FML_API int neb_add(const void* a, const void* b, void* y, int64_t n, int dtype,
 FML_API const char* fml_last_error(void);
 /* Reads and clears the device-side error word of the current device
  * (bounded waits that expired, out-of-range token ids).  0 = clean.
+ * Bits: 1 GEMM pipeline wait expired, 2 token id out of range, 4 attention
+ * position/slot out of range, 8 split-K cluster reduce wait expired,
+ * 16 attention copy-pipeline wait expired.
  * Synchronizes the current device. */
 FML_API int fml_device_status(void);
 /* Number of kernel launches issued by this library in this process. */
