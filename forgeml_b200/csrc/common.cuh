@@ -234,6 +234,13 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
       : "memory");
 }
 
+// Prefetch [src, src + bytes) into L2 (no shared memory, no completion);
+// 16-byte aligned address, size a multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+               : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // Device: tcgen05 (UMMA, TMEM)
 // ---------------------------------------------------------------------------

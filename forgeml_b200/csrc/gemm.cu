@@ -240,8 +240,10 @@ __device__ __forceinline__ bool epilogue_row32_fast(const Params& p, int m, int 
   return true;
 }
 
+// Narrow tiles are register-bounded for two CTAs per SM (the decode weight
+// stream, ~100 KB of shared memory each).
 template <int BN, bool PROMOTE>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
                 const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -333,6 +335,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (pre_limit > 0 && lane == 0) {
       int ti0, tj0;
       tile_coords(p, cluster_id, ti0, tj0);
+      // The rest of the first tile's weight slabs go to L2 now, so that DRAM
+      // keeps streaming this kernel's weights while the previous kernel
+      // finishes; after the dependency wait they come from L2.
+      if (parity == 0) {
+        const int kb_rest = kb_begin + pre_limit * S;
+        const uint8_t* rest = p.p_packed + ((size_t)ti0 * p.num_kb + kb_rest) * (size_t)(kBM * kSlab);
+        for (int kb = kb_rest; kb < kb_end; kb += 4)
+          bulk_prefetch_l2(rest + (size_t)(kb - kb_rest) * (kBM * kSlab), (uint32_t)min(4, kb_end - kb) * kBM * kSlab);
+      }
       for (int st = parity; st < pre_limit; st += 2) {
         const int kb = kb_begin + st * S;
         const int nsl = min(S, kb_end - kb);
@@ -780,16 +791,35 @@ static int smem_bytes_for(int bn, int stages, int ksplit, int* red_stride, int s
   return 1024 + stages * stage_bytes + kBarBytes + 16 + red;
 }
 
+// CTAs of one SM this configuration fits: shared memory, registers, threads
+// and TMEM columns.  Computed here because the occupancy API reports one CTA
+// per SM for any kernel that uses tcgen05, while the hardware co-schedules
+// several when their resources fit (measured on B200).
+template <int BN, bool PROMOTE>
+static int per_sm_ctas(int smem) {
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, gemm_kernel<BN, PROMOTE>) != cudaSuccess) return 1;
+  int dev = current_device(), smem_sm = 0;
+  if (cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess || smem_sm <= 0)
+    smem_sm = 233472;
+  const int warps = kThreads / 32;
+  const int regs_block = warps * ((fa.numRegs * 32 + 255) / 256) * 256;
+  constexpr int acc = BN < 32 ? 32 : BN;
+  constexpr int tmem_cols = (2 * acc <= 32) ? 32 : (2 * acc <= 64) ? 64 : (2 * acc <= 128) ? 128 : (2 * acc <= 256) ? 256 : 512;
+  int n = smem_sm / (smem + (int)fa.sharedSizeBytes + 1024);
+  n = std::min(n, 65536 / std::max(regs_block, 1));
+  n = std::min(n, 2048 / kThreads);
+  n = std::min(n, 512 / tmem_cols);
+  return std::max(n, 1);
+}
+
 template <int BN, bool PROMOTE>
 static int resident_ctas_t(int ksplit, int smem, int sms) {
   cudaFuncSetAttribute(gemm_kernel<BN, PROMOTE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-  if (ksplit <= 1) {
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemm_kernel<BN, PROMOTE>, kThreads, smem) !=
-            cudaSuccess || per_sm <= 0)
-      per_sm = 1;
-    return per_sm * sms;
-  }
+  const int per_sm = per_sm_ctas<BN, PROMOTE>(smem);
+  if (ksplit <= 1) return per_sm * sms;
+  // Clusters: the occupancy API's count (one CTA per SM, whole clusters
+  // inside a GPC) scaled by the CTAs an SM really holds.
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(ksplit);
   lc.blockDim = dim3(kThreads);
@@ -803,7 +833,7 @@ static int resident_ctas_t(int ksplit, int smem, int sms) {
   lc.numAttrs = 1;
   int n = 0;
   if (cudaOccupancyMaxActiveClusters(&n, gemm_kernel<BN, PROMOTE>, &lc) != cudaSuccess || n <= 0) return 0;
-  return n * ksplit;
+  return n * ksplit * per_sm;
 }
 
 // CTAs of this kernel configuration that can be resident at once (cached).
@@ -838,8 +868,12 @@ static int resident_ctas(int bn, bool promote, int ksplit, int smem, int sms) {
   return r;
 }
 
-static int stages_for(int bn, int ksplit, const fml_tile_cfg* cfg, int slabs) {
-  int stages = kMaxStages;
+// Pipeline stages: the hint, else as many as fit; a pre-packed (decode)
+// weight stream defaults to four one-slab stages, which keeps the CTA near
+// 100 KB of shared memory so that the next kernel's CTAs are resident beside
+// it and prefetch their weights during programmatic dependent launch.
+static int stages_for(int bn, int ksplit, const fml_tile_cfg* cfg, int slabs, bool packed = false) {
+  int stages = packed ? 4 : kMaxStages;
   if (cfg && cfg->num_stages > 0) stages = std::min(cfg->num_stages, kMaxStages);
   while (stages > 2 && smem_bytes_for(bn, stages, ksplit, nullptr, slabs) > kSmemLimit) --stages;
   return stages;
@@ -847,10 +881,11 @@ static int stages_for(int bn, int ksplit, const fml_tile_cfg* cfg, int slabs) {
 
 // K slabs per stage: block_k elements of K per stage when hinted; by default
 // four slabs (64 KB of weights per stage) for the bandwidth-bound narrow tiles
-// (BN <= 64) and one slab for the wide compute-bound tiles.
-static int slabs_for(const fml_tile_cfg* cfg, int dtype, bool promote, int bn) {
+// (BN <= 64) streamed through TMA, one slab for pre-packed weights and for
+// the wide compute-bound tiles.
+static int slabs_for(const fml_tile_cfg* cfg, int dtype, bool promote, int bn, bool packed = false) {
   if (promote) return 1;
-  if (!cfg || cfg->block_k <= 0) return bn <= 64 ? 4 : 1;
+  if (!cfg || cfg->block_k <= 0) return (bn <= 64 && !packed) ? 4 : 1;
   const int s = cfg->block_k * (int)dtype_size(dtype) / kSlab;
   return s >= 4 ? 4 : (s >= 2 ? 2 : 1);
 }
@@ -864,7 +899,7 @@ static void choose_split(Plan& pl, long long tiles, long long num_kb, const fml_
   double best_cost = 1e30;
   for (int ks : {1, 2, 4, 8}) {
     if (ks > 1 && (pl.bn > 128 || num_kb < 2LL * ks || tiles * 2 > sms)) continue;
-    const int st = stages_for(pl.bn, ks, cfg, pl.slabs);
+    const int st = stages_for(pl.bn, ks, cfg, pl.slabs, pl.packed);
     const int smem = smem_bytes_for(pl.bn, st, ks, nullptr, pl.slabs);
     if (smem > kSmemLimit) continue;
     const int res = resident_ctas(pl.bn, pl.promote, ks, smem, sms);
@@ -881,7 +916,7 @@ static void choose_split(Plan& pl, long long tiles, long long num_kb, const fml_
     if ((ks == 1 || ks == 2 || ks == 4 || ks == 8) && (ks == 1 || (pl.bn <= 128 && num_kb >= 2LL * ks))) best_ks = ks;
   }
   pl.ksplit = best_ks;
-  pl.stages = stages_for(pl.bn, best_ks, cfg, pl.slabs);
+  pl.stages = stages_for(pl.bn, best_ks, cfg, pl.slabs, pl.packed);
 }
 
 static int pick_bn(const Plan& pl, long long I, long long J, const fml_tile_cfg* cfg, int sms) {
@@ -1033,6 +1068,11 @@ static int launch_plan(const Plan& pl, const CUtensorMap& mp, const CUtensorMap&
     int res = resident_ctas(pl.bn, pl.promote, pl.ksplit, smem, sms);
     if (res <= 0) res = sms;
     grid = (int)std::min<long long>(want, res);
+  }
+  if (getenv("FORGEML_GEMM_DEBUG")) {  // diagnostic: the chosen plan
+    const int res = resident_ctas(pl.bn, pl.promote, pl.ksplit, smem, sms);
+    fprintf(stderr, "[fml_gemm] I=%d J=%d num_kb=%d bn=%d swap=%d packed=%d ksplit=%d slabs=%d stages=%d smem=%d grid=%d resident=%d\n",
+            prm.I, prm.J, prm.num_kb, pl.bn, prm.swap, pl.packed ? 1 : 0, pl.ksplit, pl.slabs, pl.stages, smem, grid, res);
   }
   if (pl.promote) {
     switch (pl.bn) {
@@ -1213,7 +1253,7 @@ extern "C" int fml_linear_packed(const void* x, int64_t ldx, const void* packed,
   if (pl.Q.pack) return fail(FML_EUNSUPPORTED, "linear_packed: x must be row-major with 16-byte aligned rows");
   pl.keff = k;
   pl.ws_bytes = 0;
-  pl.slabs = slabs_for(cfg, dtype, false, pl.bn);
+  pl.slabs = slabs_for(cfg, dtype, false, pl.bn, true);
   const long long tiles = ((n + kBM - 1) / kBM) * ((m + pl.bn - 1) / pl.bn);
   choose_split(pl, tiles, packed_kb(k, dtype), cfg, sms);
   CUtensorMap mq;
