@@ -15,7 +15,9 @@ JSON line keys (one line on rank 0):
   value        decode tokens/s, device-timed (CUDA events, max over ranks)
   e2e          the same metric through Engine.forward with the step's tokens
                copied from pinned host memory and the argmax ids read back
-  roofline     decode-attention kernel (HBM): algorithmic bytes / event time
+  roofline     the decode step's dominant kernel family (HBM): algorithmic bytes /
+               CUDA-event time of that family's launches replayed from a graph;
+               roofline_other the other family, roofline_step the whole step
   gemm         fused linear+GELU GEMM TFLOP/s at 8192^3 bf16 (N=1)
   cpu_baseline the CPU oracle of the same decode step on the host cores (N=1)
 --impl reference times that CPU restatement alone (rank 0; other ranks exit 0).
@@ -191,37 +193,118 @@ def gemm_headline(dev) -> dict:
             "peak_tflops": pk["bf16_tflops"], "frac": tf / pk["bf16_tflops"], "peak_source": pk["source"]}
 
 
-def attention_roofline(engine, dev, ctx_len: int) -> dict:
-    """Time the decode-attention kernel alone on the engine's own cache pool."""
+# DRAM traffic per launch over the algorithmic bytes, from one ncu capture of
+# each kernel family (dram__bytes_read.sum + dram__bytes_write.sum):
+#   attention: ncu --set full -k regex:neb_attn -s 3 -c 1 ... bench.py --case attention --steps 20
+#   gemm:      ncu --set full -k regex:gemm_kernel ... bench.py --case gemm-decode --steps 20 (down projection)
+# Traffic in the JSON line is this ratio times the launch's algorithmic bytes.
+TRAFFIC_RATIO = {"attention": None, "gemm": None}
+
+
+def _graph_time_us(fns, reps: int = 5) -> float:
+    """Device time per call of `fns` replayed from one CUDA graph (CUDA events
+    on the replay stream, best of `reps` replays)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for f in fns:
+            f()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for f in fns:
+            f()
+    g.replay()
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1) * 1e3)
+    del g
+    return best
+
+
+def kernel_rooflines(engine, dev, ctx_len: int, ms_per_step: float) -> dict:
+    """HBM rooflines of the decode step's two kernel families, each timed live
+    with CUDA events as one step's launches of that family replayed from a
+    CUDA graph on the engine's own weights and cache pools:
+      gemm       gemm_kernel (the 4 linears of every layer + lm_head);
+                 algorithmic bytes = weights + activations in + outputs (+ residual)
+      attention  neb_attn_bulk_kernel, one launch per layer at the step's context;
+                 algorithmic bytes = K + V rows + q + out
+    The family with the larger share of the step is reported as `roofline`."""
     from forgeml_b200.nebula import ops
+    from forgeml_b200 import _native
 
     dec = engine.decoder
-    lid = dec.owned_layer_ids[0]
-    hl, hd = dec.num_heads_local, dec.head_dim
-    q = torch.randn(BATCH, 1, hl, hd, device=dev, dtype=dec.dtype)
-    slots = torch.arange(BATCH, dtype=torch.int32, device=dev)
-    starts = torch.full((BATCH,), ctx_len - 1, dtype=torch.int32, device=dev)
-    kp, vp = dec.cache.k_pool[lid], dec.cache.v_pool[lid]
-    out = torch.empty(BATCH, 1, hl * hd, device=dev, dtype=dec.dtype)
-    for _ in range(5):
-        ops.attention(q, kp, vp, slots, starts, out)
-    torch.cuda.synchronize()
-    reps = 50
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(reps):
-        ops.attention(q, kp, vp, slots, starts, out)
-    e.record()
-    torch.cuda.synchronize()
-    sec = s.elapsed_time(e) / reps * 1e-3
     es = torch.empty((), dtype=dec.dtype).element_size()
-    algo = BATCH * hl * (2 * ctx_len * hd + 2 * hd) * es  # K + V rows + q + out
-    pk = _peaks()
-    ach = algo / sec / 1e9
-    return {"kernel": "neb_attn_kernel (decode attention over the KV pool)", "bound": "hbm",
-            "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"],
-            "peak_source": pk["source"], "algorithmic_bytes_per_launch": algo, "us_per_launch": sec * 1e6,
-            "context": ctx_len, "traffic": None}
+    b, h = BATCH, dec.config.hidden_size
+    hl_hd = dec.num_heads_local * dec.head_dim
+    g = torch.Generator(device=dev).manual_seed(11)
+
+    def rnd(*shape):
+        return torch.randn(*shape, device=dev, generator=g).to(dec.dtype)
+
+    # ---- GEMM family: one decode step's linears
+    x = rnd(b, h)
+    attn = rnd(b, hl_hd)
+    fns, gbytes = [], 0
+    for L in dec.layers:
+        f_l = L.wup.shape[0]
+        qkv_out, o_out, up_out, dn_out = (torch.empty(b, n, device=dev, dtype=dec.dtype)
+                                          for n in (3 * hl_hd, h, f_l, h))
+        mid = rnd(b, f_l)
+        res = x if dec.context.tp_size == 1 else None
+        fns += [lambda L=L, o=qkv_out: L.qkv(x, o),
+                lambda L=L, o=o_out, r=res: L.o(attn, o, residual=r),
+                lambda L=L, o=up_out: L.up(x, o, act=_native.ACT_GELU_TANH),
+                lambda L=L, o=dn_out, m=mid, r=res: L.down(m, o, residual=r)]
+        for w, n_in, n_out, r in ((L.wqkv, h, 3 * hl_hd, 0), (L.wo, hl_hd, h, res is not None),
+                                  (L.wup, h, f_l, 0), (L.wdown, f_l, h, res is not None)):
+            gbytes += (w.numel() + b * n_in + b * n_out * (2 if r else 1)) * es
+    if dec.is_last:
+        head_out = torch.empty(b, dec.config.vocab_size, device=dev, dtype=dec.dtype)
+        fns.append(lambda: dec.head_gemm(x, head_out))
+        gbytes += (dec.head.numel() + b * h + b * dec.config.vocab_size) * es
+    g_us = _graph_time_us(fns)
+    n_g = len(fns)
+
+    # ---- attention family: one launch per layer at the step's context
+    hl, hd = dec.num_heads_local, dec.head_dim
+    q = rnd(b, 1, hl, hd)
+    slots = torch.arange(b, dtype=torch.int32, device=dev)
+    starts = torch.full((b,), ctx_len - 1, dtype=torch.int32, device=dev)
+    aout = torch.empty(b, 1, hl * hd, device=dev, dtype=dec.dtype)
+    afns = [lambda lid=lid: ops.attention(q, dec.cache.k_pool[lid], dec.cache.v_pool[lid], slots, starts, aout)
+            for lid in dec.owned_layer_ids]
+    a_us = _graph_time_us(afns)
+    abytes = len(afns) * b * hl * (2 * ctx_len * hd + 2 * hd) * es
+
+    pk_ = _peaks()
+    peak = pk_["hbm_gbs"]
+
+    def entry(kernel, us, nbytes, launches, family, **more):
+        ach = nbytes / (us * 1e-6) / 1e9
+        per_launch = nbytes / launches
+        ratio = TRAFFIC_RATIO.get(family)
+        return {"kernel": kernel, "bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                "peak_source": pk_["source"], "traffic": (ratio * per_launch) if ratio else None,
+                "algorithmic_bytes_per_launch": per_launch, "us_per_launch": us / launches,
+                "launches_per_step": launches, "us_per_step": us, **more}
+
+    gemm = entry("gemm_kernel (decode linears: qkv/o/up/down x layers + lm_head)", g_us, gbytes, n_g, "gemm")
+    att = entry("neb_attn_bulk_kernel (decode attention over the KV pool)", a_us, abytes, len(afns), "attention",
+                context=ctx_len)
+    step_bytes = gbytes + abytes
+    step = {"bound": "hbm", "bytes_per_step": step_bytes, "achieved": step_bytes / (ms_per_step * 1e-3) / 1e9,
+            "peak": peak, "unit": "GB/s", "frac": step_bytes / (ms_per_step * 1e-3) / 1e9 / peak}
+    dominant, other = (gemm, att) if g_us >= a_us else (att, gemm)
+    return {"roofline": dominant, "roofline_other": other, "roofline_step": step}
 
 
 def run_native(args) -> None:
@@ -333,7 +416,8 @@ def run_native(args) -> None:
 
     extra = {}
     if rank == 0:
-        extra["roofline"] = attention_roofline(engine, dev, PROMPT + W + K)
+        with torch.inference_mode():
+            extra.update(kernel_rooflines(engine, dev, PROMPT + W + K, ms / K))
         if world == 1 and not args.no_gemm:
             extra["gemm"] = gemm_headline(dev)
     cpu = None
@@ -368,9 +452,10 @@ def run_case(args) -> None:
 
     attention    decode attention, batch 32 x 16 heads x 128, context 1024,
                  one layer's KV pool (268 MB, > L2)
-    gemm-decode  the c4 decode GEMMs at batch 32: QKV 6144x2048, o 2048x2048
-                 (+residual), up 8192x2048 (+tanh GELU), down 2048x8192 (+residual),
-                 lm_head 32000x2048
+    gemm-decode  the c4 decode GEMMs at batch 32 on pre-packed weights (the
+                 engine's path): QKV 6144x2048, o 2048x2048 (+residual),
+                 up 8192x2048 (+tanh GELU), down 2048x8192 (+residual),
+                 lm_head 32000x2048; chains replayed from a CUDA graph
     gemm         8192^3 bf16 + bias + GELU
     """
     from forgeml_b200.forgeml import kernels
@@ -381,18 +466,6 @@ def run_case(args) -> None:
     reps = args.steps
     res = {}
 
-    def timed(fn, n):
-        for _ in range(3):
-            fn()
-        torch.cuda.synchronize()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(n):
-            fn()
-        e.record()
-        torch.cuda.synchronize()
-        return s.elapsed_time(e) / n * 1e3  # us
-
     g = torch.Generator(device=dev).manual_seed(0)
     if args.case == "attention":
         b, h, d, ctx = BATCH, 16, 128, 1024
@@ -402,23 +475,26 @@ def run_case(args) -> None:
         slots = torch.arange(b, dtype=torch.int32, device=dev)
         starts = torch.full((b,), ctx - 1, dtype=torch.int32, device=dev)
         out = torch.empty(b, 1, h * d, device=dev, dtype=torch.bfloat16)
-        us = timed(lambda: ops.attention(q, kp, vp, slots, starts, out), reps)
+        us = _graph_time_us([lambda: ops.attention(q, kp, vp, slots, starts, out)] * reps) / reps
         algo = b * h * (2 * ctx * d + 2 * d) * 2
         res["attention"] = {"us": us, "GB/s": algo / (us * 1e-6) / 1e9, "algo_bytes": algo}
     elif args.case == "gemm-decode":
+        from forgeml_b200.linear import PackedLinear
         m = BATCH
         for name, n, k, act, resid in (("qkv", 6144, 2048, 0, False), ("o", 2048, 2048, 0, True),
                                        ("up", 8192, 2048, 2, False), ("down", 2048, 8192, 0, True),
                                        ("lm_head", 32000, 2048, 0, False)):
+            # enough weight copies that the replayed chain streams > L2 from HBM
+            copies = max(2, min(reps, int(400e6 // (n * k * 2)) + 1))
+            ws = [PackedLinear((torch.randn(n, k, device=dev, generator=g) * 0.02).to(torch.bfloat16))
+                  for _ in range(copies)]
             x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
-            w = (torch.randn(n, k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
             r = torch.randn(m, n, device=dev, generator=g).to(torch.bfloat16) if resid else None
             out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
-            actn = "gelu" if act else "none"
-            apx = "tanh" if act == 2 else "none"
-            us = timed(lambda: kernels.matmul(x, w.t(), activation=actn, approximate=apx, out=out, residual=r), reps)
+            us = _graph_time_us([lambda w=ws[i % copies]: w(x, out, act, r) for i in range(reps)]) / reps
             algo = (n * k + m * k + m * n * (2 if resid else 1)) * 2
-            res[name] = {"us": us, "GB/s": algo / (us * 1e-6) / 1e9, "TFLOP/s": 2 * m * n * k / (us * 1e-6) / 1e12}
+            res[name] = {"us": us, "GB/s": algo / (us * 1e-6) / 1e9, "algo_bytes": algo}
+            del ws
     elif args.case == "gemm":
         res["gemm"] = gemm_headline(dev)
     print(json.dumps({"case": args.case, "results": res}), flush=True)

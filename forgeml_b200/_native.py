@@ -90,6 +90,13 @@ _SIGNATURES = {
     "neb_embed": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I, _P]),
     "neb_argmax": (_I, [_P, _I64, _I64, _I64, _P, _I, _P]),
     "neb_add": (_I, [_P, _P, _P, _I64, _I, _P]),
+    "neb_ar_handle_bytes": (_I64, []),
+    "neb_ar_create": (_I, [_I64, _I, _I, ctypes.c_double, ctypes.POINTER(ctypes.c_void_p), _P]),
+    "neb_ar_open": (_I, [_P, _P]),
+    "neb_ar_set_peers": (_I, [_P, ctypes.POINTER(ctypes.c_void_p)]),
+    "neb_ar_buffer": (_P, [_P]),
+    "neb_ar_all_reduce": (_I, [_P, _P, _P, _P, _I64, _I, _P]),
+    "neb_ar_destroy": (_I, [_P]),
     "fml_last_error": (ctypes.c_char_p, []),
     "fml_device_status": (_I, []),
     "fml_launch_count": (_I64, []),

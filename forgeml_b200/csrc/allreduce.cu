@@ -1,0 +1,271 @@
+// Tensor-parallel SUM all-reduce over NVLink peer memory, fused with the
+// residual add that follows it in Nebula's decode step:
+//
+//   out = round(round(sum_r part_r) + residual)      (residual optional)
+//
+// which is ParallelContext.all_reduce (src/nebula/parallel.py:112-116, a SUM
+// over the TP group) followed by the `x = x + part` of
+// src/nebula/runtime.py:146,154, each rounded to the model dtype.
+//
+// One-shot push design for the small messages of a decode step (B x T x d,
+// 128 KB at config 4): every rank owns a symmetric buffer, opened by its
+// peers through CUDA IPC.  CTA b of rank r writes chunk b of its partial into
+// slot r of every rank's buffer (NVLink stores), fences, and raises flag
+// [r][b] on every peer with the launch's epoch; then it waits until every
+// peer's flag [q][b] carries the same epoch, and sums the world slots of its
+// chunk in rank order, so all ranks produce bit-identical results.
+//
+// Epochs live in the buffer (one counter per CTA index, advanced by the CTA
+// itself), so a launch recorded in a CUDA graph stays correct on replay.  Two
+// buffer sets alternate by epoch parity: CTA b of rank r writes set e&1 of a
+// peer only after it has seen that peer's epoch e-1 flag for chunk b, which the
+// peer raised after it finished reading set e&1 in epoch e-2.  The grid size
+// is fixed, so CTA b always owns the same chunk of every message.
+//
+// Every wait is bounded (the context's timeout); on expiry the kernel raises
+// DEV_ERR_AR_TIMEOUT in the device error word and finishes without hanging.
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+
+namespace fml {
+namespace ar {
+
+constexpr int kMaxWorld = 8;
+constexpr int kBlocks = 32;     // fixed grid (one chunk per CTA index)
+constexpr int kThreads = 256;
+
+struct Layout {
+  long long max_bytes;  // bytes per slot (one rank's message)
+  int world;
+  // byte offsets inside a rank's buffer
+  __host__ __device__ long long data_off(int set, int slot) const { return ((long long)set * world + slot) * max_bytes; }
+  __host__ __device__ long long flags_off() const { return 2LL * world * max_bytes; }
+  __host__ __device__ long long flag_off(int set, int src, int blk) const {
+    return flags_off() + (((long long)set * world + src) * kBlocks + blk) * 4;
+  }
+  __host__ __device__ long long epochs_off() const { return flags_off() + 2LL * world * kBlocks * 4; }
+  __host__ __device__ long long total() const { return epochs_off() + kBlocks * 4; }
+};
+
+struct Args {
+  uint8_t* base[kMaxWorld];  // every rank's buffer, mapped into this process (own included)
+  Layout lay;
+  int rank;
+  long long timeout_cycles;
+};
+
+struct Ctx {
+  Args a;
+  uint8_t* own = nullptr;
+  bool opened[kMaxWorld] = {};
+  int device = 0;
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ void add_vec(float (&acc)[16 / sizeof(T)], const uint4& raw) {
+  const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+  for (int i = 0; i < (int)(16 / sizeof(T)); ++i) acc[i] += to_f32<T>(e[i]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) ar_kernel(const Args a, const T* __restrict__ part,
+                                                      const T* __restrict__ residual, T* __restrict__ out,
+                                                      long long nvec) {
+  constexpr int VE = 16 / sizeof(T);
+  pdl_wait();
+  pdl_trigger();
+  const int blk = blockIdx.x, tid = threadIdx.x;
+  const int W = a.lay.world, r = a.rank;
+  uint32_t* epochs = reinterpret_cast<uint32_t*>(a.base[r] + a.lay.epochs_off());
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_ok;
+  if (tid == 0) {
+    s_epoch = epochs[blk] + 1u;
+    s_ok = 1;
+  }
+  __syncthreads();
+  const uint32_t e = s_epoch;
+  const int set = (int)(e & 1u);
+  const long long per = (nvec + kBlocks - 1) / kBlocks;
+  const long long v0 = (long long)blk * per, v1 = min(nvec, v0 + per);
+  const uint4* src = reinterpret_cast<const uint4*>(part);
+
+  // 1. push this chunk of the partial into slot r of every rank
+  for (long long i = v0 + tid; i < v1; i += kThreads) {
+    const uint4 v = src[i];
+    for (int q = 0; q < W; ++q)
+      reinterpret_cast<uint4*>(a.base[q] + a.lay.data_off(set, r))[i] = v;
+  }
+  __threadfence_system();
+  __syncthreads();
+  // 2. raise flag [r][blk] on every peer
+  if (tid < W && tid != r)
+    st_release_sys(reinterpret_cast<uint32_t*>(a.base[tid] + a.lay.flag_off(set, r, blk)), e);
+  // 3. wait for every peer's flag [q][blk] (bounded)
+  if (tid < W && tid != r) {
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(a.base[r] + a.lay.flag_off(set, tid, blk));
+    const long long t0 = clock64();
+    while (ld_acquire_sys(f) != e) {
+      if (clock64() - t0 > a.timeout_cycles) {
+        raise_device_error(DEV_ERR_AR_TIMEOUT);
+        s_ok = 0;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  // 4. sum the world slots of this chunk in rank order, add the residual
+  for (long long i = v0 + tid; i < v1; i += kThreads) {
+    float acc[VE];
+#pragma unroll
+    for (int k = 0; k < VE; ++k) acc[k] = 0.f;
+    for (int q = 0; q < W; ++q) add_vec<T>(acc, reinterpret_cast<const uint4*>(a.base[r] + a.lay.data_off(set, q))[i]);
+    float res[VE];
+    if (residual != nullptr) {
+      const uint4 rv = reinterpret_cast<const uint4*>(residual)[i];
+      const T* re = reinterpret_cast<const T*>(&rv);
+#pragma unroll
+      for (int k = 0; k < VE; ++k) res[k] = to_f32<T>(re[k]);
+    }
+    uint4 o;
+    T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+    for (int k = 0; k < VE; ++k) {
+      float x = to_f32<T>(from_f32<T>(acc[k]));      // the all-reduced partial in the model dtype
+      if (residual != nullptr) x = x + res[k];       // x + part, rounded once more below
+      oe[k] = from_f32<T>(x);
+    }
+    reinterpret_cast<uint4*>(out)[i] = o;
+  }
+  if (tid == 0) epochs[blk] = e;
+}
+
+}  // namespace ar
+}  // namespace fml
+
+using fml::ar::Ctx;
+using fml::ar::kMaxWorld;
+using fml::fail;
+
+extern "C" {
+
+int64_t neb_ar_handle_bytes(void) { return (int64_t)sizeof(cudaIpcMemHandle_t); }
+
+int neb_ar_create(int64_t max_bytes, int world, int rank, double timeout_ms, void** ctx_out, void* handle_out) {
+  if (!ctx_out || !handle_out) return fail(FML_EINVAL, "neb_ar_create: null pointer");
+  if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world)
+    return fail(FML_EINVAL, "neb_ar_create: world must be 1..8 and 0 <= rank < world");
+  if (max_bytes <= 0 || max_bytes % 16 != 0) return fail(FML_EINVAL, "neb_ar_create: max_bytes must be a positive multiple of 16");
+  if (!(timeout_ms > 0)) return fail(FML_EINVAL, "neb_ar_create: timeout must be positive");
+  Ctx* c = new Ctx();
+  c->a.lay.max_bytes = max_bytes;
+  c->a.lay.world = world;
+  c->a.rank = rank;
+  int clk_khz = 0;
+  c->device = fml::current_device();
+  if (cudaDeviceGetAttribute(&clk_khz, cudaDevAttrClockRate, c->device) != cudaSuccess || clk_khz <= 0) clk_khz = 2000000;
+  c->a.timeout_cycles = (long long)(timeout_ms * (double)clk_khz);
+  const long long total = c->a.lay.total();
+  cudaError_t e = cudaMalloc(&c->own, (size_t)total);
+  if (e != cudaSuccess) { delete c; return fml::check_cuda(e, "neb_ar_create: cudaMalloc"); }
+  e = cudaMemset(c->own, 0, (size_t)total);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, c->own);
+  if (e != cudaSuccess) {
+    cudaFree(c->own);
+    delete c;
+    return fml::check_cuda(e, "neb_ar_create: buffer setup");
+  }
+  std::memcpy(handle_out, &h, sizeof(h));
+  for (int q = 0; q < kMaxWorld; ++q) c->a.base[q] = nullptr;
+  c->a.base[rank] = c->own;
+  *ctx_out = c;
+  return FML_OK;
+}
+
+// handles: world consecutive IPC handles (neb_ar_handle_bytes() each), as
+// returned by neb_ar_create on every rank; this rank's own entry is ignored.
+int neb_ar_open(void* ctx, const void* handles) {
+  Ctx* c = static_cast<Ctx*>(ctx);
+  if (!c || !handles) return fail(FML_EINVAL, "neb_ar_open: null pointer");
+  const auto* hs = static_cast<const cudaIpcMemHandle_t*>(handles);
+  for (int q = 0; q < c->a.lay.world; ++q) {
+    if (q == c->a.rank || c->opened[q]) continue;
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, hs[q], cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return fml::check_cuda(e, "neb_ar_open: cudaIpcOpenMemHandle");
+    c->a.base[q] = static_cast<uint8_t*>(p);
+    c->opened[q] = true;
+  }
+  return FML_OK;
+}
+
+// Single-process form: device pointers of every rank's buffer (own entry
+// ignored), e.g. buffers of other contexts of this process.  No IPC mapping.
+int neb_ar_set_peers(void* ctx, void* const* bases) {
+  Ctx* c = static_cast<Ctx*>(ctx);
+  if (!c || !bases) return fail(FML_EINVAL, "neb_ar_set_peers: null pointer");
+  for (int q = 0; q < c->a.lay.world; ++q) {
+    if (q == c->a.rank) continue;
+    if (!bases[q]) return fail(FML_EINVAL, "neb_ar_set_peers: null peer buffer");
+    c->a.base[q] = static_cast<uint8_t*>(bases[q]);
+  }
+  return FML_OK;
+}
+
+void* neb_ar_buffer(void* ctx) { return ctx ? static_cast<Ctx*>(ctx)->own : nullptr; }
+
+int neb_ar_all_reduce(void* ctx, const void* part, const void* residual, void* out, int64_t n, int dtype, void* stream) {
+  Ctx* c = static_cast<Ctx*>(ctx);
+  if (!c || !part || !out) return fail(FML_EINVAL, "neb_ar_all_reduce: null pointer");
+  if (!fml::valid_dtype(dtype)) return fail(FML_EINVAL, "neb_ar_all_reduce: bad dtype");
+  for (int q = 0; q < c->a.lay.world; ++q)
+    if (!c->a.base[q]) return fail(FML_EINVAL, "neb_ar_all_reduce: peers not opened");
+  const long long bytes = n * (long long)fml::dtype_size(dtype);
+  if (n <= 0 || bytes % 16 != 0) return fail(FML_EUNSUPPORTED, "neb_ar_all_reduce: message must be a positive multiple of 16 bytes");
+  if (bytes > c->a.lay.max_bytes) return fail(FML_EUNSUPPORTED, "neb_ar_all_reduce: message larger than the buffer slot");
+  for (const void* p : {part, residual, (const void*)out})
+    if (p && reinterpret_cast<uintptr_t>(p) % 16 != 0) return fail(FML_EUNSUPPORTED, "neb_ar_all_reduce: pointers must be 16-byte aligned");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const long long nvec = bytes / 16;
+  cudaError_t e;
+  const dim3 grid(fml::ar::kBlocks), block(fml::ar::kThreads);
+  if (dtype == FML_F32)
+    e = fml::launch_pdl(fml::ar::ar_kernel<float>, grid, block, 0, st, 1, c->a, static_cast<const float*>(part),
+                        static_cast<const float*>(residual), static_cast<float*>(out), nvec);
+  else if (dtype == FML_BF16)
+    e = fml::launch_pdl(fml::ar::ar_kernel<__nv_bfloat16>, grid, block, 0, st, 1, c->a,
+                        static_cast<const __nv_bfloat16*>(part), static_cast<const __nv_bfloat16*>(residual),
+                        static_cast<__nv_bfloat16*>(out), nvec);
+  else
+    e = fml::launch_pdl(fml::ar::ar_kernel<__half>, grid, block, 0, st, 1, c->a, static_cast<const __half*>(part),
+                        static_cast<const __half*>(residual), static_cast<__half*>(out), nvec);
+  fml::count_launch();
+  return fml::check_cuda(e, "neb_ar_all_reduce launch");
+}
+
+int neb_ar_destroy(void* ctx) {
+  Ctx* c = static_cast<Ctx*>(ctx);
+  if (!c) return FML_OK;
+  cudaDeviceSynchronize();
+  for (int q = 0; q < kMaxWorld; ++q)
+    if (c->opened[q] && c->a.base[q]) cudaIpcCloseMemHandle(c->a.base[q]);
+  if (c->own) cudaFree(c->own);
+  delete c;
+  return FML_OK;
+}
+
+}  // extern "C"

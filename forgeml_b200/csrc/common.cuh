@@ -42,6 +42,7 @@ enum : int {
   DEV_ERR_ATTN_RANGE = 1 << 2,
   DEV_ERR_REDUCE_TIMEOUT = 1 << 3,
   DEV_ERR_ATTN_TIMEOUT = 1 << 4,
+  DEV_ERR_AR_TIMEOUT = 1 << 5,
 };
 extern __device__ int g_device_error;
 
@@ -232,13 +233,6 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
       : "memory");
-}
-
-// Prefetch [src, src + bytes) into L2 (no shared memory, no completion);
-// 16-byte aligned address, size a multiple of 16.
-__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
-               : "memory");
 }
 
 // ---------------------------------------------------------------------------

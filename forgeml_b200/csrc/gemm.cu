@@ -335,15 +335,6 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
     if (pre_limit > 0 && lane == 0) {
       int ti0, tj0;
       tile_coords(p, cluster_id, ti0, tj0);
-      // The rest of the first tile's weight slabs go to L2 now, so that DRAM
-      // keeps streaming this kernel's weights while the previous kernel
-      // finishes; after the dependency wait they come from L2.
-      if (parity == 0) {
-        const int kb_rest = kb_begin + pre_limit * S;
-        const uint8_t* rest = p.p_packed + ((size_t)ti0 * p.num_kb + kb_rest) * (size_t)(kBM * kSlab);
-        for (int kb = kb_rest; kb < kb_end; kb += 4)
-          bulk_prefetch_l2(rest + (size_t)(kb - kb_rest) * (kBM * kSlab), (uint32_t)min(4, kb_end - kb) * kBM * kSlab);
-      }
       for (int st = parity; st < pre_limit; st += 2) {
         const int kb = kb_begin + st * S;
         const int nsl = min(S, kb_end - kb);

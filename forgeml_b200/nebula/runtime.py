@@ -42,6 +42,7 @@ from forgeml_b200.nebula import ops
 from forgeml_b200.nebula.cache import CacheError, KVCache
 from forgeml_b200.nebula.model import DecoderConfig, TinyDecoder
 from forgeml_b200.nebula.parallel import ParallelContext
+from forgeml_b200.nebula import peer
 
 CMD_STOP = 0
 CMD_STEP = 1
@@ -215,6 +216,14 @@ class ShardedDecoder(nn.Module):
         self._hl_hd = hl_hd
         self._graphs: dict[int, dict] = {}
         self.use_cuda_graphs = True
+        # Decode-step TP reductions (B x 1 x d per call) go through the NVLink
+        # peer all-reduce fused with the residual add; collective over the TP
+        # group, so every rank builds it here in the same order.
+        self._peer_ar = None
+        if context.tp_size > 1 and dev.type == "cuda" and peer.enabled():
+            es = torch.empty((), dtype=dtype).element_size()
+            slot = max(16, (max_requests * h * es + 15) // 16 * 16)
+            self._peer_ar = peer.PeerAllReduce(context, max_bytes=slot)
 
     # ------------------------------------------------------------------ math
     def _layer(self, L: _Layer, lid: int, x: torch.Tensor, b: int, t: int, slots: torch.Tensor,
@@ -235,18 +244,22 @@ class ShardedDecoder(nn.Module):
         if ctx.tp_size == 1:
             x = L.o(attn, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x)
         else:
-            part = L.o(attn, torch.empty((bt, h), dtype=self.dtype, device=dev))
-            ctx.all_reduce(part)
-            x = ops.add(x, part)
+            x = self._tp_sum_add(L.o(attn, torch.empty((bt, h), dtype=self.dtype, device=dev)), x)
         h2 = _ln(x, L.ln2_w, L.ln2_b, torch.empty_like(x), bt)
         mid = L.up(h2, torch.empty((bt, L.wup.shape[0]), dtype=self.dtype, device=dev), act=_native.ACT_GELU_TANH)
         if ctx.tp_size == 1:
             x = L.down(mid, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x)
         else:
-            part = L.down(mid, torch.empty((bt, h), dtype=self.dtype, device=dev))
-            ctx.all_reduce(part)
-            x = ops.add(x, part)
+            x = self._tp_sum_add(L.down(mid, torch.empty((bt, h), dtype=self.dtype, device=dev)), x)
         return x
+
+    def _tp_sum_add(self, part: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+        """x + SUM-all-reduce(part) over the TP group (reference runtime.py:146,154)."""
+        if self._peer_ar is not None and self._peer_ar.fits(part) and x.is_contiguous():
+            with record_function("nebula::tp_all_reduce_add"):
+                return self._peer_ar(part, x, torch.empty_like(x))
+        self.context.all_reduce(part)
+        return ops.add(x, part)
 
     def _core(self, tokens: torch.Tensor, slots: torch.Tensor, starts: torch.Tensor, b: int, t: int,
               last_only: bool) -> torch.Tensor:
@@ -300,7 +313,12 @@ class ShardedDecoder(nn.Module):
         tt = 1 if last_only else t
         if logits is None:
             logits = torch.empty((b * tt, v), dtype=self.dtype, device=ctx.device)
-        if ctx.world_size > 1:
+        if ctx.pp_size > 1:
+            # Only the last pipeline stage computes logits.  (With tensor
+            # parallelism alone every rank already holds the same logits: the
+            # TP reductions give bit-identical results on all ranks and the
+            # lm_head runs on identical inputs, so the reference's broadcast
+            # (runtime.py:188) would copy equal values.)
             dist.broadcast(logits, src=(ctx.pp_size - 1) * ctx.tp_size)
         self.cache.advance(request_ids, start_pos + t)
         return logits.view(b, tt, v)
@@ -349,6 +367,13 @@ class ShardedDecoder(nn.Module):
 
     def release_graphs(self) -> None:
         self._graphs.clear()
+
+    def close(self) -> None:
+        """Release the captured graphs and the peer all-reduce buffers."""
+        self.release_graphs()
+        if self._peer_ar is not None:
+            self._peer_ar.close()
+            self._peer_ar = None
 
 
 def _validate_prompt(config: DecoderConfig, prompt: list[int], max_new: int) -> None:
@@ -631,7 +656,9 @@ class Engine:
                     with contextlib.suppress(Exception):
                         self._bcast(header)
                 self.decoder.cache.clear()
-                if hasattr(self.decoder, "release_graphs"):
+                if hasattr(self.decoder, "close"):
+                    self.decoder.close()
+                elif hasattr(self.decoder, "release_graphs"):
                     self.decoder.release_graphs()
                 self._healthy = False
             finally:

@@ -11,7 +11,9 @@
  *     launched when validation fails.  No entry point falls back to another
  *     implementation: an unsupported layout is an error.
  *   - Kernels never allocate.  Entry points that need scratch take a
- *     caller-owned workspace and have a *_workspace_size() query.
+ *     caller-owned workspace and have a *_workspace_size() query; the one
+ *     exception is neb_ar_create, which allocates the all-reduce context's
+ *     symmetric buffer once (freed by neb_ar_destroy).
  *   - dtype codes: FML_F32, FML_F16, FML_BF16.
  */
 #ifndef FORGEML_B200_H
@@ -48,7 +50,7 @@ enum { FML_ACT_NONE = 0, FML_ACT_GELU_ERF = 1, FML_ACT_GELU_TANH = 2 };
  * block_k the K elements carried per pipeline stage (one, two or four 128-byte
  * slabs; 16-bit inputs only).  NULL
  * means "choose by heuristic".  block_m, block_k and num_warps are fixed by the
- * tcgen05 design (128-row UMMA tiles, 128-byte K slabs, 6 warps) and are only
+ * tcgen05 design (128-row UMMA tiles, 128-byte K slabs, 9 warps) and are only
  * range-checked. */
 typedef struct fml_tile_cfg {
   int32_t block_m, block_n, block_k, num_warps, num_stages;
@@ -223,6 +225,34 @@ FML_API int neb_add(const void* a, const void* b, void* y, int64_t n, int dtype,
             void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Tensor-parallel SUM all-reduce over NVLink peer memory, fused with the
+ * residual add.  Replaces ParallelContext.all_reduce
+ * (src/nebula/parallel.py:112-116) followed by `x = x + part`
+ * (src/nebula/runtime.py:146,154):  out = round(round(sum_r part_r) + residual)
+ * with the sum taken in rank order (bit-identical on every rank).  Each rank
+ * creates a context (a symmetric buffer of 2 x world slots of max_bytes),
+ * exchanges the IPC handles with its TP group, opens the peers' buffers, then
+ * every rank calls neb_ar_all_reduce with the same sizes in the same order
+ * (stream-ordered, CUDA-graph capturable).  A wait that exceeds timeout_ms
+ * raises bit 32 of fml_device_status() instead of hanging.
+ * ------------------------------------------------------------------------- */
+/* Bytes of one IPC handle (cudaIpcMemHandle_t). */
+FML_API int64_t neb_ar_handle_bytes(void);
+FML_API int neb_ar_create(int64_t max_bytes, int world, int rank, double timeout_ms, void** ctx_out,
+                          void* handle_out);
+/* handles: world consecutive handles in rank order (this rank's is ignored). */
+FML_API int neb_ar_open(void* ctx, const void* handles);
+/* Single-process alternative to neb_ar_open: device pointers of every rank's
+ * buffer (neb_ar_buffer of the other contexts); this rank's entry ignored. */
+FML_API int neb_ar_set_peers(void* ctx, void* const* bases);
+FML_API void* neb_ar_buffer(void* ctx);
+/* n elements of dtype; residual may be NULL (then out = round(sum)); 16-byte
+ * aligned pointers, n * sizeof(dtype) a multiple of 16 and <= max_bytes. */
+FML_API int neb_ar_all_reduce(void* ctx, const void* part, const void* residual, void* out, int64_t n,
+                              int dtype, void* stream);
+FML_API int neb_ar_destroy(void* ctx);
+
+/* ---------------------------------------------------------------------------
  * Diagnostics.
  * ------------------------------------------------------------------------- */
 /* Message for the last nonzero return on this thread ("" if none). */
@@ -231,7 +261,7 @@ FML_API const char* fml_last_error(void);
  * (bounded waits that expired, out-of-range token ids).  0 = clean.
  * Bits: 1 GEMM pipeline wait expired, 2 token id out of range, 4 attention
  * position/slot out of range, 8 split-K cluster reduce wait expired,
- * 16 attention copy-pipeline wait expired.
+ * 16 attention copy-pipeline wait expired, 32 all-reduce peer wait expired.
  * Synchronizes the current device. */
 FML_API int fml_device_status(void);
 /* Number of kernel launches issued by this library in this process. */

@@ -107,3 +107,93 @@ def test_tp2_pp2_bf16():
 
 def test_tp8_bf16():
     _run(8, 8, 1, "bfloat16")
+
+
+def _ar_worker(rank, world, store, dtype_name):
+    import os
+
+    from forgeml_b200.nebula import ParallelContext
+    from forgeml_b200.nebula.peer import PeerAllReduce
+
+    os.environ["LOCAL_RANK"] = str(rank)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"file://{store}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    ctx = ParallelContext.from_env(tp_size=world, pp_size=1, device="cuda", timeout_s=60)
+    dtype = getattr(torch, dtype_name)
+    dev = ctx.device
+    ar = PeerAllReduce(ctx, max_bytes=1 << 20)
+    try:
+        for it, n in enumerate((2048 * 32, 8, 4096, 2048 * 32)):
+            g = torch.Generator().manual_seed(1000 * it + rank)
+            part = torch.randn(n, generator=g).to(dtype)
+            res = torch.randn(n, generator=torch.Generator().manual_seed(77 + it)).to(dtype)  # same on all ranks
+            parts = [torch.empty_like(part) for _ in range(world)]
+            dist.all_gather_object(parts, part)
+            acc = torch.zeros(n, dtype=torch.float32)
+            for p in parts:  # rank order, fp32
+                acc += p.float()
+            want = (acc.to(dtype).float() + res.float()).to(dtype)
+            out = torch.empty(n, dtype=dtype, device=dev)
+            ar(part.to(dev), res.to(dev), out)
+            assert torch.equal(out.cpu(), want), f"rank {rank} iteration {it}"
+            want_plain = acc.to(dtype)
+            ar(part.to(dev), None, out)
+            assert torch.equal(out.cpu(), want_plain)
+        # replay inside a CUDA graph: epochs advance on the device
+        part = torch.full((4096,), float(rank + 1), dtype=dtype, device=dev)
+        res = torch.ones(4096, dtype=dtype, device=dev)
+        out = torch.empty_like(part)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            ar(part, res, out)
+        torch.cuda.current_stream().wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            ar(part, res, out)
+        for _ in range(5):
+            out.zero_()
+            graph.replay()
+            torch.cuda.synchronize()
+            assert torch.all(out.float() == 1 + world * (world + 1) / 2)
+        del graph
+        from forgeml_b200 import _native
+        assert _native.device_status() == 0
+    finally:
+        ar.close()
+        torch.cuda.synchronize()
+        dist.barrier()
+        ctx.close()
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _run_ar(world, dtype_name):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    with tempfile.TemporaryDirectory() as d:
+        procs = mp.start_processes(_ar_worker, args=(world, f"{d}/store", dtype_name), nprocs=world,
+                                   join=False, start_method="spawn")
+        deadline = time.time() + 180
+        while time.time() < deadline and not all(p.exitcode is not None for p in procs.processes):
+            time.sleep(0.2)
+        for p in procs.processes:
+            if p.is_alive():
+                p.terminate()
+        for p in procs.processes:
+            p.join()
+        assert [p.exitcode for p in procs.processes] == [0] * world
+
+
+def test_peer_all_reduce_2_bf16():
+    _run_ar(2, "bfloat16")
+
+
+def test_peer_all_reduce_2_fp32():
+    _run_ar(2, "float32")
+
+
+def test_peer_all_reduce_8_bf16():
+    _run_ar(8, "bfloat16")
