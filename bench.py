@@ -266,7 +266,7 @@ def gemm_headline(dev) -> dict:
 #   attention: ncu --set full -k regex:neb_attn -s 3 -c 1 ... bench.py --case attention --steps 20
 #   gemm:      ncu --set full -k regex:gemm_kernel ... bench.py --case gemm-decode --steps 20 (down projection)
 # Traffic in the JSON line is this ratio times the launch's algorithmic bytes.
-TRAFFIC_RATIO = {"attention": None, "gemm": None}
+TRAFFIC_RATIO = {"attention": (268.618240e6 + 4.372736e6) / 268697600, "gemm": (34.288384e6 + 1.28e3) / 34340864}
 
 
 def _graph_time_us(fns, reps: int = 5) -> float:
