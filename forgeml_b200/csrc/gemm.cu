@@ -97,6 +97,10 @@ __device__ __forceinline__ uint32_t bar_tempty(const Smem& s, int a) {
 __device__ __forceinline__ uint32_t bar_recv(const Smem& s) {
   return s.bars + 8 * (2 * kMaxStages + 4);
 }
+// CTA pair: each CTA tells the other it is done with TMEM before either frees it.
+__device__ __forceinline__ uint32_t bar_dealloc(const Smem& s) {
+  return s.bars + 8 * (2 * kMaxStages + 5);
+}
 __device__ __forceinline__ uint32_t bar_drain(const Smem& s) {
   return s.bars + 8 * (2 * kMaxStages + 6);
 }
@@ -242,7 +246,10 @@ __device__ __forceinline__ bool epilogue_row32_fast(const Params& p, int m, int 
 
 // Narrow tiles are register-bounded for two CTAs per SM (the decode weight
 // stream, ~100 KB of shared memory each).
-template <int BN, bool PROMOTE>
+// PAIR: a CTA pair (cluster of 2) computes 256 x BN tiles with cta_group::2
+// UMMAs; each CTA loads its 128 rows of P and BN/2 rows of Q (16-bit,
+// non-split only).
+template <int BN, bool PROMOTE, bool PAIR = false>
 __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
                 const Params p) {
@@ -254,18 +261,25 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
   s.stage_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const int S = p.slabs;
   s.p_bytes = S * kBM * kSlab;
-  s.stage_bytes = S * (kBM + BN) * kSlab;
+  constexpr int kQRows = PAIR ? BN / 2 : BN;  // Q rows this CTA loads per tile
+  constexpr int kTileM = PAIR ? 2 * kBM : kBM;  // output rows per tile
+  s.stage_bytes = S * (kBM + kQRows) * kSlab;
   s.bars = s.stage_base + p.stages * s.stage_bytes;
   s.red = s.bars + kBarBytes;
   s.red = (s.red + 15u) & ~15u;
   const uint32_t tmem_holder = s.bars + 8 * kNumBars;
 
-  const int ksplit = p.ksplit;
-  const uint32_t crank = ksplit > 1 ? cluster_ctarank() : 0u;
-  const int cluster_id = blockIdx.x / ksplit;
-  const int num_clusters = gridDim.x / ksplit;
-  const int kb_begin = (int)((long long)crank * p.num_kb / ksplit);
-  const int kb_end = (int)((long long)(crank + 1) * p.num_kb / ksplit);
+  const int ksplit = PAIR ? 1 : p.ksplit;
+  constexpr bool kClusterLaunch = true;  // (ksplit > 1 or PAIR) -> launched as clusters
+  const int csize = PAIR ? 2 : ksplit;
+  const uint32_t crank = csize > 1 ? cluster_ctarank() : 0u;
+  const bool leader = !PAIR || crank == 0;
+  const int prank = PAIR ? (int)crank : 0;  // this CTA's half of a pair tile
+  const int cluster_id = blockIdx.x / csize;
+  const int num_clusters = gridDim.x / csize;
+  const int kb_begin = PAIR ? 0 : (int)((long long)crank * p.num_kb / ksplit);
+  const int kb_end = PAIR ? p.num_kb : (int)((long long)(crank + 1) * p.num_kb / ksplit);
+  (void)kClusterLaunch;
 
   constexpr int kAccStride = BN < 32 ? 32 : BN;
   constexpr int kTmemCols = (2 * kAccStride <= 32) ? 32
@@ -280,21 +294,27 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(bar_tfull(s, a), 1);
-      mbar_init(bar_tempty(s, a), 4);
+      mbar_init(bar_tempty(s, a), PAIR ? 8 : 4);  // a pair's leader hears both CTAs' epilogues
     }
     mbar_init(bar_recv(s), 1);
+    mbar_init(bar_dealloc(s), 1);
     mbar_init(bar_drain(s), 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmP);
     tma_prefetch_desc(&tmQ);
   }
   if (warp == kMmaWarp) {
-    tmem_alloc(tmem_holder, kTmemCols);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(tmem_holder, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_holder, kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
-  if (ksplit > 1) cluster_sync_all();
+  if (csize > 1) cluster_sync_all();
   tc_fence_after();
   uint32_t tmem_base;
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(tmem_base) : "r"(tmem_holder) : "memory");
@@ -318,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
     const int parity = pw & 1;
     const CUtensorMap* tm = is_q ? &tmQ : &tmP;
     const int mn = is_q ? p.q_mn : p.p_mn;
-    const int rows = is_q ? BN : kBM;
+    const int rows = is_q ? kQRows : kBM;
     const uint32_t op_off = is_q ? s.p_bytes : 0u;
     const uint32_t slab_bytes = (uint32_t)rows * kSlab;
     const bool packed = !is_q && p.p_packed != nullptr;
@@ -352,15 +372,17 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
     for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
       int ti, tj;
       tile_coords(p, t, ti, tj);
-      const int rbase = is_q ? tj * BN : ti * kBM;
+      const int rbase = is_q ? tj * BN + prank * kQRows : ti * kTileM + prank * kBM;
       for (int kb = kb_begin; kb < kb_end; kb += S, ++step) {
         if ((step & 1) == parity && step >= pre_limit) {
           const int nsl = min(S, kb_end - kb);
-          const uint32_t fb = bar_full(s, stage);
+          // A pair's copies all complete on the leader's full barrier, which
+          // the leader's producer arms with both CTAs' bytes.
+          const uint32_t fb = PAIR ? mapa(bar_full(s, stage), 0) : bar_full(s, stage);
           bool got = true;
           if (lane == 0) {
             got = mbar_wait(bar_empty(s, stage), phase ^ 1u, DEV_ERR_GEMM_TIMEOUT);
-            if (got) mbar_arrive_expect_tx(fb, (uint32_t)nsl * slab_bytes);
+            if (got && leader) mbar_arrive_expect_tx(bar_full(s, stage), (uint32_t)nsl * slab_bytes * (PAIR ? 2u : 1u));
           }
           if (!__shfl_sync(0xffffffffu, got ? 1 : 0, 0)) { ok = false; break; }
           const uint32_t dst0 = s.stage_base + stage * s.stage_bytes + op_off;
@@ -372,8 +394,10 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
           } else if (lane < nsl * nbox) {
             const int sl = lane / nbox, b = lane % nbox;
             const uint32_t dst = dst0 + sl * slab_bytes + b * slab_box_bytes;
-            if (!mn) tma_load_2d(tm, fb, dst, (kb + sl) * bke, rbase);
-            else tma_load_2d(tm, fb, dst, rbase + b * mn_box, (kb + sl) * bke);
+            const int x = mn ? rbase + b * mn_box : (kb + sl) * bke;
+            const int y = mn ? (kb + sl) * bke : rbase;
+            if (PAIR) tma_load_2d_pair(tm, fb, dst, x, y);
+            else tma_load_2d(tm, fb, dst, x, y);
           }
           __syncwarp();
           issued_mask |= 1u << stage;
@@ -393,8 +417,8 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
     // ------------------------------------------------------------ UMMA issuer
     pdl_wait();
     pdl_trigger();
-    if (lane == 0) {
-      const uint32_t idesc = umma_idesc(p.fmt, p.p_mn, p.q_mn, BN);
+    if (lane == 0 && leader) {
+      const uint32_t idesc = umma_idesc(p.fmt, p.p_mn, p.q_mn, BN, PAIR ? 256 : 128);
       const uint32_t p_lbo = p.p_mn ? slab_box_bytes : 16u;
       const uint32_t q_lbo = p.q_mn ? slab_box_bytes : 16u;
       // Descriptors of stage 0 / slab 0 / K step 0; everything else is a
@@ -404,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
       const uint64_t dp0 = umma_desc_sw128(s.stage_base, p_lbo, 1024u);
       const uint64_t dq0 = umma_desc_sw128(s.stage_base + s.p_bytes, q_lbo, 1024u);
       const uint32_t d_stage = s.stage_bytes >> 4;
-      const uint32_t dp_slab = (kBM * kSlab) >> 4, dq_slab = (BN * kSlab) >> 4;
+      const uint32_t dp_slab = (kBM * kSlab) >> 4, dq_slab = (kQRows * kSlab) >> 4;
       const uint32_t dp_k = (p.p_mn ? (uint32_t)(32 / p.esize) * kSlab : 32u) >> 4;
       const uint32_t dq_k = (p.q_mn ? (uint32_t)(32 / p.esize) * kSlab : 32u) >> 4;
       const bool tf32 = p.fmt == 2;
@@ -432,7 +456,10 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
             const uint64_t dp = dp0 + stage * d_stage, dq = dq0 + stage * d_stage;
             for (int sl = 0; sl < nsl; ++sl) {
               const uint64_t ap = dp + sl * dp_slab, bq = dq + sl * dq_slab;
-              if (tf32) {
+              if (PAIR) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) { umma_f16_pair(d_tmem, ap + k * dp_k, bq + k * dq_k, idesc, accum); accum = 1u; }
+              } else if (tf32) {
 #pragma unroll
                 for (int k = 0; k < 4; ++k) { umma_tf32(d_tmem, ap + k * dp_k, bq + k * dq_k, idesc, accum); accum = 1u; }
               } else {
@@ -440,16 +467,27 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
                 for (int k = 0; k < 4; ++k) { umma_f16(d_tmem, ap + k * dp_k, bq + k * dq_k, idesc, accum); accum = 1u; }
               }
             }
-            umma_commit(bar_empty(s, stage));
+            if (PAIR) {
+              umma_commit_pair(bar_empty(s, stage));
+              umma_commit_pair(mapa(bar_empty(s, stage), 1));
+            } else {
+              umma_commit(bar_empty(s, stage));
+            }
             if (++stage == p.stages) { stage = 0; phase ^= 1u; }
           }
           if (!ok) break;
-          umma_commit(bar_tfull(s, acc));
+          if (PAIR) {
+            umma_commit_pair(bar_tfull(s, acc));
+            umma_commit_pair(mapa(bar_tfull(s, acc), 1));
+          } else {
+            umma_commit(bar_tfull(s, acc));
+          }
           if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
         }
       }
       // Drain: every UMMA issued above has completed before TMEM is freed.
-      umma_commit(bar_drain(s));
+      if (PAIR) umma_commit_pair(bar_drain(s));
+      else umma_commit(bar_drain(s));
       mbar_wait(bar_drain(s), 0, DEV_ERR_GEMM_TIMEOUT);
     }
     __syncwarp();
@@ -482,7 +520,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
     for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
       int ti, tj;
       tile_coords(p, t, ti, tj);
-      const int i = ti * kBM + row;
+      const int i = ti * kTileM + prank * kBM + row;
       if (ksplit > 1 && ep_tid == 0)
         mbar_arrive_expect_tx(bar_recv(s), (uint32_t)((ksplit - 1) * rows_per * BN * 4));
       float racc[PROMOTE ? BN : 1];
@@ -504,7 +542,10 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
           }
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar_tempty(s, acc));
+          if (lane == 0) {
+            if (PAIR && !leader) mbar_arrive_remote(mapa(bar_tempty(s, acc), 0));
+            else mbar_arrive(bar_tempty(s, acc));
+          }
         } else {
 #pragma unroll 1
           for (int c = 0; c < kChunks; ++c) {
@@ -513,7 +554,10 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
             if (c == kChunks - 1) {
               tc_fence_before();
               __syncwarp();
-              if (lane == 0) mbar_arrive(bar_tempty(s, acc));
+              if (lane == 0) {
+            if (PAIR && !leader) mbar_arrive_remote(mapa(bar_tempty(s, acc), 0));
+            else mbar_arrive(bar_tempty(s, acc));
+          }
             }
             const int nvalid = min(32, BN - c * 32);
             if (ksplit == 1) {
@@ -570,7 +614,23 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
   __syncthreads();
   if (warp == kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    if (PAIR) {
+      // Both CTAs are done with the pair's TMEM before either frees it.
+      if (lane == 0) {
+        const uint32_t peer = crank ^ 1u;
+        if (leader) {
+          mbar_wait_cluster(bar_dealloc(s), 0, DEV_ERR_GEMM_TIMEOUT);
+          mbar_arrive_remote(mapa(bar_dealloc(s), peer));
+        } else {
+          mbar_arrive_remote(mapa(bar_dealloc(s), peer));
+          mbar_wait_cluster(bar_dealloc(s), 0, DEV_ERR_GEMM_TIMEOUT);
+        }
+      }
+      __syncwarp();
+      tmem_dealloc_pair(tmem_base, kTmemCols);
+    } else {
+      tmem_dealloc(tmem_base, kTmemCols);
+    }
   }
 }
 
@@ -760,6 +820,7 @@ static int encode(CUtensorMap* map, const void* ptr, int dtype, bool tf32, bool 
 }
 
 struct Plan {
+  bool pair = false;  // CTA-pair (cta_group::2) 256 x 256 tiles
   bool swap;
   bool promote;  // fp32: sum TMEM partials in fp32 registers every kPromoteKb slabs
   bool packed;   // P is a pre-packed constant weight (fml_linear_packed)
@@ -774,8 +835,8 @@ struct Plan {
 
 static const int kBNs[] = {16, 32, 64, 128, 256};
 
-static int smem_bytes_for(int bn, int stages, int ksplit, int* red_stride, int slabs = 1) {
-  int stage_bytes = slabs * (kBM + bn) * kSlab;
+static int smem_bytes_for(int bn, int stages, int ksplit, int* red_stride, int slabs = 1, bool pair = false) {
+  int stage_bytes = slabs * (kBM + (pair ? bn / 2 : bn)) * kSlab;
   int rs = bn + 4;
   if (red_stride) *red_stride = rs;
   int red = ksplit > 1 ? kBM * rs * 4 + 16 : 0;
@@ -863,10 +924,12 @@ static int resident_ctas(int bn, bool promote, int ksplit, int smem, int sms) {
 // weight stream defaults to four one-slab stages, which keeps the CTA near
 // 100 KB of shared memory so that the next kernel's CTAs are resident beside
 // it and prefetch their weights during programmatic dependent launch.
-static int stages_for(int bn, int ksplit, const fml_tile_cfg* cfg, int slabs, bool packed = false) {
+static int stages_for(int bn, int ksplit, const fml_tile_cfg* cfg, int slabs, bool packed = false, bool pair = false) {
   int stages = packed ? 4 : kMaxStages;
-  if (cfg && cfg->num_stages > 0) stages = std::min(cfg->num_stages, kMaxStages);
-  while (stages > 2 && smem_bytes_for(bn, stages, ksplit, nullptr, slabs) > kSmemLimit) --stages;
+  // The stage hint applies to single-CTA tiles; a CTA pair always takes the
+  // deepest ring that fits (its stages are a third smaller).
+  if (cfg && cfg->num_stages > 0 && !pair) stages = std::min(cfg->num_stages, kMaxStages);
+  while (stages > 2 && smem_bytes_for(bn, stages, ksplit, nullptr, slabs, pair) > kSmemLimit) --stages;
   return stages;
 }
 
@@ -968,20 +1031,34 @@ static int make_plan(Plan& pl, const void* a, long long lda_m, long long lda_k, 
   const long long tiles = ((I + kBM - 1) / kBM) * ((J + pl.bn - 1) / pl.bn);
   const long long num_kb = (pl.keff * es + kSlab - 1) / kSlab;
   pl.slabs = slabs_for(cfg, dtype, pl.promote, pl.bn);
-  choose_split(pl, tiles, num_kb, cfg, sms);
-  if (smem_bytes_for(pl.bn, pl.stages, pl.ksplit, nullptr, pl.slabs) > kSmemLimit)
+  // Large 16-bit tiles run as CTA pairs (256 x 256 per pair, each CTA
+  // loading half of Q) when there are enough pair tiles to fill the GPU.
+  {
+    const char* e = getenv("FORGEML_GEMM_PAIR");  // diagnostic switch, default on
+    const bool allow = !(e && e[0] == '0');
+    const long long pair_tiles = ((I + 2 * kBM - 1) / (2 * kBM)) * ((J + 255) / 256);
+    pl.pair = allow && !pl.swap && !pl.promote && dtype != FML_F32 && pl.bn == 256 && I >= 2 * kBM &&
+              pair_tiles * 2 >= sms && pl.slabs == 1;
+  }
+  if (pl.pair) {
+    pl.ksplit = 1;
+    pl.stages = stages_for(pl.bn, 1, cfg, pl.slabs, false, true);
+  } else {
+    choose_split(pl, tiles, num_kb, cfg, sms);
+  }
+  if (smem_bytes_for(pl.bn, pl.stages, pl.ksplit, nullptr, pl.slabs, pl.pair) > kSmemLimit)
     return fail(FML_EUNSUPPORTED, "gemm tile does not fit in shared memory");
   return FML_OK;
 }
 
-template <int BN, bool PROMOTE>
+template <int BN, bool PROMOTE, bool PAIR = false>
 static int launch_bn(const CUtensorMap& mp, const CUtensorMap& mq, const Params& prm, int grid,
                      int smem, cudaStream_t st) {
   static std::once_flag once[64];
   const int dev = current_device();
   cudaError_t e = cudaSuccess;
   std::call_once(once[dev & 63], [&]() {
-    e = cudaFuncSetAttribute(gemm_kernel<BN, PROMOTE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(gemm_kernel<BN, PROMOTE, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemLimit);
   });
   if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(gemm)");
@@ -995,16 +1072,16 @@ static int launch_bn(const CUtensorMap& mp, const CUtensorMap& mq, const Params&
   attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[na].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   ++na;
-  if (prm.ksplit > 1) {
+  if (prm.ksplit > 1 || PAIR) {
     attr[na].id = cudaLaunchAttributeClusterDimension;
-    attr[na].val.clusterDim.x = prm.ksplit;
+    attr[na].val.clusterDim.x = PAIR ? 2 : prm.ksplit;
     attr[na].val.clusterDim.y = 1;
     attr[na].val.clusterDim.z = 1;
     ++na;
   }
   lc.attrs = attr;
   lc.numAttrs = na;
-  e = cudaLaunchKernelEx(&lc, gemm_kernel<BN, PROMOTE>, mp, mq, prm);
+  e = cudaLaunchKernelEx(&lc, gemm_kernel<BN, PROMOTE, PAIR>, mp, mq, prm);
   if (e != cudaSuccess) return check_cuda(e, "gemm launch");
   count_launch();
   return FML_OK;
@@ -1021,10 +1098,16 @@ static int launch_plan(const Plan& pl, const CUtensorMap& mp, const CUtensorMap&
   const long long es = (long long)dtype_size(dtype);
   prm.num_kb = (int)((pl.keff * es + kSlab - 1) / kSlab);
   prm.slabs = pl.slabs;
-  prm.tiles_i = (int)((prm.I + kBM - 1) / kBM);
+  prm.tiles_i = (int)((prm.I + (pl.pair ? 2 : 1) * kBM - 1) / ((pl.pair ? 2 : 1) * kBM));
   prm.tiles_j = (int)((prm.J + pl.bn - 1) / pl.bn);
   prm.num_tiles = prm.tiles_i * prm.tiles_j;
-  prm.group_i = std::min(prm.tiles_i, 16);
+  // Tile raster: groups of group_i tile rows advance along N together
+  // (measured on B200: 8 for CTA pairs, 16 for single CTAs).
+  prm.group_i = std::min(prm.tiles_i, pl.pair ? 8 : 16);
+  if (const char* g = getenv("FORGEML_GEMM_GROUP")) {  // tuning override: tile-raster group height
+    const int v = atoi(g);
+    if (v > 0) prm.group_i = std::min(prm.tiles_i, v);
+  }
   prm.ksplit = pl.ksplit;
   prm.fmt = dtype == FML_F32 ? 2 : dtype == FML_BF16 ? 1 : 0;
   prm.p_mn = (pl.P.pack || pl.packed) ? 0 : (pl.P.mn ? 1 : 0);
@@ -1044,7 +1127,7 @@ static int launch_plan(const Plan& pl, const CUtensorMap& mp, const CUtensorMap&
   prm.cols_out = (int)n;
   prm.p_packed = p_packed;
   int red_stride = 0;
-  const int smem = smem_bytes_for(pl.bn, pl.stages, pl.ksplit, &red_stride, pl.slabs);
+  const int smem = smem_bytes_for(pl.bn, pl.stages, pl.ksplit, &red_stride, pl.slabs, pl.pair);
   prm.red_stride = red_stride;
   prm.promote_kb = kPromoteKb;
   // Persistent grid (as many CTAs as are co-resident) without split-K; with
@@ -1052,7 +1135,10 @@ static int launch_plan(const Plan& pl, const CUtensorMap& mp, const CUtensorMap&
   // buffer once).
   const long long want = (long long)prm.num_tiles * prm.ksplit;
   int grid;
-  if (prm.ksplit > 1) {
+  if (pl.pair) {
+    // one CTA per SM (the ring fills shared memory), whole pairs
+    grid = (int)std::min<long long>((long long)prm.num_tiles * 2, (long long)(sms / 2) * 2);
+  } else if (prm.ksplit > 1) {
     if (want > 0x7fffffffLL) return fail(FML_EUNSUPPORTED, "gemm: too many split-K tiles");
     grid = (int)want;
   } else {
@@ -1065,6 +1151,7 @@ static int launch_plan(const Plan& pl, const CUtensorMap& mp, const CUtensorMap&
     fprintf(stderr, "[fml_gemm] I=%d J=%d num_kb=%d bn=%d swap=%d packed=%d ksplit=%d slabs=%d stages=%d smem=%d grid=%d resident=%d\n",
             prm.I, prm.J, prm.num_kb, pl.bn, prm.swap, pl.packed ? 1 : 0, pl.ksplit, pl.slabs, pl.stages, smem, grid, res);
   }
+  if (pl.pair) return launch_bn<256, false, true>(mp, mq, prm, grid, smem, st);
   if (pl.promote) {
     switch (pl.bn) {
       case 16: return launch_bn<16, true>(mp, mq, prm, grid, smem, st);
@@ -1173,7 +1260,7 @@ extern "C" int fml_gemm(const void* a, int64_t lda_m, int64_t lda_k, const void*
   for (int w = 0; w < 2; ++w) {
     Operand& o = w == 0 ? pl.P : pl.Q;
     CUtensorMap* map = w == 0 ? &mp : &mq;
-    const int box_rows = w == 0 ? kBM : pl.bn;
+    const int box_rows = w == 0 ? kBM : (pl.pair ? pl.bn / 2 : pl.bn);
     if (o.pack) {
       const void* ptr = static_cast<uint8_t*>(workspace) + o.ws_off;
       rc = encode(map, ptr, dtype, tf32, false, o.rows, pl.keff, tf32 ? 3 * o.kp : o.kp,
