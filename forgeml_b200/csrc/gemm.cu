@@ -4,16 +4,22 @@
 // (src/forgeml/_triton.py:6-62, launched by :65-93) and the cuBLAS F.linear
 // calls of Nebula (src/nebula/runtime.py:131-133,145,152-153,186).
 //
-// Design (one persistent kernel, warp-specialised, 192 threads):
-//   warp 0      TMA producer: 2-D tiled loads of 128-byte K slabs of both
-//               operands into a ring of shared-memory stages (SWIZZLE_128B).
-//   warp 1      TMEM allocator + single-thread UMMA issuer
-//               (tcgen05.mma.cta_group::1, M=128, N=BN, fp32 accumulate in
-//               TMEM, two accumulator buffers so the epilogue of tile t
-//               overlaps the main loop of tile t+1).
-//   warps 2..5  epilogue: tcgen05.ld the accumulator, apply the reference's
-//               rounding contract (round to output dtype, + bias, round,
-//               GELU in fp32), optional residual add, store.
+// Design (one persistent kernel, warp-specialised, 288 threads):
+//   warps 5..8  TMA producers (P or Q operand x even or odd pipeline step):
+//               2-D tiled loads of 128-byte K slabs into a ring of shared-
+//               memory stages (SWIZZLE_128B), or one bulk copy per stage of
+//               a pre-packed weight.  A stage's copies go out in one
+//               instruction across lanes: a warp's copies otherwise complete
+//               one after another.
+//   warp 4      TMEM allocator + single-thread UMMA issuer
+//               (tcgen05.mma, M=128 or a CTA pair's 256, N=BN, fp32
+//               accumulate in TMEM, two accumulator buffers so the epilogue
+//               of tile t overlaps the main loop of tile t+1); descriptors
+//               are precomputed and stepped by constant offsets.
+//   warps 0..3  epilogue (TMEM lane quadrant = warp): tcgen05.ld the
+//               accumulator, apply the reference's rounding contract (round
+//               to output dtype, + bias, round, GELU in fp32), optional
+//               residual add, store.
 //
 // The kernel works in "MMA space": D[i][j] = sum_k P[i][k] * Q[j][k] where P
 // supplies the 128 TMEM lanes and Q the BN columns.  For ordinary shapes
@@ -24,8 +30,10 @@
 // (ForgeML) and [N,K] weights (Nebula) need no copies.
 //
 // Split-K: for few output tiles the K range is split across the CTAs of a
-// thread-block cluster; partial tiles are reduced through distributed shared
-// memory (no global scratch), each CTA reducing a slice of the rows.
+// thread-block cluster; each CTA pushes its partial rows to the row's owner
+// CTA with st.async into distributed shared memory (no global scratch, no
+// round trip).  Large 16-bit GEMMs run as CTA pairs (cta_group::2, 256-row
+// tiles, each CTA loading half of Q).
 #include <algorithm>
 #include <cstdio>
 #include <map>
