@@ -19,6 +19,8 @@ JSON line keys (one line on rank 0):
                CUDA-event time of that family's launches replayed from a graph;
                roofline_other the other family, roofline_step the whole step
   gemm         fused linear+GELU GEMM TFLOP/s at 8192^3 bf16 (N=1)
+  forgeml      configs 1-3 on the native kernels: compiled MLP and encoder
+               block, GEMM sweep (N=1)
   cpu_baseline the reference's own CPU implementation of the decode step (its
                Engine from baseline/_ref, fp32, all host cores; N=1), or the
                CPU oracle restatement when the reference is not installed
@@ -261,6 +263,94 @@ def gemm_headline(dev) -> dict:
             "peak_tflops": pk["bf16_tflops"], "frac": tf / pk["bf16_tflops"], "peak_source": pk["source"]}
 
 
+def forgeml_cases(dev) -> dict:
+    """ForgeML configs 1-3 on the native kernels (N=1, CUDA events, inputs
+    resident on the device):
+      c1  2-layer MLP, fp32 (3xTF32), compiled (fused_linear_gelu + linear)
+      c2  pre-LN encoder block, fp32 and bf16, compiled (24-node graph)
+      c3  GEMM + bias + GELU sweep: squares 256..8192 (bf16 and fp32) and
+          skinny M in {1, 16, 128} with N = K = 4096 (bf16, HBM-bound)."""
+    from forgeml_b200.forgeml import compile as fml_compile
+    from forgeml_b200.forgeml import kernels
+    from forgeml_b200.workloads import make_c1_mlp, make_c2_block, make_c3_operands
+
+    pk = _peaks()
+
+    def timed_ms(fn, reps):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    out = {}
+    with torch.inference_mode():
+        m, x = make_c1_mlp()
+        c = fml_compile(m.to(dev), (x.to(dev),), backend="triton")
+        xd = x.to(dev)
+        ms = timed_ms(lambda: c(xd), 50)
+        out["c1_mlp_fp32"] = {"us_per_call": ms * 1e3, "gflop": 0.268,
+                              "tflops": 0.268e9 / (ms * 1e-3) / 1e12}
+        for dt, name in ((torch.float32, "c2_block_fp32"), (torch.bfloat16, "c2_block_bf16")):
+            m, x = make_c2_block(dtype=dt)
+            m = m.to(dev, dt)
+            c = fml_compile(m, (x.to(dev),), backend="triton")
+            xd = x.to(dev)
+            ms = timed_ms(lambda: c(xd), 10)
+            out[name] = {"ms_per_call": ms, "gflop": 64.42, "tflops": 64.42e9 / (ms * 1e-3) / 1e12}
+        sweep = {}
+        for dt, dn in ((torch.bfloat16, "bf16"), (torch.float32, "fp32")):
+            for sz in (256, 1024, 4096, 8192):
+                a, b, bias = make_c3_operands(sz, sz, sz, dt, device=str(dev))
+                o = torch.empty(sz, sz, dtype=dt, device=dev)
+                ms = timed_ms(lambda: kernels.matmul(a, b, bias, activation="gelu", out=o), 5 if sz == 8192 else 20)
+                tf = 2 * sz ** 3 / (ms * 1e-3) / 1e12
+                sweep[f"{dn}_{sz}^3"] = {"ms": ms, "tflops": tf, "frac_of_bf16_peak": tf / pk["bf16_tflops"]}
+        for mm in (1, 16, 128):
+            a, b, bias = make_c3_operands(mm, 4096, 4096, torch.bfloat16, transposed_b=True, device=str(dev))
+            o = torch.empty(mm, 4096, dtype=torch.bfloat16, device=dev)
+            ms = timed_ms(lambda: kernels.matmul(a, b, bias, activation="gelu", out=o), 50)
+            nbytes = (4096 * 4096 + mm * 4096 * 2 + 4096) * 2
+            sweep[f"bf16_m{mm}_n4096_k4096"] = {"us": ms * 1e3, "GB/s": nbytes / (ms * 1e-3) / 1e9,
+                                                "frac_of_hbm": nbytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"]}
+        out["c3_sweep"] = sweep
+    out["reference_cpu"] = reference_forgeml_cpu()
+    return out
+
+
+def reference_forgeml_cpu() -> dict | None:
+    """The reference's own compiled forward on the host cores (its
+    `compile(..., backend="torch")` from baseline/_ref, fp32, all threads) for
+    configs 1 and 2: the CPU baseline beside the native numbers."""
+    ref_root = REPO / "baseline" / "_ref"
+    if not (ref_root / "forgeml").is_dir():
+        return None
+    from forgeml_b200.workloads import make_c1_mlp, make_c2_block
+
+    sys.path.insert(0, str(ref_root))
+    try:
+        import forgeml as ref_forgeml
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        res = {"cores": os.cpu_count() or 1, "kind": "reference"}
+        with torch.inference_mode():
+            for name, (m, x), reps in (("c1_mlp_fp32", make_c1_mlp(), 20), ("c2_block_fp32", make_c2_block(), 3)):
+                c = ref_forgeml.compile(m, (x,), backend="torch")
+                c(x)
+                t0 = time.perf_counter()
+                for _ in range(reps):
+                    c(x)
+                res[name + "_ms"] = (time.perf_counter() - t0) / reps * 1e3
+        return res
+    finally:
+        sys.path.remove(str(ref_root))
+
+
 # DRAM traffic per launch over the algorithmic bytes, from one ncu capture of
 # each kernel family (dram__bytes_read.sum + dram__bytes_write.sum):
 #   attention: ncu --set full -k regex:neb_attn -s 3 -c 1 ... bench.py --case attention --steps 20
@@ -488,6 +578,7 @@ def run_native(args) -> None:
             extra.update(kernel_rooflines(engine, dev, PROMPT + W + K, ms / K))
         if world == 1 and not args.no_gemm:
             extra["gemm"] = gemm_headline(dev)
+            extra["forgeml"] = forgeml_cases(dev)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = reference_decode(args.cpu_steps, 1, os.cpu_count() or 1, layers=args.cpu_layers)
@@ -515,6 +606,81 @@ def run_native(args) -> None:
         torch.cuda.synchronize(dev)
         dist.barrier()
         ctx.close()
+
+
+C5 = dict(vocab_size=32000, hidden_size=4096, num_heads=32, num_layers=32, intermediate_size=16384,
+          max_seq_len=4096, seed=4)
+
+
+def run_c5(args) -> None:
+    """Config 5: 32-layer d4096 decoder, TP x PP over the launched ranks (TP4 x
+    PP2 on 8 GPUs), served through the AsyncBatcher (batch cap 64).  Requests
+    arrive Poisson at 64 req/s with prompt lengths uniform in [128, 2048] and
+    uniform token ids (seeded); the sample is --c5-requests requests of
+    --c5-new tokens each (256 x 256 in the full workload).  Rank 0 drives the
+    batcher; the other ranks serve.  Metric: generated tokens per second of
+    wall time from the first arrival to the last completion."""
+    import asyncio
+    import random
+
+    import torch.distributed as dist
+
+    from forgeml_b200.nebula import AsyncBatcher, DecoderConfig, Engine, ParallelContext
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    pp = 2 if world % 2 == 0 and world >= 2 else 1
+    tp = world // pp
+    ctx = ParallelContext.from_env(tp_size=tp, pp_size=pp, device="cuda", timeout_s=300.0)
+    cfg = DecoderConfig(**C5)
+    engine = Engine(cfg, context=ctx, dtype=torch.bfloat16, max_requests=64, init="normal")
+    if ctx.rank != 0:
+        engine.serve()
+        engine.close()
+        torch.cuda.synchronize()
+        dist.barrier()
+        ctx.close()
+        return
+    rng = random.Random(C5["seed"])
+    n_req, n_new = args.c5_requests, args.c5_new
+    prompts = [[rng.randrange(cfg.vocab_size) for _ in range(rng.randint(128, 2048))] for _ in range(n_req)]
+    gaps = [rng.expovariate(64.0) for _ in range(n_req)]
+
+    async def drive():
+        b = AsyncBatcher(engine, max_batch_size=64, max_queue_size=n_req + 1, batch_window_ms=2.0)
+        lat = []
+
+        async def one(i, delay):
+            await asyncio.sleep(delay)
+            t0 = time.perf_counter()
+            toks = await b.submit(prompts[i], n_new)
+            lat.append(time.perf_counter() - t0)
+            return len(toks)
+
+        t_start = time.perf_counter()
+        delays, acc = [], 0.0
+        for g_ in gaps:
+            acc += g_
+            delays.append(acc)
+        counts = await asyncio.gather(*(one(i, d) for i, d in enumerate(delays)))
+        wall = time.perf_counter() - t_start
+        await b.close()  # closes the engine (STOP to the serving ranks)
+        return sum(counts), wall, sorted(lat)
+
+    # warm-up: one short request (captures nothing for PP, loads kernels)
+    engine.generate([prompts[0][:128]], 4)
+    total, wall, lat = asyncio.run(drive())
+    line = {"metric": "nebula_c5_serving_tokens_per_s", "value": total / wall, "unit": "tokens/s", "n_gpus": world,
+            "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "nebula_c5_async_batcher", "model": "32L d4096 h32x128 ffn16384 v32000",
+                       "parallelism": f"tp{tp}xpp{pp}", "requests": n_req, "new_tokens": n_new,
+                       "arrivals": "poisson 64 req/s (seeded)", "prompt_len": "uniform [128, 2048]",
+                       "batch_cap": 64},
+            "wall_s": wall, "generated_tokens": total,
+            "latency_s": {"p50": lat[len(lat) // 2], "p90": lat[int(len(lat) * 0.9)], "max": lat[-1]}}
+    print(json.dumps(line), flush=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ctx.close()
 
 
 def run_case(args) -> None:
@@ -582,9 +748,16 @@ def main() -> None:
     ap.add_argument("--cpu-layers", type=int, default=None, help="time this many layers of the CPU oracle")
     ap.add_argument("--case", choices=("attention", "gemm-decode", "gemm"), default=None,
                     help="run one kernel micro-benchmark instead of the decode bench")
+    ap.add_argument("--workload", choices=("c4", "c5"), default="c4",
+                    help="c5: serve config 5 through the AsyncBatcher over TP x PP (launch with torchrun)")
+    ap.add_argument("--c5-requests", type=int, default=32)
+    ap.add_argument("--c5-new", type=int, default=64)
     args = ap.parse_args()
     if args.case:
         run_case(args)
+        return
+    if args.workload == "c5":
+        run_c5(args)
         return
     if args.warmup < 3 and args.impl == "native":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
