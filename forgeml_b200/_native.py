@@ -55,6 +55,26 @@ class fml_tile_cfg(ctypes.Structure):
     ]
 
 
+class neb_fusion(ctypes.Structure):
+    """Fusions of neb_linear_fused (include/forgeml_b200.h)."""
+
+    _fields_ = [
+        ("ln_gamma", ctypes.c_void_p),
+        ("ln_beta", ctypes.c_void_p),
+        ("ln_eps", ctypes.c_float),
+        ("k_pool", ctypes.c_void_p),
+        ("v_pool", ctypes.c_void_p),
+        ("slot_of", ctypes.c_void_p),
+        ("start_pos", ctypes.c_void_p),
+        ("q_cols", ctypes.c_int32),
+        ("kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("max_seq", ctypes.c_int32),
+        ("tq", ctypes.c_int32),
+        ("ar_ctx", ctypes.c_void_p),
+    ]
+
+
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _I = ctypes.c_int
@@ -97,6 +117,10 @@ _SIGNATURES = {
     "neb_ar_buffer": (_P, [_P]),
     "neb_ar_all_reduce": (_I, [_P, _P, _P, _P, _I64, _I, _P]),
     "neb_ar_destroy": (_I, [_P]),
+    "neb_linear_fused": (
+        _I, [_P, _I64, _P, _I64, _I64, _P, _I64, _P, _I64, _I64, _I, _I, ctypes.POINTER(neb_fusion), _P]
+    ),
+    "neb_linear_fused_ok": (_I, [_I64, _I64, _I64, _I]),
     "fml_last_error": (ctypes.c_char_p, []),
     "fml_device_status": (_I, []),
     "fml_launch_count": (_I64, []),

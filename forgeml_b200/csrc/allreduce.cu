@@ -24,53 +24,26 @@
 //
 // Every wait is bounded (the context's timeout); on expiry the kernel raises
 // DEV_ERR_AR_TIMEOUT in the device error word and finishes without hanging.
+//
+// The same buffer carries a second region for the all-reduce fused into the
+// decode GEMM's epilogue (gemm.cu); its layout is in peer_layout.cuh.
 #include <cstring>
 #include <string>
 
 #include "common.cuh"
 
+#include "peer_layout.cuh"
+
 namespace fml {
 namespace ar {
 
-constexpr int kMaxWorld = 8;
-constexpr int kBlocks = 32;     // fixed grid (one chunk per CTA index)
+using peer::Ctx;
+using peer::kMaxWorld;
+using peer::ld_acquire_sys;
+using peer::st_release_sys;
+constexpr int kBlocks = peer::kArBlocks;  // fixed grid (one chunk per CTA index)
 constexpr int kThreads = 256;
-
-struct Layout {
-  long long max_bytes;  // bytes per slot (one rank's message)
-  int world;
-  // byte offsets inside a rank's buffer
-  __host__ __device__ long long data_off(int set, int slot) const { return ((long long)set * world + slot) * max_bytes; }
-  __host__ __device__ long long flags_off() const { return 2LL * world * max_bytes; }
-  __host__ __device__ long long flag_off(int set, int src, int blk) const {
-    return flags_off() + (((long long)set * world + src) * kBlocks + blk) * 4;
-  }
-  __host__ __device__ long long epochs_off() const { return flags_off() + 2LL * world * kBlocks * 4; }
-  __host__ __device__ long long total() const { return epochs_off() + kBlocks * 4; }
-};
-
-struct Args {
-  uint8_t* base[kMaxWorld];  // every rank's buffer, mapped into this process (own included)
-  Layout lay;
-  int rank;
-  long long timeout_cycles;
-};
-
-struct Ctx {
-  Args a;
-  uint8_t* own = nullptr;
-  bool opened[kMaxWorld] = {};
-  int device = 0;
-};
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
+using Args = peer::View;
 
 template <typename T>
 __device__ __forceinline__ void add_vec(float (&acc)[16 / sizeof(T)], const uint4& raw) {
@@ -88,7 +61,7 @@ __global__ void __launch_bounds__(kThreads) ar_kernel(const Args a, const T* __r
   pdl_trigger();
   const int blk = blockIdx.x, tid = threadIdx.x;
   const int W = a.lay.world, r = a.rank;
-  uint32_t* epochs = reinterpret_cast<uint32_t*>(a.base[r] + a.lay.epochs_off());
+  uint32_t* epochs = reinterpret_cast<uint32_t*>(a.base[r] + a.lay.epoch_off(0, 0));
   __shared__ uint32_t s_epoch;
   __shared__ int s_ok;
   if (tid == 0) {
@@ -106,16 +79,16 @@ __global__ void __launch_bounds__(kThreads) ar_kernel(const Args a, const T* __r
   for (long long i = v0 + tid; i < v1; i += kThreads) {
     const uint4 v = src[i];
     for (int q = 0; q < W; ++q)
-      reinterpret_cast<uint4*>(a.base[q] + a.lay.data_off(set, r))[i] = v;
+      reinterpret_cast<uint4*>(a.base[q] + a.lay.data_off(0, set, r))[i] = v;
   }
   __threadfence_system();
   __syncthreads();
   // 2. raise flag [r][blk] on every peer
   if (tid < W && tid != r)
-    st_release_sys(reinterpret_cast<uint32_t*>(a.base[tid] + a.lay.flag_off(set, r, blk)), e);
+    st_release_sys(reinterpret_cast<uint32_t*>(a.base[tid] + a.lay.flag_off(0, set, r, blk)), e);
   // 3. wait for every peer's flag [q][blk] (bounded)
   if (tid < W && tid != r) {
-    const uint32_t* f = reinterpret_cast<const uint32_t*>(a.base[r] + a.lay.flag_off(set, tid, blk));
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(a.base[r] + a.lay.flag_off(0, set, tid, blk));
     const long long t0 = clock64();
     while (ld_acquire_sys(f) != e) {
       if (clock64() - t0 > a.timeout_cycles) {
@@ -131,7 +104,7 @@ __global__ void __launch_bounds__(kThreads) ar_kernel(const Args a, const T* __r
     float acc[VE];
 #pragma unroll
     for (int k = 0; k < VE; ++k) acc[k] = 0.f;
-    for (int q = 0; q < W; ++q) add_vec<T>(acc, reinterpret_cast<const uint4*>(a.base[r] + a.lay.data_off(set, q))[i]);
+    for (int q = 0; q < W; ++q) add_vec<T>(acc, reinterpret_cast<const uint4*>(a.base[r] + a.lay.data_off(0, set, q))[i]);
     float res[VE];
     if (residual != nullptr) {
       const uint4 rv = reinterpret_cast<const uint4*>(residual)[i];
@@ -170,14 +143,15 @@ int neb_ar_create(int64_t max_bytes, int world, int rank, double timeout_ms, voi
   if (max_bytes <= 0 || max_bytes % 16 != 0) return fail(FML_EINVAL, "neb_ar_create: max_bytes must be a positive multiple of 16");
   if (!(timeout_ms > 0)) return fail(FML_EINVAL, "neb_ar_create: timeout must be positive");
   Ctx* c = new Ctx();
-  c->a.lay.max_bytes = max_bytes;
-  c->a.lay.world = world;
-  c->a.rank = rank;
+  c->v.lay.slot_bytes = max_bytes;
+  c->v.lay.nsub = (int)((max_bytes + 1023) / 1024);
+  c->v.lay.world = world;
+  c->v.rank = rank;
   int clk_khz = 0;
   c->device = fml::current_device();
   if (cudaDeviceGetAttribute(&clk_khz, cudaDevAttrClockRate, c->device) != cudaSuccess || clk_khz <= 0) clk_khz = 2000000;
-  c->a.timeout_cycles = (long long)(timeout_ms * (double)clk_khz);
-  const long long total = c->a.lay.total();
+  c->v.timeout_cycles = (long long)(timeout_ms * (double)clk_khz);
+  const long long total = c->v.lay.total();
   cudaError_t e = cudaMalloc(&c->own, (size_t)total);
   if (e != cudaSuccess) { delete c; return fml::check_cuda(e, "neb_ar_create: cudaMalloc"); }
   e = cudaMemset(c->own, 0, (size_t)total);
@@ -190,8 +164,8 @@ int neb_ar_create(int64_t max_bytes, int world, int rank, double timeout_ms, voi
     return fml::check_cuda(e, "neb_ar_create: buffer setup");
   }
   std::memcpy(handle_out, &h, sizeof(h));
-  for (int q = 0; q < kMaxWorld; ++q) c->a.base[q] = nullptr;
-  c->a.base[rank] = c->own;
+  for (int q = 0; q < kMaxWorld; ++q) c->v.base[q] = nullptr;
+  c->v.base[rank] = c->own;
   *ctx_out = c;
   return FML_OK;
 }
@@ -202,12 +176,12 @@ int neb_ar_open(void* ctx, const void* handles) {
   Ctx* c = static_cast<Ctx*>(ctx);
   if (!c || !handles) return fail(FML_EINVAL, "neb_ar_open: null pointer");
   const auto* hs = static_cast<const cudaIpcMemHandle_t*>(handles);
-  for (int q = 0; q < c->a.lay.world; ++q) {
-    if (q == c->a.rank || c->opened[q]) continue;
+  for (int q = 0; q < c->v.lay.world; ++q) {
+    if (q == c->v.rank || c->opened[q]) continue;
     void* p = nullptr;
     cudaError_t e = cudaIpcOpenMemHandle(&p, hs[q], cudaIpcMemLazyEnablePeerAccess);
     if (e != cudaSuccess) return fml::check_cuda(e, "neb_ar_open: cudaIpcOpenMemHandle");
-    c->a.base[q] = static_cast<uint8_t*>(p);
+    c->v.base[q] = static_cast<uint8_t*>(p);
     c->opened[q] = true;
   }
   return FML_OK;
@@ -218,10 +192,10 @@ int neb_ar_open(void* ctx, const void* handles) {
 int neb_ar_set_peers(void* ctx, void* const* bases) {
   Ctx* c = static_cast<Ctx*>(ctx);
   if (!c || !bases) return fail(FML_EINVAL, "neb_ar_set_peers: null pointer");
-  for (int q = 0; q < c->a.lay.world; ++q) {
-    if (q == c->a.rank) continue;
+  for (int q = 0; q < c->v.lay.world; ++q) {
+    if (q == c->v.rank) continue;
     if (!bases[q]) return fail(FML_EINVAL, "neb_ar_set_peers: null peer buffer");
-    c->a.base[q] = static_cast<uint8_t*>(bases[q]);
+    c->v.base[q] = static_cast<uint8_t*>(bases[q]);
   }
   return FML_OK;
 }
@@ -232,11 +206,11 @@ int neb_ar_all_reduce(void* ctx, const void* part, const void* residual, void* o
   Ctx* c = static_cast<Ctx*>(ctx);
   if (!c || !part || !out) return fail(FML_EINVAL, "neb_ar_all_reduce: null pointer");
   if (!fml::valid_dtype(dtype)) return fail(FML_EINVAL, "neb_ar_all_reduce: bad dtype");
-  for (int q = 0; q < c->a.lay.world; ++q)
-    if (!c->a.base[q]) return fail(FML_EINVAL, "neb_ar_all_reduce: peers not opened");
+  for (int q = 0; q < c->v.lay.world; ++q)
+    if (!c->v.base[q]) return fail(FML_EINVAL, "neb_ar_all_reduce: peers not opened");
   const long long bytes = n * (long long)fml::dtype_size(dtype);
   if (n <= 0 || bytes % 16 != 0) return fail(FML_EUNSUPPORTED, "neb_ar_all_reduce: message must be a positive multiple of 16 bytes");
-  if (bytes > c->a.lay.max_bytes) return fail(FML_EUNSUPPORTED, "neb_ar_all_reduce: message larger than the buffer slot");
+  if (bytes > c->v.lay.slot_bytes) return fail(FML_EUNSUPPORTED, "neb_ar_all_reduce: message larger than the buffer slot");
   for (const void* p : {part, residual, (const void*)out})
     if (p && reinterpret_cast<uintptr_t>(p) % 16 != 0) return fail(FML_EUNSUPPORTED, "neb_ar_all_reduce: pointers must be 16-byte aligned");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -244,14 +218,14 @@ int neb_ar_all_reduce(void* ctx, const void* part, const void* residual, void* o
   cudaError_t e;
   const dim3 grid(fml::ar::kBlocks), block(fml::ar::kThreads);
   if (dtype == FML_F32)
-    e = fml::launch_pdl(fml::ar::ar_kernel<float>, grid, block, 0, st, 1, c->a, static_cast<const float*>(part),
+    e = fml::launch_pdl(fml::ar::ar_kernel<float>, grid, block, 0, st, 1, c->v, static_cast<const float*>(part),
                         static_cast<const float*>(residual), static_cast<float*>(out), nvec);
   else if (dtype == FML_BF16)
-    e = fml::launch_pdl(fml::ar::ar_kernel<__nv_bfloat16>, grid, block, 0, st, 1, c->a,
+    e = fml::launch_pdl(fml::ar::ar_kernel<__nv_bfloat16>, grid, block, 0, st, 1, c->v,
                         static_cast<const __nv_bfloat16*>(part), static_cast<const __nv_bfloat16*>(residual),
                         static_cast<__nv_bfloat16*>(out), nvec);
   else
-    e = fml::launch_pdl(fml::ar::ar_kernel<__half>, grid, block, 0, st, 1, c->a, static_cast<const __half*>(part),
+    e = fml::launch_pdl(fml::ar::ar_kernel<__half>, grid, block, 0, st, 1, c->v, static_cast<const __half*>(part),
                         static_cast<const __half*>(residual), static_cast<__half*>(out), nvec);
   fml::count_launch();
   return fml::check_cuda(e, "neb_ar_all_reduce launch");
@@ -262,7 +236,7 @@ int neb_ar_destroy(void* ctx) {
   if (!c) return FML_OK;
   cudaDeviceSynchronize();
   for (int q = 0; q < kMaxWorld; ++q)
-    if (c->opened[q] && c->a.base[q]) cudaIpcCloseMemHandle(c->a.base[q]);
+    if (c->opened[q] && c->v.base[q]) cudaIpcCloseMemHandle(c->v.base[q]);
   if (c->own) cudaFree(c->own);
   delete c;
   return FML_OK;

@@ -42,6 +42,7 @@
 #include <tuple>
 
 #include "common.cuh"
+#include "peer_layout.cuh"
 
 namespace fml {
 namespace gemm {
@@ -80,6 +81,23 @@ struct Params {
   int red_stride;          // floats per row of the split-K partial buffer
   int promote_kb;          // K slabs per TMEM chunk when partial sums are promoted to registers
   const uint8_t* p_packed; // P pre-packed as swizzled 16 KB tiles (nullptr: P comes through tmP)
+  // Fused decode linear (FUSED kernels: pre-packed 16-bit weight, one tile per cluster).
+  // LayerNorm prologue: Q = LN(x) over ln_k columns, computed by the epilogue warps.
+  const void* ln_x;        // nullptr: Q comes through tmQ
+  long long ln_ldx;
+  const void* ln_g;
+  const void* ln_b;
+  float ln_eps;
+  int ln_k;
+  // KV-append epilogue: output feature n >= kv_q_cols goes to the K (then V) pool.
+  void* kv_k;              // nullptr: no KV epilogue
+  void* kv_v;
+  const int32_t* kv_slot;
+  const int32_t* kv_start;
+  int kv_q_cols, kv_cols, kv_heads, kv_hd, kv_max_seq, kv_tq;
+  // SUM all-reduce over the TP group (peer buffers) fused into the epilogue.
+  int ar_on;
+  peer::View ar;
 };
 
 struct Smem {
@@ -88,6 +106,7 @@ struct Smem {
   uint32_t p_bytes;
   uint32_t bars;        // base of the barrier block
   uint32_t red;         // split-K partial buffer
+  uint32_t aux;         // FUSED kernels: LayerNorm statistics and all-reduce staging
 };
 
 __device__ __forceinline__ uint32_t bar_full(const Smem& s, int i) { return s.bars + 8 * i; }
@@ -112,7 +131,12 @@ __device__ __forceinline__ uint32_t bar_dealloc(const Smem& s) {
 __device__ __forceinline__ uint32_t bar_drain(const Smem& s) {
   return s.bars + 8 * (2 * kMaxStages + 6);
 }
-constexpr int kNumBars = 2 * kMaxStages + 7;
+// LayerNorm prologue: completes once every other CTA of the cluster has
+// pushed its row statistics of its K slice.
+__device__ __forceinline__ uint32_t bar_ln(const Smem& s) {
+  return s.bars + 8 * (2 * kMaxStages + 7);
+}
+constexpr int kNumBars = 2 * kMaxStages + 8;
 constexpr int kBarBytes = 8 * kNumBars + 16;  // + tmem holder
 
 __device__ __forceinline__ void tile_coords(const Params& p, int t, int& ti, int& tj) {
@@ -252,12 +276,314 @@ __device__ __forceinline__ bool epilogue_row32_fast(const Params& p, int m, int 
   return true;
 }
 
+// ---------------------------------------------------------------------------
+// Fused decode linear (FUSED kernels).  Nebula's decode step chains
+//   LayerNorm -> QKV GEMM -> KV append            (src/nebula/runtime.py:130-138)
+//   o GEMM -> SUM all-reduce -> + residual        (runtime.py:145-146)
+//   LayerNorm -> up GEMM + GELU                   (runtime.py:151-152)
+//   down GEMM -> SUM all-reduce -> + residual     (runtime.py:153-154)
+// and the FUSED kernels run each line as one launch: the LayerNorm of the Q
+// operand is computed by the epilogue warps while the weight stream starts
+// (they are idle until the accumulator is ready), the KV rows go from the
+// split-K reduction straight into the cache pools, and the row-parallel
+// partial is exchanged with the other TP ranks over NVLink from the epilogue.
+//
+// Shared-memory block after the split-K buffer:
+//   stats [8][BN] float2   each cluster CTA's row sums of its K slice
+//   rowst [BN] float2      row mean and 1/sqrt(var + eps)
+//   ep    [8] u32          exchange epochs of this CTA's sub-blocks
+//   stage [128][32] u16    the rounded partial, feature-major, for the exchange
+// ---------------------------------------------------------------------------
+__host__ __device__ constexpr int aux_rowst(int bn) { return 8 * bn * 8; }
+__host__ __device__ constexpr int aux_ep(int bn) { return aux_rowst(bn) + bn * 8; }
+__host__ __device__ constexpr int aux_stage(int bn) { return (aux_ep(bn) + 32 + 15) / 16 * 16; }
+__host__ __device__ constexpr int aux_bytes(int bn) {
+  return aux_stage(bn) + 128 * peer::kSubTokens * 2;
+}
+
+__device__ __forceinline__ float h2f(uint32_t v, bool bf) {
+  return bf ? __uint_as_float((v & 0xffffu) << 16) : __half2float(__ushort_as_half((unsigned short)(v & 0xffffu)));
+}
+__device__ __forceinline__ uint32_t f2h(float v, bool bf) {
+  return bf ? (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v))
+            : (uint32_t)__half_as_ushort(__float2half_rn(v));
+}
+__device__ __forceinline__ void unpack8(const uint4& r, bool bf, float (&v)[8]) {
+  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = h2f(w[i], bf);
+    v[2 * i + 1] = h2f(w[i] >> 16, bf);
+  }
+}
+__device__ __forceinline__ void st_async_v2(uint32_t addr, float a, float b, uint32_t mbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(addr),
+               "f"(a), "f"(b), "r"(mbar)
+               : "memory");
+}
+__device__ __forceinline__ void st_shared_v2(uint32_t addr, float a, float b) {
+  asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
+}
+__device__ __forceinline__ float2 ld_shared_v2(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_shared_u4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_u4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_shared_u2(uint32_t addr, uint32_t a, uint32_t b) {
+  asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_shared_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_shared_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+// Generic-proxy shared-memory writes become visible to the tensor core (async proxy).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// Barrier of the 128 epilogue threads that also ANDs a predicate over them,
+// so that every thread takes the same branch afterwards.
+__device__ __forceinline__ bool epi_bar_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)(v ? 1 : 0))
+      : "memory");
+  return r != 0;
+}
+
+// LayerNorm of the Q operand (x rows = tokens) into this CTA's pipeline
+// stages, in the SWIZZLE_128B K-major image a TMA load would produce:
+//   y = (x - mean) / sqrt(var + eps) * gamma + beta   over all ln_k columns,
+// rounded to the 16-bit dtype (src/nebula/runtime.py:130,151; biased
+// variance as F.layer_norm).  Each CTA of the split-K cluster reads only its
+// K slice: it sums (x - x[r][0]) and its square over the slice, the cluster
+// exchanges these partials through distributed shared memory, and every CTA
+// adds them in cluster-rank order (identical statistics in every CTA).  The
+// shift by the row's first element keeps var = E[d^2] - E[d]^2 well
+// conditioned.  Then the slice is normalised stage by stage; each stage is
+// handed to the UMMA warp like a TMA stage (one arrival on its full barrier).
+// All 128 threads run every barrier; a timed-out wait only clears the result.
+template <int BN>
+__device__ bool ln_prologue(const Params& p, const Smem& s, int ksplit, uint32_t crank, int kb_begin,
+                            int kb_end, int tid) {
+  constexpr int TPR = 128 / BN;  // threads per row
+  const int r = tid / TPR, q = tid % TPR;
+  const bool bf = p.fmt == 1;
+  const bool valid = r < p.J;
+  const uint16_t* xr = static_cast<const uint16_t*>(p.ln_x) + (long long)(valid ? r : 0) * p.ln_ldx;
+  const int nchunk = (kb_end - kb_begin) * (kSlab / 16);
+  const int e0 = kb_begin * (kSlab / 2);
+  float shift = 0.f, s1 = 0.f, s2 = 0.f;
+  if (valid) {
+    shift = h2f(xr[0], bf);
+#pragma unroll 4
+    for (int c = q; c < nchunk; c += TPR) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(xr + e0 + c * 8);
+      float v[8];
+      unpack8(raw, bf, v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float d = v[e] - shift;
+        s1 += d;
+        s2 += d * d;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 1; o < TPR; o <<= 1) {
+    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+    s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+  }
+  const uint32_t stats = s.aux;
+  const uint32_t rowst = s.aux + aux_rowst(BN);
+  const uint32_t bar = bar_ln(s);
+  if (ksplit > 1 && tid == 0) mbar_arrive_expect_tx(bar, (uint32_t)((ksplit - 1) * BN * 8));
+  if (q == 0) {
+    const uint32_t slot = stats + (uint32_t)(((int)crank * BN + r) * 8);
+    st_shared_v2(slot, s1, s2);
+    for (int c = 0; c < ksplit; ++c)
+      if (c != (int)crank) st_async_v2(mapa(slot, (uint32_t)c), s1, s2, mapa(bar, (uint32_t)c));
+  }
+  bool ok = true;
+  if (ksplit > 1) ok = mbar_wait_cluster(bar, 0, DEV_ERR_REDUCE_TIMEOUT);
+  epi_bar_sync();
+  if (q == 0) {
+    float S1 = 0.f, S2 = 0.f;
+    for (int c = 0; c < ksplit; ++c) {
+      const float2 v = ld_shared_v2(stats + (uint32_t)((c * BN + r) * 8));
+      S1 += v.x;
+      S2 += v.y;
+    }
+    const float kf = (float)p.ln_k;
+    const float md = S1 / kf;
+    const float var = fmaxf(S2 / kf - md * md, 0.f);
+    st_shared_v2(rowst + r * 8, shift + md, 1.0f / sqrtf(var + p.ln_eps));
+  }
+  epi_bar_sync();
+  const float2 ms = ld_shared_v2(rowst + r * 8);
+  const uint16_t* g = static_cast<const uint16_t*>(p.ln_g);
+  const uint16_t* b = static_cast<const uint16_t*>(p.ln_b);
+  int stage = 0;
+  uint32_t phase = 0;
+  for (int kb = kb_begin; kb < kb_end; ++kb) {
+    // first pass over the ring: the stage is free; later: wait for the UMMA
+    // warp to release it (as a TMA producer would)
+    if (!mbar_wait(bar_empty(s, stage), phase ^ 1u, DEV_ERR_GEMM_TIMEOUT)) ok = false;
+    const uint32_t qb = s.stage_base + stage * s.stage_bytes + s.p_bytes;
+    const int kel = kb * (kSlab / 2);
+#pragma unroll
+    for (int c = q; c < kSlab / 16; c += TPR) {
+      uint32_t w[4] = {0u, 0u, 0u, 0u};
+      if (valid) {
+        float v[8], gv[8], bv[8];
+        unpack8(*reinterpret_cast<const uint4*>(xr + kel + c * 8), bf, v);
+        unpack8(*reinterpret_cast<const uint4*>(g + kel + c * 8), bf, gv);
+        unpack8(*reinterpret_cast<const uint4*>(b + kel + c * 8), bf, bv);
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          float t0 = (v[e] - ms.x) * ms.y, t1 = (v[e + 1] - ms.x) * ms.y;
+          t0 = t0 * gv[e] + bv[e];
+          t1 = t1 * gv[e + 1] + bv[e + 1];
+          w[e / 2] = f2h(t0, bf) | (f2h(t1, bf) << 16);
+        }
+      }
+      st_shared_u4(qb + (uint32_t)(r * kSlab + ((c ^ (r & 7)) << 4)), w[0], w[1], w[2], w[3]);
+    }
+    fence_proxy_async_smem();
+    epi_bar_sync();
+    if (tid == 0) mbar_arrive(bar_full(s, stage));
+    if (++stage == p.stages) { stage = 0; phase ^= 1u; }
+  }
+  return ok;
+}
+
+// KV-append epilogue for one output element: feature n (>= kv_q_cols) of
+// token m goes to pool[slot_of[b], head, start_pos[b] + t, d] of the K or V
+// pool (m = b * tq + t), rounded to the 16-bit dtype like the GEMM output it
+// replaces (src/nebula/cache.py:161-165 via runtime.py:136-138).
+__device__ __forceinline__ void kv_store(const Params& p, int n, int m, float v) {
+  if (n >= p.cols_out || m >= p.J) return;
+  const int nn = n - p.kv_q_cols;
+  const bool is_v = nn >= p.kv_cols;
+  const int c = is_v ? nn - p.kv_cols : nn;
+  const int head = c / p.kv_hd, d = c - head * p.kv_hd;
+  const int b = m / p.kv_tq, t = m - b * p.kv_tq;
+  const int slot = p.kv_slot[b];
+  const int pos = p.kv_start[b] + t;
+  if (slot < 0 || pos < 0 || pos >= p.kv_max_seq) {
+    raise_device_error(DEV_ERR_ATTN_RANGE);
+    return;
+  }
+  const long long dst = (((long long)slot * p.kv_heads + head) * p.kv_max_seq + pos) * p.kv_hd + d;
+  uint16_t* pool = static_cast<uint16_t*>(is_v ? p.kv_v : p.kv_k);
+  pool[dst] = (uint16_t)f2h(v, p.fmt == 1);
+}
+
+// All-reduce epilogue of one owner CTA: its rows_per features (rows r0.. of
+// tile ti) x 32 tokens, already rounded into the staging block.  Per 16-
+// feature sub-block c: push the 1 KB block into slot `rank` of every rank's
+// buffer (NVLink stores), fence, raise flag [rank][c] on every peer with the
+// sub-block's epoch, wait for every peer's flag [q][c], then
+//   out = round(round(sum over q in rank order of slot q) + residual)
+// (ParallelContext.all_reduce + `x + part`, src/nebula/parallel.py:112-116,
+// runtime.py:146,154), identical on every rank.  Epochs and the two buffer
+// sets follow the standalone all-reduce's protocol (allreduce.cu) with the
+// sub-block as the unit.  Waits are bounded (DEV_ERR_AR_TIMEOUT).
+template <int BN>
+__device__ bool ar_exchange(const Params& p, const Smem& s, int ti, int r0, int rows_per, int tid) {
+  const peer::View& a = p.ar;
+  const int W = a.lay.world, rank = a.rank;
+  const bool bf = p.fmt == 1;
+  const int nsb = rows_per / peer::kSubFeatures;
+  const int c0 = (ti * kBM + r0) / peer::kSubFeatures;
+  const int nsub_valid = (p.cols_out + peer::kSubFeatures - 1) / peer::kSubFeatures;
+  constexpr int kSubBytes = peer::kSubFeatures * peer::kSubTokens * 2;  // 1 KB
+  constexpr int kChunks = kSubBytes / 16;
+  const uint32_t ep = s.aux + aux_ep(BN);
+  const uint32_t stg = s.aux + aux_stage(BN);
+  uint32_t* epochs = reinterpret_cast<uint32_t*>(a.base[rank] + a.lay.epoch_off(1, 0));
+  if (tid < nsb) st_shared_u32(ep + 4 * tid, c0 + tid < nsub_valid ? epochs[c0 + tid] + 1u : 0u);
+  epi_bar_sync();  // staging block and epochs visible to all epilogue threads
+  for (int u = tid; u < nsb * W * kChunks; u += 128) {
+    const int sb = u / (W * kChunks), rem = u - sb * (W * kChunks);
+    const int q = rem / kChunks, ch = rem - q * kChunks;
+    if (c0 + sb >= nsub_valid) continue;
+    const uint32_t e = ld_shared_u32(ep + 4 * sb);
+    const uint4 v = ld_shared_u4(stg + (uint32_t)(sb * kSubBytes + ch * 16));
+    *reinterpret_cast<uint4*>(a.base[q] + a.lay.data_off(1, (int)(e & 1u), rank) + (long long)(c0 + sb) * kSubBytes +
+                              ch * 16) = v;
+  }
+  __threadfence_system();
+  epi_bar_sync();
+  for (int u = tid; u < nsb * W; u += 128) {
+    const int sb = u / W, q = u - sb * W;
+    if (q == rank || c0 + sb >= nsub_valid) continue;
+    const uint32_t e = ld_shared_u32(ep + 4 * sb);
+    peer::st_release_sys(reinterpret_cast<uint32_t*>(a.base[q] + a.lay.flag_off(1, (int)(e & 1u), rank, c0 + sb)), e);
+  }
+  bool got = true;
+  for (int u = tid; u < nsb * W; u += 128) {
+    const int sb = u / W, q = u - sb * W;
+    if (q == rank || c0 + sb >= nsub_valid) continue;
+    const uint32_t e = ld_shared_u32(ep + 4 * sb);
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(a.base[rank] + a.lay.flag_off(1, (int)(e & 1u), q, c0 + sb));
+    const long long t0 = clock64();
+    while (peer::ld_acquire_sys(f) != e) {
+      if (clock64() - t0 > a.timeout_cycles) {
+        raise_device_error(DEV_ERR_AR_TIMEOUT);
+        got = false;
+        break;
+      }
+    }
+  }
+  got = epi_bar_and(got);  // every peer's block of this CTA's sub-blocks has landed
+  const uint16_t* res = static_cast<const uint16_t*>(p.residual);
+  uint16_t* out = static_cast<uint16_t*>(p.out);
+  for (int u = tid; u < rows_per * p.J; u += 128) {
+    const int f = u % rows_per, m = u / rows_per;
+    const int sb = f / peer::kSubFeatures;
+    const int n = ti * kBM + r0 + f;
+    if (n >= p.cols_out) continue;
+    const uint32_t e = ld_shared_u32(ep + 4 * sb);
+    const long long off = (long long)(c0 + sb) * kSubBytes + ((f % peer::kSubFeatures) * peer::kSubTokens + m) * 2;
+    float acc = 0.f;
+    for (int q = 0; q < W; ++q)
+      acc += h2f(*reinterpret_cast<const uint16_t*>(a.base[rank] + a.lay.data_off(1, (int)(e & 1u), q) + off), bf);
+    float x = h2f(f2h(acc, bf), bf);  // the all-reduced partial in the model dtype
+    if (res != nullptr) x = x + h2f(res[(long long)m * p.ldr + n], bf);
+    out[(long long)m * p.ldo + n] = (uint16_t)f2h(x, bf);
+  }
+  epi_bar_sync();
+  if (tid < nsb && c0 + tid < nsub_valid) epochs[c0 + tid] = ld_shared_u32(ep + 4 * tid);
+  return got;
+}
+
 // Narrow tiles are register-bounded for two CTAs per SM (the decode weight
 // stream, ~100 KB of shared memory each).
 // PAIR: a CTA pair (cluster of 2) computes 256 x BN tiles with cta_group::2
 // UMMAs; each CTA loads its 128 rows of P and BN/2 rows of Q (16-bit,
 // non-split only).
-template <int BN, bool PROMOTE, bool PAIR = false>
+// FUSED: the decode linear with the LayerNorm prologue, KV-append and
+// all-reduce epilogues (pre-packed 16-bit P, swapped, one tile per cluster,
+// always through the split-K reduction buffer).
+template <int BN, bool PROMOTE, bool PAIR = false, bool FUSED = false>
 __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
                 const Params p) {
@@ -275,6 +601,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
   s.bars = s.stage_base + p.stages * s.stage_bytes;
   s.red = s.bars + kBarBytes;
   s.red = (s.red + 15u) & ~15u;
+  s.aux = s.red + (uint32_t)(kBM * p.red_stride * 4 + 16);  // FUSED only (the split-K buffer is always there)
   const uint32_t tmem_holder = s.bars + 8 * kNumBars;
 
   const int ksplit = PAIR ? 1 : p.ksplit;
@@ -305,6 +632,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
       mbar_init(bar_tempty(s, a), PAIR ? 8 : 4);  // a pair's leader hears both CTAs' epilogues
     }
     mbar_init(bar_recv(s), 1);
+    mbar_init(bar_ln(s), 1);
     mbar_init(bar_dealloc(s), 1);
     mbar_init(bar_drain(s), 1);
     fence_mbar_init();
@@ -350,6 +678,8 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
     const uint32_t op_off = is_q ? s.p_bytes : 0u;
     const uint32_t slab_bytes = (uint32_t)rows * kSlab;
     const bool packed = !is_q && p.p_packed != nullptr;
+    // FUSED with the LayerNorm prologue: the epilogue warps write Q.
+    const bool idle = FUSED && is_q && p.ln_x != nullptr;
     const int nbox = mn ? rows / mn_box : 1;
     int stage = 0;
     uint32_t phase = 0;
@@ -382,7 +712,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
       tile_coords(p, t, ti, tj);
       const int rbase = is_q ? tj * BN + prank * kQRows : ti * kTileM + prank * kBM;
       for (int kb = kb_begin; kb < kb_end; kb += S, ++step) {
-        if ((step & 1) == parity && step >= pre_limit) {
+        if (!idle && (step & 1) == parity && step >= pre_limit) {
           const int nsl = min(S, kb_end - kb);
           // A pair's copies all complete on the leader's full barrier, which
           // the leader's producer arms with both CTAs' bytes.
@@ -525,6 +855,14 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
       if (owner == (int)crank) st_shared_v4(push_local + col * 4, a, b, c, d);
       else st_async_v4(push_dst + col * 4, a, b, c, d, push_bar);
     };
+    // FUSED kernels always reduce through the split-K buffer (also with one
+    // CTA per tile), where the KV and all-reduce epilogues take over.
+    constexpr bool kRedAlways = FUSED;
+    const bool use_red = ksplit > 1 || kRedAlways;
+    if constexpr (FUSED) {
+      if (p.ln_x != nullptr && cluster_id < p.num_tiles)
+        ok = epi_bar_and(ln_prologue<BN>(p, s, ksplit, crank, kb_begin, kb_end, ep_tid));
+    }
     for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
       int ti, tj;
       tile_coords(p, t, ti, tj);
@@ -568,7 +906,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
           }
             }
             const int nvalid = min(32, BN - c * 32);
-            if (ksplit == 1) {
+            if (!use_red) {
               const int j0 = tj * BN + c * 32;
               if (nvalid == 32 && epilogue_row32_fast(p, i, j0, v)) continue;
 #pragma unroll 1
@@ -584,7 +922,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
       }
       if (!ok) break;
       if (PROMOTE) {
-        if (ksplit == 1) {
+        if (!use_red) {
 #pragma unroll 1
           for (int e = 0; e < BN; ++e) epilogue_store(p, i, tj * BN + e, racc[e]);
         } else {
@@ -593,9 +931,16 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
             push4(4 * q, racc[4 * q], racc[4 * q + 1], racc[4 * q + 2], racc[4 * q + 3]);
         }
       }
-      if (ksplit > 1) {
+      if (use_red) {
         epi_bar_sync();  // own rows' plain stores visible to every epilogue thread
-        if (!mbar_wait_cluster(bar_recv(s), 0, DEV_ERR_REDUCE_TIMEOUT)) { ok = false; break; }
+        if (FUSED) {
+          // every thread must leave together: the exchange below has barriers
+          const bool got = ksplit == 1 || mbar_wait_cluster(bar_recv(s), 0, DEV_ERR_REDUCE_TIMEOUT);
+          if (!epi_bar_and(got)) { ok = false; break; }
+        } else if (!mbar_wait_cluster(bar_recv(s), 0, DEV_ERR_REDUCE_TIMEOUT)) {
+          ok = false;
+          break;
+        }
         const int r0 = crank * rows_per;
         constexpr int kGroups = BN / 4 > 0 ? BN / 4 : 1;  // 4-column groups per row
         const int items = rows_per * kGroups;
@@ -611,8 +956,27 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
             sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
           }
           const float quad4[4] = {sum.x, sum.y, sum.z, sum.w};
+          if constexpr (FUSED) {
+            // MMA row = output feature, column = token (swapped form)
+            const int n = ti * kBM + r0 + rr;
+            const bool bf = p.fmt == 1;
+            if (p.ar_on) {
+              // rounded partial -> staging block [feature][token] for the exchange
+              st_shared_u2(s.aux + aux_stage(BN) + (uint32_t)((rr * peer::kSubTokens + 4 * cg) * 2),
+                           f2h(sum.x, bf) | (f2h(sum.y, bf) << 16), f2h(sum.z, bf) | (f2h(sum.w, bf) << 16));
+              continue;
+            }
+            if (p.kv_k != nullptr && n >= p.kv_q_cols) {
+#pragma unroll 1
+              for (int e = 0; e < 4; ++e) kv_store(p, n, tj * BN + 4 * cg + e, quad4[e]);
+              continue;
+            }
+          }
 #pragma unroll 1
           for (int e = 0; e < 4; ++e) epilogue_store(p, ti * kBM + r0 + rr, tj * BN + 4 * cg + e, quad4[e]);
+        }
+        if constexpr (FUSED) {
+          if (p.ar_on && !ar_exchange<BN>(p, s, ti, r0, rows_per, ep_tid)) ok = false;
         }
       }
     }
@@ -832,6 +1196,7 @@ struct Plan {
   bool swap;
   bool promote;  // fp32: sum TMEM partials in fp32 registers every kPromoteKb slabs
   bool packed;   // P is a pre-packed constant weight (fml_linear_packed)
+  bool fused = false;  // FUSED decode-linear kernel (neb_linear_fused)
   int bn;
   int ksplit;
   int stages;
@@ -843,12 +1208,13 @@ struct Plan {
 
 static const int kBNs[] = {16, 32, 64, 128, 256};
 
-static int smem_bytes_for(int bn, int stages, int ksplit, int* red_stride, int slabs = 1, bool pair = false) {
+static int smem_bytes_for(int bn, int stages, int ksplit, int* red_stride, int slabs = 1, bool pair = false,
+                          bool fused = false) {
   int stage_bytes = slabs * (kBM + (pair ? bn / 2 : bn)) * kSlab;
   int rs = bn + 4;
   if (red_stride) *red_stride = rs;
-  int red = ksplit > 1 ? kBM * rs * 4 + 16 : 0;
-  return 1024 + stages * stage_bytes + kBarBytes + 16 + red;
+  int red = (ksplit > 1 || fused) ? kBM * rs * 4 + 16 : 0;
+  return 1024 + stages * stage_bytes + kBarBytes + 16 + red + (fused ? aux_bytes(bn) : 0);
 }
 
 // CTAs of one SM this configuration fits: shared memory, registers, threads
@@ -962,7 +1328,7 @@ static void choose_split(Plan& pl, long long tiles, long long num_kb, const fml_
   for (int ks : {1, 2, 4, 8}) {
     if (ks > 1 && (pl.bn > 128 || num_kb < 2LL * ks || tiles * 2 > sms)) continue;
     const int st = stages_for(pl.bn, ks, cfg, pl.slabs, pl.packed);
-    const int smem = smem_bytes_for(pl.bn, st, ks, nullptr, pl.slabs);
+    const int smem = smem_bytes_for(pl.bn, st, ks, nullptr, pl.slabs, false, pl.fused);
     if (smem > kSmemLimit) continue;
     const int res = resident_ctas(pl.bn, pl.promote, ks, smem, sms);
     if (res <= 0) continue;
@@ -1059,14 +1425,14 @@ static int make_plan(Plan& pl, const void* a, long long lda_m, long long lda_k, 
   return FML_OK;
 }
 
-template <int BN, bool PROMOTE, bool PAIR = false>
+template <int BN, bool PROMOTE, bool PAIR = false, bool FUSED = false>
 static int launch_bn(const CUtensorMap& mp, const CUtensorMap& mq, const Params& prm, int grid,
                      int smem, cudaStream_t st) {
   static std::once_flag once[64];
   const int dev = current_device();
   cudaError_t e = cudaSuccess;
   std::call_once(once[dev & 63], [&]() {
-    e = cudaFuncSetAttribute(gemm_kernel<BN, PROMOTE, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(gemm_kernel<BN, PROMOTE, PAIR, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemLimit);
   });
   if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(gemm)");
@@ -1089,7 +1455,7 @@ static int launch_bn(const CUtensorMap& mp, const CUtensorMap& mq, const Params&
   }
   lc.attrs = attr;
   lc.numAttrs = na;
-  e = cudaLaunchKernelEx(&lc, gemm_kernel<BN, PROMOTE, PAIR>, mp, mq, prm);
+  e = cudaLaunchKernelEx(&lc, gemm_kernel<BN, PROMOTE, PAIR, FUSED>, mp, mq, prm);
   if (e != cudaSuccess) return check_cuda(e, "gemm launch");
   count_launch();
   return FML_OK;
@@ -1099,8 +1465,8 @@ static int launch_bn(const CUtensorMap& mp, const CUtensorMap& mq, const Params&
 static int launch_plan(const Plan& pl, const CUtensorMap& mp, const CUtensorMap& mq, int dtype, int act,
                        const void* bias, long long bias_stride, const void* residual, long long ldr, void* c,
                        long long ldc, long long m, long long n, const uint8_t* p_packed, int sms,
-                       cudaStream_t st) {
-  Params prm = {};
+                       cudaStream_t st, const Params* fusion = nullptr) {
+  Params prm = fusion ? *fusion : Params{};
   prm.I = (int)pl.P.rows;
   prm.J = (int)pl.Q.rows;
   const long long es = (long long)dtype_size(dtype);
@@ -1135,7 +1501,7 @@ static int launch_plan(const Plan& pl, const CUtensorMap& mp, const CUtensorMap&
   prm.cols_out = (int)n;
   prm.p_packed = p_packed;
   int red_stride = 0;
-  const int smem = smem_bytes_for(pl.bn, pl.stages, pl.ksplit, &red_stride, pl.slabs, pl.pair);
+  const int smem = smem_bytes_for(pl.bn, pl.stages, pl.ksplit, &red_stride, pl.slabs, pl.pair, pl.fused);
   prm.red_stride = red_stride;
   prm.promote_kb = kPromoteKb;
   // Persistent grid (as many CTAs as are co-resident) without split-K; with
@@ -1158,6 +1524,15 @@ static int launch_plan(const Plan& pl, const CUtensorMap& mp, const CUtensorMap&
     const int res = resident_ctas(pl.bn, pl.promote, pl.ksplit, smem, sms);
     fprintf(stderr, "[fml_gemm] I=%d J=%d num_kb=%d bn=%d swap=%d packed=%d ksplit=%d slabs=%d stages=%d smem=%d grid=%d resident=%d\n",
             prm.I, prm.J, prm.num_kb, pl.bn, prm.swap, pl.packed ? 1 : 0, pl.ksplit, pl.slabs, pl.stages, smem, grid, res);
+  }
+  if (pl.fused) {
+    // one tile per cluster: the LayerNorm prologue and the exchange run once per CTA
+    if (grid < want) return fail(FML_EUNSUPPORTED, "linear_fused: output tiles exceed the co-resident CTAs");
+    switch (pl.bn) {
+      case 16: return launch_bn<16, false, false, true>(mp, mq, prm, grid, smem, st);
+      case 32: return launch_bn<32, false, false, true>(mp, mq, prm, grid, smem, st);
+    }
+    return fail(FML_EUNSUPPORTED, "linear_fused: batch of more than 32 tokens");
   }
   if (pl.pair) return launch_bn<256, false, true>(mp, mq, prm, grid, smem, st);
   if (pl.promote) {
@@ -1313,6 +1688,27 @@ extern "C" int fml_pack_weight(const void* w, int64_t ldw, int64_t n, int64_t k,
   return check_cuda(cudaGetLastError(), "pack_weight launch");
 }
 
+// MMA-space plan of a packed-weight product: P = packed W (N rows), Q = x
+// (M rows), always the swapped form.
+static int packed_plan(Plan& pl, const void* x, long long ldx, const void* packed, long long n, long long k,
+                       long long m, int dtype, const fml_tile_cfg* cfg, int sms, bool fused) {
+  pl.packed = true;
+  pl.fused = fused;
+  pl.swap = true;
+  pl.promote = false;
+  pl.P = Operand{packed, 0, 1, n, k, false, false, 0, 0};
+  pl.Q = Operand{x, ldx, 1, m, k, false, false, 0, 0};
+  pl.bn = pick_bn(pl, n, m, cfg, sms);
+  classify(pl.Q, dtype, pl.bn, false);
+  if (pl.Q.pack) return fail(FML_EUNSUPPORTED, "linear_packed: x must be row-major with 16-byte aligned rows");
+  pl.keff = k;
+  pl.ws_bytes = 0;
+  pl.slabs = slabs_for(cfg, dtype, false, pl.bn, true);
+  const long long tiles = ((n + kBM - 1) / kBM) * ((m + pl.bn - 1) / pl.bn);
+  choose_split(pl, tiles, packed_kb(k, dtype), cfg, sms);
+  return FML_OK;
+}
+
 extern "C" int fml_linear_packed(const void* x, int64_t ldx, const void* packed, int64_t n, int64_t k,
                                  const void* bias, int64_t bias_stride, const void* residual, int64_t ldr,
                                  void* out, int64_t ldo, int64_t m, int dtype, int act,
@@ -1327,26 +1723,109 @@ extern "C" int fml_linear_packed(const void* x, int64_t ldx, const void* packed,
     return fail(FML_EINVAL, "linear_packed: packed weight must be 1024-byte aligned");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int sms = num_sms(current_device());
-  // MMA space: P = packed W (N rows), Q = x (M rows): always the swapped form.
   Plan pl;
-  pl.packed = true;
-  pl.swap = true;
-  pl.promote = false;
-  pl.P = Operand{packed, 0, 1, n, k, false, false, 0, 0};
-  pl.Q = Operand{x, ldx, 1, m, k, false, false, 0, 0};
-  pl.bn = pick_bn(pl, n, m, cfg, sms);
-  classify(pl.Q, dtype, pl.bn, false);
-  if (pl.Q.pack) return fail(FML_EUNSUPPORTED, "linear_packed: x must be row-major with 16-byte aligned rows");
-  pl.keff = k;
-  pl.ws_bytes = 0;
-  pl.slabs = slabs_for(cfg, dtype, false, pl.bn, true);
-  const long long tiles = ((n + kBM - 1) / kBM) * ((m + pl.bn - 1) / pl.bn);
-  choose_split(pl, tiles, packed_kb(k, dtype), cfg, sms);
+  rc = packed_plan(pl, x, ldx, packed, n, k, m, dtype, cfg, sms, false);
+  if (rc) return rc;
   CUtensorMap mq;
   rc = encode(&mq, x, dtype, false, false, m, k, pl.Q.s_r, pl.bn);
   if (rc) return rc;
   return launch_plan(pl, mq, mq, dtype, act, bias, bias_stride, residual, ldr, out, ldo, m, n,
                      static_cast<const uint8_t*>(packed), sms, st);
+}
+
+// Whether the FUSED kernel covers the shape: 16-bit, m <= 32 (BN 16 or 32),
+// one slab per stage, and one output tile per cluster with every CTA
+// resident at once.
+static bool fused_plan_ok(const Plan& pl, long long n, long long m, int sms) {
+  if (pl.bn > 32 || pl.slabs != 1) return false;  // the LayerNorm prologue fills one slab per stage
+  const long long tiles = ((n + kBM - 1) / kBM) * ((m + pl.bn - 1) / pl.bn);
+  // Every CTA resident at once: the all-reduce epilogue waits on the other
+  // ranks' CTAs of the same tile, which must not queue behind waiting CTAs.
+  const int smem = smem_bytes_for(pl.bn, pl.stages, pl.ksplit, nullptr, pl.slabs, false, true);
+  const int res = resident_ctas(pl.bn, false, pl.ksplit, smem, sms);
+  return res > 0 && tiles * pl.ksplit <= res;
+}
+
+extern "C" int neb_linear_fused_ok(int64_t n, int64_t k, int64_t m, int dtype) {
+  if ((dtype != FML_BF16 && dtype != FML_F16) || n <= 0 || k <= 0 || m <= 0 || m > 32) return 0;
+  const int sms = num_sms(current_device());
+  Plan pl;
+  const void* fake = reinterpret_cast<const void*>(uintptr_t(1024));
+  if (packed_plan(pl, fake, k, fake, n, k, m, dtype, nullptr, sms, true) != FML_OK) return 0;
+  return fused_plan_ok(pl, n, m, sms) ? 1 : 0;
+}
+
+extern "C" int neb_linear_fused(const void* x, int64_t ldx, const void* packed, int64_t n, int64_t k,
+                                const void* residual, int64_t ldr, void* out, int64_t ldo, int64_t m, int dtype,
+                                int act, const neb_fusion* fu, void* stream) {
+  if (dtype != FML_BF16 && dtype != FML_F16) return fail(FML_EUNSUPPORTED, "linear_fused: 16-bit only");
+  int rc = validate_gemm(x, packed, out, m, n, k, dtype);
+  if (rc) return rc;
+  if (!fu) return fail(FML_EINVAL, "linear_fused: null fusion descriptor");
+  if (act < 0 || act > 2) return fail(FML_EINVAL, "linear_fused: bad act");
+  if (m > 32) return fail(FML_EUNSUPPORTED, "linear_fused: more than 32 tokens");
+  if (reinterpret_cast<uintptr_t>(packed) % 1024 != 0)
+    return fail(FML_EINVAL, "linear_fused: packed weight must be 1024-byte aligned");
+  if ((m > 1 && ldx < k) || (residual && ldr < n)) return fail(FML_EINVAL, "linear_fused: bad leading dimension");
+  Params fz = {};
+  const bool kv = fu->k_pool != nullptr;
+  const bool ar = fu->ar_ctx != nullptr;
+  if (fu->ln_gamma) {
+    if (!fu->ln_beta) return fail(FML_EINVAL, "linear_fused: LayerNorm needs gamma and beta");
+    if (k % 64 != 0) return fail(FML_EUNSUPPORTED, "linear_fused: LayerNorm prologue needs k a multiple of 64");
+    if (reinterpret_cast<uintptr_t>(x) % 16 || (ldx * 2) % 16 || reinterpret_cast<uintptr_t>(fu->ln_gamma) % 16 ||
+        reinterpret_cast<uintptr_t>(fu->ln_beta) % 16)
+      return fail(FML_EUNSUPPORTED, "linear_fused: LayerNorm operands must be 16-byte aligned");
+    fz.ln_x = x;
+    fz.ln_ldx = ldx;
+    fz.ln_g = fu->ln_gamma;
+    fz.ln_b = fu->ln_beta;
+    fz.ln_eps = fu->ln_eps;
+    fz.ln_k = (int)k;
+  }
+  if (kv) {
+    if (!fu->v_pool || !fu->slot_of || !fu->start_pos) return fail(FML_EINVAL, "linear_fused: KV epilogue pointers");
+    if (fu->q_cols < 0 || fu->kv_heads <= 0 || fu->head_dim <= 0 || fu->max_seq <= 0 || fu->tq <= 0 ||
+        m % fu->tq != 0 || (long long)fu->q_cols + 2LL * fu->kv_heads * fu->head_dim != n)
+      return fail(FML_EINVAL, "linear_fused: KV epilogue shape (n must be q_cols + 2*kv_heads*head_dim)");
+    if (ldo < fu->q_cols) return fail(FML_EINVAL, "linear_fused: ldo < q_cols");
+    if (ar) return fail(FML_EUNSUPPORTED, "linear_fused: the KV and all-reduce epilogues do not combine");
+    fz.kv_k = fu->k_pool;
+    fz.kv_v = fu->v_pool;
+    fz.kv_slot = fu->slot_of;
+    fz.kv_start = fu->start_pos;
+    fz.kv_q_cols = fu->q_cols;
+    fz.kv_cols = fu->kv_heads * fu->head_dim;
+    fz.kv_heads = fu->kv_heads;
+    fz.kv_hd = fu->head_dim;
+    fz.kv_max_seq = fu->max_seq;
+    fz.kv_tq = fu->tq;
+  } else if (ldo < n) {
+    return fail(FML_EINVAL, "linear_fused: ldo < n");
+  }
+  if (ar) {
+    const peer::Ctx* c = static_cast<const peer::Ctx*>(fu->ar_ctx);
+    if (act != 0) return fail(FML_EUNSUPPORTED, "linear_fused: the all-reduce epilogue takes no activation");
+    if (n % peer::kSubFeatures != 0 || n / peer::kSubFeatures > c->v.lay.nsub ||
+        n * peer::kSubTokens * 2 > c->v.lay.slot_bytes)
+      return fail(FML_EUNSUPPORTED, "linear_fused: n must be a multiple of 16 with n*64 <= the context's max_bytes");
+    for (int q = 0; q < c->v.lay.world; ++q)
+      if (!c->v.base[q]) return fail(FML_EINVAL, "linear_fused: all-reduce peers not opened");
+    fz.ar_on = 1;
+    fz.ar = c->v;
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int sms = num_sms(current_device());
+  Plan pl;
+  rc = packed_plan(pl, x, ldx, packed, n, k, m, dtype, nullptr, sms, true);
+  if (rc) return rc;
+  if (!fused_plan_ok(pl, n, m, sms))
+    return fail(FML_EUNSUPPORTED, "linear_fused: shape not covered (see neb_linear_fused_ok)");
+  CUtensorMap mq;
+  rc = encode(&mq, x, dtype, false, false, m, k, pl.Q.s_r, pl.bn);
+  if (rc) return rc;
+  return launch_plan(pl, mq, mq, dtype, act, nullptr, 0, residual, ldr, out, ldo, m, n,
+                     static_cast<const uint8_t*>(packed), sms, st, &fz);
 }
 
 // ---------------------------------------------------------------------------

@@ -49,3 +49,40 @@ class PackedLinear:
             cfg, _native.stream_ptr(x.device),
         )
         return out
+
+    def fused_ok(self, m: int) -> bool:
+        """Whether ``fused`` covers an m-token call on the current device."""
+        return bool(_native.load().neb_linear_fused_ok(self.n, self.k, m, self.code))
+
+    def fused(self, x: torch.Tensor, out: torch.Tensor, *, act: int = 0, residual: torch.Tensor | None = None,
+              ln: tuple | None = None, kv: tuple | None = None, ar_ctx=None, rows: int | None = None) -> torch.Tensor:
+        """Decode-step linear with its neighbours fused into the one launch
+        (``neb_linear_fused``):
+
+        ``ln=(gamma, beta, eps)``: the product reads LayerNorm(x) instead of x.
+        ``kv=(k_pool, v_pool, slot_of, start_pos, q_cols, tq)``: output
+        features from ``q_cols`` on are appended to the KV pools
+        [slots, heads, max_seq, head_dim] at (slot_of[b], start_pos[b] + t).
+        ``ar_ctx``: a ``neb_ar`` context; out = residual + SUM over the TP
+        group of this product (every rank calls in the same order).
+        """
+        m = x.shape[0] if rows is None else rows
+        fz = _native.neb_fusion()
+        if ln is not None:
+            g, b, eps = ln
+            fz.ln_gamma, fz.ln_beta, fz.ln_eps = g.data_ptr(), b.data_ptr(), float(eps)
+        if kv is not None:
+            kp, vp, slots, starts, q_cols, tq = kv
+            fz.k_pool, fz.v_pool = kp.data_ptr(), vp.data_ptr()
+            fz.slot_of, fz.start_pos = slots.data_ptr(), starts.data_ptr()
+            fz.q_cols, fz.tq = int(q_cols), int(tq)
+            fz.kv_heads, fz.max_seq, fz.head_dim = kp.shape[1], kp.shape[2], kp.shape[3]
+        if ar_ctx is not None:
+            fz.ar_ctx = ar_ctx
+        _native.call(
+            "neb_linear_fused", x.data_ptr(), x.stride(0), self.ptr, self.n, self.k,
+            residual.data_ptr() if residual is not None else None,
+            residual.stride(0) if residual is not None else 0, out.data_ptr(), out.stride(0), m, self.code, act,
+            ctypes.byref(fz), _native.stream_ptr(x.device),
+        )
+        return out

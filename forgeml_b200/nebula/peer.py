@@ -45,6 +45,11 @@ class PeerAllReduce:
             self.close()
             raise
 
+    @property
+    def handle(self) -> int | None:
+        """The native context pointer (for the fused GEMM all-reduce epilogue)."""
+        return None if self._ctx is None else self._ctx.value
+
     def fits(self, t: torch.Tensor) -> bool:
         nbytes = t.numel() * t.element_size()
         return (self._ctx is not None and t.is_cuda and t.is_contiguous() and t.dtype in _DTYPES

@@ -6,7 +6,16 @@ start_pos], ids, tokens; SHA-256 config handshake; cache preflight agreed by
 a MAX all-reduce; poisoning on any failure -- runtime.py:19-27,192-516).
 
 The decoder runs every layer on native kernels (no torch compute on the hot
-path):
+path).  A layer of at most 32 tokens (every decode step of configs 4 and 5)
+runs as fused launches of the tcgen05 GEMM (neb_linear_fused) plus the
+attention kernel:
+
+  LN1 + QKV GEMM + KV append -> attention -> o GEMM (+ TP all-reduce) + residual
+  -> LN2 + up GEMM + tanh-GELU -> down GEMM (+ TP all-reduce) + residual
+
+with the LayerNorm computed in the GEMM prologue, the K/V columns written
+into the pools by the GEMM epilogue, and (TP > 1) the partials exchanged over
+NVLink from the GEMM epilogue.  Larger steps (prefill) run the unfused chain:
 
   LN -> fused QKV GEMM (one [3*h_local*hd, h] weight per rank)
      -> KV append into the slot pool -> attention over the pool (no prefix copy)
@@ -28,6 +37,7 @@ from __future__ import annotations
 import contextlib
 import ctypes
 import hashlib
+import os
 import threading
 from dataclasses import asdict
 
@@ -222,14 +232,55 @@ class ShardedDecoder(nn.Module):
         self._peer_ar = None
         if context.tp_size > 1 and dev.type == "cuda" and peer.enabled():
             es = torch.empty((), dtype=dtype).element_size()
-            slot = max(16, (max_requests * h * es + 15) // 16 * 16)
+            slot = max(16, (max(max_requests, 32) * h * es + 15) // 16 * 16)
             self._peer_ar = peer.PeerAllReduce(context, max_bytes=slot)
+        self._fused_cache: dict[int, bool] = {}
 
     # ------------------------------------------------------------------ math
+    def _fused_ok(self, bt: int) -> bool:
+        """Whether a layer of ``bt`` tokens runs as the fused launches
+        (LN+QKV+KV append, o+all-reduce, LN+up+GELU, down+all-reduce)."""
+        ok = self._fused_cache.get(bt)
+        if ok is None:
+            ctx = self.context
+            L = self.layers[0] if self.layers else None
+            ok = (L is not None and fused_enabled() and bt <= 32 and self.dtype in (torch.bfloat16, torch.float16)
+                  and self.config.hidden_size % 64 == 0
+                  and all(isinstance(g, PackedLinear) and g.fused_ok(bt) for g in (L.qkv, L.o, L.up, L.down))
+                  and (ctx.tp_size == 1 or (self._peer_ar is not None and self.config.hidden_size % 16 == 0
+                                            and self.config.hidden_size * 64 <= self._peer_ar.max_bytes)))
+            self._fused_cache[bt] = ok
+        return ok
+
+    def _layer_fused(self, L: _Layer, lid: int, x: torch.Tensor, b: int, t: int, slots: torch.Tensor,
+                     starts: torch.Tensor) -> torch.Tensor:
+        bt = b * t
+        h = self.config.hidden_size
+        hl, hd, hl_hd = self.num_heads_local, self.head_dim, self._hl_hd
+        dev = x.device
+        kp, vp = self.cache.k_pool[lid], self.cache.v_pool[lid]
+        q = L.qkv.fused(x, torch.empty((bt, hl_hd), dtype=self.dtype, device=dev), ln=(L.ln1_w, L.ln1_b, 1e-5),
+                        kv=(kp, vp, slots, starts, hl_hd, t))
+        attn = ops.attention(q.view(b, t, hl, hd), kp, vp, slots, starts).view(bt, hl_hd)
+        if self.context.tp_size == 1:  # residual add in the plain epilogue
+            x = L.o(attn, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x)
+        else:
+            x = L.o.fused(attn, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x,
+                          ar_ctx=self._peer_ar.handle)
+        mid = L.up.fused(x, torch.empty((bt, L.wup.shape[0]), dtype=self.dtype, device=dev),
+                         act=_native.ACT_GELU_TANH, ln=(L.ln2_w, L.ln2_b, 1e-5))
+        if self.context.tp_size == 1:
+            return L.down(mid, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x)
+        return L.down.fused(mid, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x,
+                            ar_ctx=self._peer_ar.handle)
+
     def _layer(self, L: _Layer, lid: int, x: torch.Tensor, b: int, t: int, slots: torch.Tensor,
                starts: torch.Tensor) -> torch.Tensor:
         ctx = self.context
         bt = b * t
+        if self._fused_ok(bt):
+            with record_function("nebula::layer_fused"):
+                return self._layer_fused(L, lid, x, b, t, slots, starts)
         h = self.config.hidden_size
         hl, hd, hl_hd = self.num_heads_local, self.head_dim, self._hl_hd
         dev = x.device
@@ -374,6 +425,12 @@ class ShardedDecoder(nn.Module):
         if self._peer_ar is not None:
             self._peer_ar.close()
             self._peer_ar = None
+
+
+def fused_enabled() -> bool:
+    """Decode layers run as fused launches unless FORGEML_FUSED_DECODE=0 (a
+    diagnostic switch: the unfused chain computes the same step)."""
+    return os.environ.get("FORGEML_FUSED_DECODE", "1") != "0"
 
 
 def _validate_prompt(config: DecoderConfig, prompt: list[int], max_new: int) -> None:

@@ -253,6 +253,51 @@ FML_API int neb_ar_all_reduce(void* ctx, const void* part, const void* residual,
 FML_API int neb_ar_destroy(void* ctx);
 
 /* ---------------------------------------------------------------------------
+ * Fused decode linear: one launch for each of the decode step's chains
+ *   LN -> QKV linear -> KV append        (src/nebula/runtime.py:130-138, cache.py:161-165)
+ *   o linear -> SUM all-reduce -> + x    (runtime.py:145-146, parallel.py:112-116)
+ *   LN -> up linear -> GELU              (runtime.py:151-152)
+ *   down linear -> SUM all-reduce -> + x (runtime.py:153-154)
+ * on a packed weight (fml_pack_weight), for M <= 32 tokens.  Same results as
+ * the unfused chain (fml_layernorm, fml_linear_packed, neb_kv_append,
+ * neb_ar_all_reduce) up to the LayerNorm statistics, which are summed in a
+ * different order.
+ *   LayerNorm prologue (ln_gamma != NULL): the GEMM reads LN(x) over x's k
+ *     columns (eps ln_eps, ln_beta required); k a multiple of 64.
+ *   KV epilogue (k_pool != NULL): output features [0, q_cols) go to out (row
+ *     stride ldo >= q_cols); features q_cols + [0, kv_heads*head_dim) go to
+ *     K and the next kv_heads*head_dim to V, at pool[slot_of[b], head,
+ *     start_pos[b] + t, d] for token m = b*tq + t (pools [slots, kv_heads,
+ *     max_seq, head_dim]); an out-of-range position raises bit 4 of
+ *     fml_device_status() like neb_kv_append.  n = q_cols + 2*kv_heads*head_dim.
+ *   All-reduce epilogue (ar_ctx != NULL, a neb_ar context opened on every TP
+ *     rank): out = round(round(sum over ranks in rank order) + residual),
+ *     exchanged in 16-feature sub-blocks over NVLink from the GEMM epilogue;
+ *     every rank calls with the same n and m in the same order; n a multiple
+ *     of 16 with n * 64 <= the context's max_bytes; act must be 0; not
+ *     combined with the KV epilogue.  A peer wait beyond the context's timeout
+ *     raises bit 32 of fml_device_status().
+ * ------------------------------------------------------------------------- */
+typedef struct neb_fusion {
+  const void* ln_gamma;
+  const void* ln_beta;
+  float ln_eps;
+  void* k_pool;
+  void* v_pool;
+  const int32_t* slot_of;
+  const int32_t* start_pos;
+  int32_t q_cols, kv_heads, head_dim, max_seq, tq;
+  void* ar_ctx;
+} neb_fusion;
+
+FML_API int neb_linear_fused(const void* x, int64_t ldx, const void* packed, int64_t n, int64_t k,
+                             const void* residual, int64_t ldr, void* out, int64_t ldo, int64_t m,
+                             int dtype, int act, const neb_fusion* fusion, void* stream);
+/* 1 if neb_linear_fused covers an [m x k] x [n x k]^T product on this device
+ * (16-bit, m <= 32, every output tile resident at once), else 0. */
+FML_API int neb_linear_fused_ok(int64_t n, int64_t k, int64_t m, int dtype);
+
+/* ---------------------------------------------------------------------------
  * Diagnostics.
  * ------------------------------------------------------------------------- */
 /* Message for the last nonzero return on this thread ("" if none). */

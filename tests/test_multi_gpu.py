@@ -197,3 +197,103 @@ def test_peer_all_reduce_2_fp32():
 
 def test_peer_all_reduce_8_bf16():
     _run_ar(8, "bfloat16")
+
+
+def _far_worker(rank, world, store):
+    """Row-parallel linear with the all-reduce fused into the GEMM epilogue:
+    every rank holds its own K slice of x and W; the result must equal the
+    rank-ordered fp32 sum of the ranks' rounded partials (each partial computed
+    by the same kernel without the exchange), rounded, plus the residual."""
+    import os
+
+    from forgeml_b200 import _native
+    from forgeml_b200.linear import PackedLinear
+    from forgeml_b200.nebula import ParallelContext
+    from forgeml_b200.nebula.peer import PeerAllReduce
+
+    os.environ["LOCAL_RANK"] = str(rank)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"file://{store}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    ctx = ParallelContext.from_env(tp_size=world, pp_size=1, device="cuda", timeout_s=60)
+    dev = ctx.device
+    bf = torch.bfloat16
+    ar = PeerAllReduce(ctx, max_bytes=4096 * 64)
+    try:
+        for it, (n, k_total, m) in enumerate(((2048, 2048, 32), (2048, 8192, 32), (4096, 4096, 7), (2048, 2048, 1))):
+            k = k_total // world
+            g = torch.Generator().manual_seed(100 * it + rank)
+            w = (torch.randn(n, k, generator=g) * 0.02).to(bf).to(dev)
+            x = torch.randn(m, k, generator=g).to(bf).to(dev)
+            res = torch.randn(m, n, generator=torch.Generator().manual_seed(9 + it)).to(bf).to(dev)  # same on all ranks
+            lin = PackedLinear(w)
+            assert lin.fused_ok(m)
+            part = lin.fused(x, torch.empty(m, n, dtype=bf, device=dev)).cpu()
+            parts = [None] * world
+            dist.all_gather_object(parts, part)
+            acc = torch.zeros(m, n, dtype=torch.float32)
+            for p in parts:  # rank order, fp32
+                acc += p.float()
+            want = (acc.to(bf).float() + res.cpu().float()).to(bf)
+            for _ in range(2):
+                got = lin.fused(x, torch.empty(m, n, dtype=bf, device=dev), residual=res, ar_ctx=ar.handle)
+                assert torch.equal(got.cpu(), want), f"rank {rank} case {it}"
+            got = lin.fused(x, torch.empty(m, n, dtype=bf, device=dev), ar_ctx=ar.handle)
+            assert torch.equal(got.cpu(), acc.to(bf))
+        # CUDA-graph replay (epochs advance on the device)
+        n, k, m = 2048, 2048 // world, 32
+        w = torch.zeros((n, k), dtype=bf, device=dev)
+        w[:, 0] = 1.0
+        x = torch.zeros(m, k, dtype=bf, device=dev)
+        x[:, 0] = float(rank + 1)
+        lin = PackedLinear(w)
+        res = torch.ones(m, n, dtype=bf, device=dev)
+        out = torch.empty(m, n, dtype=bf, device=dev)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            lin.fused(x, out, residual=res, ar_ctx=ar.handle)
+        torch.cuda.current_stream().wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            lin.fused(x, out, residual=res, ar_ctx=ar.handle)
+        for _ in range(5):
+            out.zero_()
+            graph.replay()
+            torch.cuda.synchronize()
+            assert torch.all(out.float() == 1 + world * (world + 1) / 2)
+        del graph
+        assert _native.device_status() == 0
+    finally:
+        ar.close()
+        torch.cuda.synchronize()
+        dist.barrier()
+        ctx.close()
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _run_far(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    with tempfile.TemporaryDirectory() as d:
+        procs = mp.start_processes(_far_worker, args=(world, f"{d}/store"), nprocs=world, join=False,
+                                   start_method="spawn")
+        deadline = time.time() + 180
+        while time.time() < deadline and not all(p.exitcode is not None for p in procs.processes):
+            time.sleep(0.2)
+        for p in procs.processes:
+            if p.is_alive():
+                p.terminate()
+        for p in procs.processes:
+            p.join()
+        assert [p.exitcode for p in procs.processes] == [0] * world
+
+
+def test_fused_all_reduce_linear_2():
+    _run_far(2)
+
+
+def test_fused_all_reduce_linear_8():
+    _run_far(8)
