@@ -703,17 +703,18 @@ extern "C" int neb_attention(const void* q, const int64_t q_strides[4], const vo
   if (head_dim > attn::kMaxD) return fail(FML_EUNSUPPORTED, "neb_attention: head_dim > 256");
   if (q_strides[3] != 1) return fail(FML_EUNSUPPORTED, "neb_attention: q innermost stride must be 1");
   if (batch * t * heads * 8 > (1ll << 31) - 1) return fail(FML_EUNSUPPORTED, "neb_attention: too many queries");
-  // Key splits per query (combined in a cluster of at most 8): enough CTAs
-  // for two per SM (the bulk-copy pipeline keeps 96 KB in flight per CTA),
-  // but no more, so each CTA streams a long run of keys; measured on B200,
-  // more and shorter CTAs lose to their per-CTA start-up.  Depends only on
-  // the launch shape (not on the device-side positions), so a captured
-  // decode step keeps a valid split.
+  // Key splits per query (combined in a cluster of at most 8): as many as
+  // keep every CTA of the launch resident at once (two per SM: the bulk-copy
+  // pipeline keeps 96 KB in flight per CTA), so each CTA streams a long run
+  // of keys and no split spills into a second wave; measured on B200, more
+  // and shorter CTAs lose to their per-CTA start-up.  Depends only on the
+  // launch shape (not on the device-side positions), so a captured decode
+  // step keeps a valid split.
   const long long nq = batch * t * heads;
   const char* tune = getenv("FORGEML_NEB_ATTN_CTAS_PER_SM");  // tuning override
   const long long target_per_sm = (tune && atoll(tune) > 0) ? atoll(tune) : 2LL;
   const long long target = target_per_sm * num_sms(current_device());
-  int nsplit = (int)std::min<long long>(8, std::max<long long>(1, (target + nq - 1) / nq));
+  int nsplit = (int)std::min<long long>(8, std::max<long long>(1, target / nq));
   nsplit = (int)std::min<long long>(nsplit, std::max<long long>(1, max_seq / 64));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == FML_F32)

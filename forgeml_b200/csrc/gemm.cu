@@ -276,6 +276,143 @@ __device__ __forceinline__ bool epilogue_row32_fast(const Params& p, int m, int 
   return true;
 }
 
+__device__ __forceinline__ float h2f(uint32_t v, bool bf) {
+  return bf ? __uint_as_float((v & 0xffffu) << 16) : __half2float(__ushort_as_half((unsigned short)(v & 0xffffu)));
+}
+__device__ __forceinline__ uint32_t f2h(float v, bool bf) {
+  return bf ? (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v))
+            : (uint32_t)__half_as_ushort(__float2half_rn(v));
+}
+__device__ __forceinline__ void unpack8(const uint4& r, bool bf, float (&v)[8]) {
+  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = h2f(w[i], bf);
+    v[2 * i + 1] = h2f(w[i] >> 16, bf);
+  }
+}
+// Epilogue value of output (m, n) from the fp32 accumulator v: the same
+// contract as epilogue_store, without the store.
+__device__ __forceinline__ float epilogue_value(const Params& p, int m, int n, float v) {
+  const int od = p.out_dtype;
+  float x = round_to(v, od);
+  if (p.bias != nullptr) {
+    float b;
+    if (od == FML_F32) b = reinterpret_cast<const float*>(p.bias)[n * p.bias_stride];
+    else if (od == FML_BF16) b = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.bias)[n * p.bias_stride]);
+    else b = __half2float(reinterpret_cast<const __half*>(p.bias)[n * p.bias_stride]);
+    x = round_to(x + b, od);
+  }
+  if (p.act == FML_ACT_GELU_ERF) x = gelu_erf(x);
+  else if (p.act == FML_ACT_GELU_TANH) x = gelu_tanh(x);
+  if (p.residual != nullptr) {
+    const long long roff = (long long)m * p.ldr + n;
+    float r;
+    if (od == FML_F32) r = reinterpret_cast<const float*>(p.residual)[roff];
+    else if (od == FML_BF16) r = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.residual)[roff]);
+    else r = __half2float(reinterpret_cast<const __half*>(p.residual)[roff]);
+    x = round_to(x, od) + r;
+  }
+  return x;
+}
+
+__device__ __forceinline__ float ld_shared_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// Sum of the split-K partials of eight outputs: element e of source CTA r at
+// shared address red + r * src_stride + e * e_stride (bytes), added in
+// source order.  All loads of one source are independent; the values stay in
+// registers (compile-time indices only).
+__device__ __forceinline__ void red_sum8(uint32_t red, int src_stride, int e_stride, int nsrc, float (&v)[8]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = 0.f;
+  for (int r = 0; r < nsrc; ++r) {
+    float t[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) t[e] = ld_shared_f32(red + (uint32_t)(r * src_stride + e * e_stride));
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] += t[e];
+  }
+}
+
+__device__ __forceinline__ uint4 pack8_16(const float (&x)[8], bool bf) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (bf) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&h);
+    } else {
+      __half2 h = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Eight consecutive outputs (m, n0..n0+7) from the split-K buffer with the
+// epilogue contract of epilogue_store.  16-bit outputs with 16-byte aligned
+// rows take a straight-line path: round, bias, GELU, residual (one 16-byte
+// load) and one 16-byte store; GELU runs in a rolled loop that rotates the
+// eight registers (one copy of its code, nothing indexed dynamically, so
+// nothing goes to local memory).  Other cases store element by element.
+__device__ __forceinline__ void epilogue_store8(const Params& p, int m, int n0, uint32_t red, int src_stride,
+                                                int e_stride, int nsrc) {
+  if (m >= p.rows_out || n0 >= p.cols_out) return;
+  float x[8];
+  red_sum8(red, src_stride, e_stride, nsrc, x);
+  const int od = p.out_dtype;
+  const long long off = (long long)m * p.ldo + n0;
+  const long long roff = (long long)m * p.ldr + n0;
+  const bool vec = od != FML_F32 && n0 + 8 <= p.cols_out && (off & 7) == 0 &&
+                   (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 &&
+                   (p.residual == nullptr || ((roff & 7) == 0 && (reinterpret_cast<uintptr_t>(p.residual) & 15) == 0));
+  if (!vec) {
+#pragma unroll 1
+    for (int e = 0; e < 8; ++e) {
+      const float v = x[0];
+#pragma unroll
+      for (int i = 0; i < 7; ++i) x[i] = x[i + 1];
+      if (n0 + e < p.cols_out) {
+        const float y = epilogue_value(p, m, n0 + e, v);
+        if (od == FML_F32) reinterpret_cast<float*>(p.out)[off + e] = y;
+        else if (od == FML_BF16) reinterpret_cast<__nv_bfloat16*>(p.out)[off + e] = __float2bfloat16_rn(y);
+        else reinterpret_cast<__half*>(p.out)[off + e] = __float2half_rn(y);
+      }
+    }
+    return;
+  }
+  const bool bf = od == FML_BF16;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) x[e] = round_to(x[e], od);
+  if (p.bias != nullptr) {
+    const uint16_t* bb = reinterpret_cast<const uint16_t*>(p.bias);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] = round_to(x[e] + h2f(bb[(long long)(n0 + e) * p.bias_stride], bf), od);
+  }
+  if (p.act != FML_ACT_NONE) {
+    const bool erf_act = p.act == FML_ACT_GELU_ERF;
+#pragma unroll 1
+    for (int e = 0; e < 8; ++e) {
+      const float g = erf_act ? gelu_erf(x[0]) : gelu_tanh(x[0]);
+#pragma unroll
+      for (int i = 0; i < 7; ++i) x[i] = x[i + 1];
+      x[7] = g;
+    }
+  }
+  if (p.residual != nullptr) {
+    const uint4 rv = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.residual) + roff);
+    float r[8];
+    unpack8(rv, bf, r);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] = round_to(x[e], od) + r[e];
+  }
+  *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + off) = pack8_16(x, bf);
+}
+
 // ---------------------------------------------------------------------------
 // Fused decode linear (FUSED kernels).  Nebula's decode step chains
 //   LayerNorm -> QKV GEMM -> KV append            (src/nebula/runtime.py:130-138)
@@ -301,21 +438,6 @@ __host__ __device__ constexpr int aux_bytes(int bn) {
   return aux_stage(bn) + 128 * peer::kSubTokens * 2;
 }
 
-__device__ __forceinline__ float h2f(uint32_t v, bool bf) {
-  return bf ? __uint_as_float((v & 0xffffu) << 16) : __half2float(__ushort_as_half((unsigned short)(v & 0xffffu)));
-}
-__device__ __forceinline__ uint32_t f2h(float v, bool bf) {
-  return bf ? (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v))
-            : (uint32_t)__half_as_ushort(__float2half_rn(v));
-}
-__device__ __forceinline__ void unpack8(const uint4& r, bool bf, float (&v)[8]) {
-  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    v[2 * i] = h2f(w[i], bf);
-    v[2 * i + 1] = h2f(w[i] >> 16, bf);
-  }
-}
 __device__ __forceinline__ void st_async_v2(uint32_t addr, float a, float b, uint32_t mbar) {
   asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(addr),
                "f"(a), "f"(b), "r"(mbar)
@@ -474,13 +596,19 @@ __device__ bool ln_prologue(const Params& p, const Smem& s, int ksplit, uint32_t
   return ok;
 }
 
-// KV-append epilogue for one output element: feature n (>= kv_q_cols) of
-// token m goes to pool[slot_of[b], head, start_pos[b] + t, d] of the K or V
-// pool (m = b * tq + t), rounded to the 16-bit dtype like the GEMM output it
-// replaces (src/nebula/cache.py:161-165 via runtime.py:136-138).
-__device__ __forceinline__ void kv_store(const Params& p, int n, int m, float v) {
-  if (n >= p.cols_out || m >= p.J) return;
-  const int nn = n - p.kv_q_cols;
+// KV-append epilogue: output features n >= kv_q_cols of token m go to
+// pool[slot_of[b], head, start_pos[b] + t, d] of the K or V pool
+// (m = b * tq + t), rounded to the 16-bit dtype like the GEMM output they
+// replace (src/nebula/cache.py:161-165 via runtime.py:136-138); a position
+// out of range raises DEV_ERR_ATTN_RANGE like neb_kv_append.
+// Eight consecutive features n0..n0+7 of token m (one head, same K or V
+// pool: q_cols and head_dim are multiples of 8) as one 16-byte store.
+__device__ __forceinline__ void kv_store8(const Params& p, int n0, int m, uint32_t red, int src_stride,
+                                          int e_stride, int nsrc) {
+  if (n0 >= p.cols_out || m >= p.J) return;
+  float x[8];
+  red_sum8(red, src_stride, e_stride, nsrc, x);
+  const int nn = n0 - p.kv_q_cols;
   const bool is_v = nn >= p.kv_cols;
   const int c = is_v ? nn - p.kv_cols : nn;
   const int head = c / p.kv_hd, d = c - head * p.kv_hd;
@@ -493,7 +621,10 @@ __device__ __forceinline__ void kv_store(const Params& p, int n, int m, float v)
   }
   const long long dst = (((long long)slot * p.kv_heads + head) * p.kv_max_seq + pos) * p.kv_hd + d;
   uint16_t* pool = static_cast<uint16_t*>(is_v ? p.kv_v : p.kv_k);
-  pool[dst] = (uint16_t)f2h(v, p.fmt == 1);
+  *reinterpret_cast<uint4*>(pool + dst) = pack8_16(x, p.fmt == 1);
+}
+__device__ __forceinline__ void st_shared_u16(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"((unsigned short)v) : "memory");
 }
 
 // All-reduce epilogue of one owner CTA: its rows_per features (rows r0.. of
@@ -857,8 +988,10 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
     };
     // FUSED kernels always reduce through the split-K buffer (also with one
     // CTA per tile), where the KV and all-reduce epilogues take over.
+    // Narrow swapped tiles (the decode linears) also store through it: eight
+    // outputs per thread as one vector instead of 32 scattered 2-byte stores.
     constexpr bool kRedAlways = FUSED;
-    const bool use_red = ksplit > 1 || kRedAlways;
+    const bool use_red = ksplit > 1 || kRedAlways || (BN <= 32 && p.swap);
     if constexpr (FUSED) {
       if (p.ln_x != nullptr && cluster_id < p.num_tiles)
         ok = epi_bar_and(ln_prologue<BN>(p, s, ksplit, crank, kb_begin, kb_end, ep_tid));
@@ -937,44 +1070,47 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
           // every thread must leave together: the exchange below has barriers
           const bool got = ksplit == 1 || mbar_wait_cluster(bar_recv(s), 0, DEV_ERR_REDUCE_TIMEOUT);
           if (!epi_bar_and(got)) { ok = false; break; }
-        } else if (!mbar_wait_cluster(bar_recv(s), 0, DEV_ERR_REDUCE_TIMEOUT)) {
+        } else if (ksplit > 1 && !mbar_wait_cluster(bar_recv(s), 0, DEV_ERR_REDUCE_TIMEOUT)) {
           ok = false;
           break;
         }
         const int r0 = crank * rows_per;
-        constexpr int kGroups = BN / 4 > 0 ? BN / 4 : 1;  // 4-column groups per row
-        const int items = rows_per * kGroups;
+        // Items of eight consecutive output columns of one output row.  swap:
+        // output row = token (MMA column c), columns = features (MMA rows
+        // rr0..rr0+7), consecutive threads on consecutive tokens (conflict-
+        // free reads of the buffer); otherwise one MMA row, eight columns.
+        const int src_stride = rows_per * p.red_stride * 4;  // bytes between source CTAs' slices
+        const int row_bytes = p.red_stride * 4;
+        const int items = p.swap ? (rows_per / 8) * BN : rows_per * (BN / 8);
         for (int idx = ep_tid; idx < items; idx += 128) {
-          // swap: consecutive threads take consecutive rows (output columns) so
-          // the stores coalesce; otherwise consecutive column groups.
-          int rr, cg;
-          if (p.swap) { rr = idx % rows_per; cg = idx / rows_per; }
-          else { rr = idx / kGroups; cg = idx % kGroups; }
-          float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int r = 0; r < ksplit; ++r) {
-            const float4 v = *reinterpret_cast<const float4*>(red + (r * rows_per + rr) * p.red_stride + 4 * cg);
-            sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
-          }
-          const float quad4[4] = {sum.x, sum.y, sum.z, sum.w};
+          int rr0, c0;
+          if (p.swap) { c0 = idx % BN; rr0 = (idx / BN) * 8; }
+          else { rr0 = idx / (BN / 8); c0 = (idx % (BN / 8)) * 8; }
+          const uint32_t base = s.red + (uint32_t)((rr0 * p.red_stride + c0) * 4);
           if constexpr (FUSED) {
-            // MMA row = output feature, column = token (swapped form)
-            const int n = ti * kBM + r0 + rr;
-            const bool bf = p.fmt == 1;
+            const int n0 = ti * kBM + r0 + rr0;  // first feature (the fused kernels are swapped)
+            const int m = tj * BN + c0;
             if (p.ar_on) {
               // rounded partial -> staging block [feature][token] for the exchange
-              st_shared_u2(s.aux + aux_stage(BN) + (uint32_t)((rr * peer::kSubTokens + 4 * cg) * 2),
-                           f2h(sum.x, bf) | (f2h(sum.y, bf) << 16), f2h(sum.z, bf) | (f2h(sum.w, bf) << 16));
+              const bool bf = p.fmt == 1;
+              float x[8];
+              red_sum8(base, src_stride, row_bytes, ksplit, x);
+#pragma unroll
+              for (int e = 0; e < 8; ++e)
+                st_shared_u16(s.aux + aux_stage(BN) + (uint32_t)(((rr0 + e) * peer::kSubTokens + c0) * 2), f2h(x[e], bf));
               continue;
             }
-            if (p.kv_k != nullptr && n >= p.kv_q_cols) {
-#pragma unroll 1
-              for (int e = 0; e < 4; ++e) kv_store(p, n, tj * BN + 4 * cg + e, quad4[e]);
+            if (p.kv_k != nullptr && n0 >= p.kv_q_cols) {
+              kv_store8(p, n0, m, base, src_stride, row_bytes, ksplit);
               continue;
             }
+            epilogue_store8(p, m, n0, base, src_stride, row_bytes, ksplit);
+            continue;
           }
-#pragma unroll 1
-          for (int e = 0; e < 4; ++e) epilogue_store(p, ti * kBM + r0 + rr, tj * BN + 4 * cg + e, quad4[e]);
+          if (p.swap) epilogue_store8(p, tj * BN + c0, ti * kBM + r0 + rr0, base, src_stride, row_bytes, ksplit);
+          else epilogue_store8(p, ti * kBM + r0 + rr0, tj * BN + c0, base, src_stride, 4, ksplit);
         }
+        if (ksplit == 1) epi_bar_sync();  // the buffer is refilled by this CTA's next tile
         if constexpr (FUSED) {
           if (p.ar_on && !ar_exchange<BN>(p, s, ti, r0, rows_per, ep_tid)) ok = false;
         }
@@ -1213,7 +1349,7 @@ static int smem_bytes_for(int bn, int stages, int ksplit, int* red_stride, int s
   int stage_bytes = slabs * (kBM + (pair ? bn / 2 : bn)) * kSlab;
   int rs = bn + 4;
   if (red_stride) *red_stride = rs;
-  int red = (ksplit > 1 || fused) ? kBM * rs * 4 + 16 : 0;
+  int red = (ksplit > 1 || fused || bn <= 32) ? kBM * rs * 4 + 16 : 0;  // narrow swapped tiles store through it
   return 1024 + stages * stage_bytes + kBarBytes + 16 + red + (fused ? aux_bytes(bn) : 0);
 }
 
@@ -1789,6 +1925,9 @@ extern "C" int neb_linear_fused(const void* x, int64_t ldx, const void* packed, 
         m % fu->tq != 0 || (long long)fu->q_cols + 2LL * fu->kv_heads * fu->head_dim != n)
       return fail(FML_EINVAL, "linear_fused: KV epilogue shape (n must be q_cols + 2*kv_heads*head_dim)");
     if (ldo < fu->q_cols) return fail(FML_EINVAL, "linear_fused: ldo < q_cols");
+    if (fu->q_cols % 8 != 0 || fu->head_dim % 8 != 0 || reinterpret_cast<uintptr_t>(fu->k_pool) % 16 ||
+        reinterpret_cast<uintptr_t>(fu->v_pool) % 16)
+      return fail(FML_EUNSUPPORTED, "linear_fused: KV epilogue needs q_cols and head_dim multiples of 8, aligned pools");
     if (ar) return fail(FML_EUNSUPPORTED, "linear_fused: the KV and all-reduce epilogues do not combine");
     fz.kv_k = fu->k_pool;
     fz.kv_v = fu->v_pool;

@@ -8,14 +8,14 @@ a MAX all-reduce; poisoning on any failure -- runtime.py:19-27,192-516).
 The decoder runs every layer on native kernels (no torch compute on the hot
 path).  A layer of at most 32 tokens (every decode step of configs 4 and 5)
 runs as fused launches of the tcgen05 GEMM (neb_linear_fused) plus the
-attention kernel:
+attention and LayerNorm kernels:
 
-  LN1 + QKV GEMM + KV append -> attention -> o GEMM (+ TP all-reduce) + residual
-  -> LN2 + up GEMM + tanh-GELU -> down GEMM (+ TP all-reduce) + residual
+  LN1 -> QKV GEMM + KV append -> attention -> o GEMM (+ TP all-reduce) + residual
+  -> LN2 -> up GEMM + tanh-GELU -> down GEMM (+ TP all-reduce) + residual
 
-with the LayerNorm computed in the GEMM prologue, the K/V columns written
-into the pools by the GEMM epilogue, and (TP > 1) the partials exchanged over
-NVLink from the GEMM epilogue.  Larger steps (prefill) run the unfused chain:
+with the K/V columns written into the pools by the GEMM epilogue and (TP > 1)
+the partials exchanged over NVLink from the GEMM epilogue; the LayerNorms can
+also run in the GEMM prologue (FORGEML_FUSED_LN=1).  Larger steps (prefill) run the unfused chain:
 
   LN -> fused QKV GEMM (one [3*h_local*hd, h] weight per rank)
      -> KV append into the slot pool -> attention over the pool (no prefix copy)
@@ -259,16 +259,26 @@ class ShardedDecoder(nn.Module):
         hl, hd, hl_hd = self.num_heads_local, self.head_dim, self._hl_hd
         dev = x.device
         kp, vp = self.cache.k_pool[lid], self.cache.v_pool[lid]
-        q = L.qkv.fused(x, torch.empty((bt, hl_hd), dtype=self.dtype, device=dev), ln=(L.ln1_w, L.ln1_b, 1e-5),
-                        kv=(kp, vp, slots, starts, hl_hd, t))
+        fuse_ln = fused_ln_enabled()
+        if fuse_ln:
+            q = L.qkv.fused(x, torch.empty((bt, hl_hd), dtype=self.dtype, device=dev), ln=(L.ln1_w, L.ln1_b, 1e-5),
+                            kv=(kp, vp, slots, starts, hl_hd, t))
+        else:
+            h1 = _ln(x, L.ln1_w, L.ln1_b, torch.empty_like(x), bt)
+            q = L.qkv.fused(h1, torch.empty((bt, hl_hd), dtype=self.dtype, device=dev),
+                            kv=(kp, vp, slots, starts, hl_hd, t))
         attn = ops.attention(q.view(b, t, hl, hd), kp, vp, slots, starts).view(bt, hl_hd)
         if self.context.tp_size == 1:  # residual add in the plain epilogue
             x = L.o(attn, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x)
         else:
             x = L.o.fused(attn, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x,
                           ar_ctx=self._peer_ar.handle)
-        mid = L.up.fused(x, torch.empty((bt, L.wup.shape[0]), dtype=self.dtype, device=dev),
-                         act=_native.ACT_GELU_TANH, ln=(L.ln2_w, L.ln2_b, 1e-5))
+        if fuse_ln:
+            mid = L.up.fused(x, torch.empty((bt, L.wup.shape[0]), dtype=self.dtype, device=dev),
+                             act=_native.ACT_GELU_TANH, ln=(L.ln2_w, L.ln2_b, 1e-5))
+        else:
+            h2 = _ln(x, L.ln2_w, L.ln2_b, torch.empty_like(x), bt)
+            mid = L.up(h2, torch.empty((bt, L.wup.shape[0]), dtype=self.dtype, device=dev), act=_native.ACT_GELU_TANH)
         if self.context.tp_size == 1:
             return L.down(mid, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x)
         return L.down.fused(mid, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x,
@@ -431,6 +441,14 @@ def fused_enabled() -> bool:
     """Decode layers run as fused launches unless FORGEML_FUSED_DECODE=0 (a
     diagnostic switch: the unfused chain computes the same step)."""
     return os.environ.get("FORGEML_FUSED_DECODE", "1") != "0"
+
+
+def fused_ln_enabled() -> bool:
+    """LayerNorm inside the QKV / up GEMM prologue (FORGEML_FUSED_LN=1).  Off
+    by default: measured on B200 the prologue (statistics exchange, then a
+    second read of x, gamma and beta) lengthens the GEMM's critical path by
+    more than the separate LayerNorm launch costs in the PDL chain."""
+    return os.environ.get("FORGEML_FUSED_LN", "0") == "1"
 
 
 def _validate_prompt(config: DecoderConfig, prompt: list[int], max_new: int) -> None:
