@@ -13,8 +13,9 @@ attention and LayerNorm kernels:
   LN1 -> QKV GEMM + KV append -> attention -> o GEMM (+ TP all-reduce) + residual
   -> LN2 -> up GEMM + tanh-GELU -> down GEMM (+ TP all-reduce) + residual
 
-with the K/V columns written into the pools by the GEMM epilogue and (TP > 1)
-the partials exchanged over NVLink from the GEMM epilogue; the LayerNorms can
+with the K/V columns written into the pools by the GEMM epilogue and (TP = 2)
+the partials exchanged over NVLink from the GEMM epilogue (larger TP groups use
+the standalone NVLink all-reduce kernel after the GEMM); the LayerNorms can
 also run in the GEMM prologue (FORGEML_FUSED_LN=1).  Larger steps (prefill) run the unfused chain:
 
   LN -> fused QKV GEMM (one [3*h_local*hd, h] weight per rank)
@@ -268,21 +269,26 @@ class ShardedDecoder(nn.Module):
             q = L.qkv.fused(h1, torch.empty((bt, hl_hd), dtype=self.dtype, device=dev),
                             kv=(kp, vp, slots, starts, hl_hd, t))
         attn = ops.attention(q.view(b, t, hl, hd), kp, vp, slots, starts).view(bt, hl_hd)
-        if self.context.tp_size == 1:  # residual add in the plain epilogue
+        tp = self.context.tp_size
+        if tp == 1:  # residual add in the plain epilogue
             x = L.o(attn, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x)
-        else:
+        elif fused_ar_enabled(tp):
             x = L.o.fused(attn, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x,
                           ar_ctx=self._peer_ar.handle)
+        else:
+            x = self._tp_sum_add(L.o(attn, torch.empty((bt, h), dtype=self.dtype, device=dev)), x)
         if fuse_ln:
             mid = L.up.fused(x, torch.empty((bt, L.wup.shape[0]), dtype=self.dtype, device=dev),
                              act=_native.ACT_GELU_TANH, ln=(L.ln2_w, L.ln2_b, 1e-5))
         else:
             h2 = _ln(x, L.ln2_w, L.ln2_b, torch.empty_like(x), bt)
             mid = L.up(h2, torch.empty((bt, L.wup.shape[0]), dtype=self.dtype, device=dev), act=_native.ACT_GELU_TANH)
-        if self.context.tp_size == 1:
+        if tp == 1:
             return L.down(mid, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x)
-        return L.down.fused(mid, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x,
-                            ar_ctx=self._peer_ar.handle)
+        if fused_ar_enabled(tp):
+            return L.down.fused(mid, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x,
+                                ar_ctx=self._peer_ar.handle)
+        return self._tp_sum_add(L.down(mid, torch.empty((bt, h), dtype=self.dtype, device=dev)), x)
 
     def _layer(self, L: _Layer, lid: int, x: torch.Tensor, b: int, t: int, slots: torch.Tensor,
                starts: torch.Tensor) -> torch.Tensor:
@@ -441,6 +447,19 @@ def fused_enabled() -> bool:
     """Decode layers run as fused launches unless FORGEML_FUSED_DECODE=0 (a
     diagnostic switch: the unfused chain computes the same step)."""
     return os.environ.get("FORGEML_FUSED_DECODE", "1") != "0"
+
+
+def fused_ar_enabled(tp: int) -> bool:
+    """TP all-reduce inside the o / down GEMM epilogue, or the standalone peer
+    all-reduce kernel after the GEMM.  FORGEML_FUSED_AR=1/0 forces either;
+    by default the epilogue exchange is used for two ranks and the standalone
+    kernel for more (measured on B200 at config 4: TP2 1.30 vs 1.35 ms per
+    step in favour of the epilogue, TP8 1.38 vs 1.13 ms in favour of the
+    standalone kernel)."""
+    v = os.environ.get("FORGEML_FUSED_AR")
+    if v is not None:
+        return v == "1"
+    return tp <= 2
 
 
 def fused_ln_enabled() -> bool:
