@@ -307,16 +307,16 @@ __global__ void __launch_bounds__(32 * (kBulkConsumers + 1))
     fence_mbar_init();
   }
   __syncthreads();
-  pdl_wait();
-  pdl_trigger();
-
+  // slot_of / start_pos are step inputs (never written by this library's
+  // kernels), so they may be read before waiting for the previous grid.
   const long long qidx = blockIdx.x / nsplit;
   const int split = (int)(blockIdx.x % nsplit);
   const int h = (int)(qidx % H);
   const int t = (int)((qidx / H) % tq);
   const int b = (int)(qidx / ((long long)H * tq));
   const int slot = slot_of[b];
-  const int pos = start_pos[b] + t;
+  const int first_new = start_pos[b];  // rows from here on are this step's (written by the previous grid)
+  const int pos = first_new + t;
   const bool bad = (slot < 0) || (pos < 0) || (pos >= max_seq);
   const int len = bad ? 0 : pos + 1;
   if (bad && split == 0 && threadIdx.x == 0) raise_device_error(DEV_ERR_ATTN_RANGE);
@@ -339,8 +339,18 @@ __global__ void __launch_bounds__(32 * (kBulkConsumers + 1))
     // warps have arrived on empty_bar[s].
     const uint8_t* src = reinterpret_cast<const uint8_t*>((lane & 1) ? vpool : kpool) +
                          (head_off + (long long)lo * D) * (long long)sizeof(T);
+    // Stages wholly below first_new hold keys written by earlier steps: the
+    // first of them are copied before waiting for the previous grid (the
+    // QKV projection that appends this step's rows), hiding one memory
+    // latency behind its tail.
+    int pre = 0;
+    while (pre < nst && pre < kBulkStages && lo + (pre + 1) * NK <= first_new) ++pre;
     int issued = 0;
     for (int j = 0; j < nst; ++j) {
+      if (j == pre) {
+        pdl_wait();
+        pdl_trigger();
+      }
       const int s = j % kBulkStages;
       const uint32_t bytes = (uint32_t)min(NK, hi - lo - j * NK) * RB;
       const uint32_t fb = smem_u32(&full_bar[s]);
@@ -361,7 +371,13 @@ __global__ void __launch_bounds__(32 * (kBulkConsumers + 1))
     if (lane == 0)
       for (int j = max(0, issued - kBulkStages); j < issued; ++j)
         mbar_wait(smem_u32(&full_bar[j % kBulkStages]), (j / kBulkStages) & 1, DEV_ERR_ATTN_TIMEOUT);
+    if (pre == nst) {
+      pdl_wait();
+      pdl_trigger();
+    }
   } else {
+    pdl_wait();
+    pdl_trigger();
     // Query slice of this lane, pre-scaled.
     float qv[VE];
     {

@@ -52,13 +52,25 @@ __global__ void __launch_bounds__(kWarps * 32)
     ln_vec_kernel(const T* __restrict__ x, long long xs, const T* __restrict__ g,
                   const T* __restrict__ b, float eps, T* __restrict__ y, long long ys, long long rows,
                   int cols) {
-  pdl_wait();
-  pdl_trigger();
   constexpr int W = Vec<T>::N;
   const int lane = threadIdx.x & 31;
+  const int nvec = cols / W;
+  // gamma / beta are constant weights: bring them into L2 while the
+  // previous grid finishes (they are read only after the statistics).
+  if (g != nullptr) {
+#pragma unroll
+    for (int i = 0; i < VPL_MAX; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nvec && (vi & 7) == 0) {
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(g + vi * W));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(b + vi * W));
+      }
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
   const long long row = (long long)blockIdx.x * kWarps + threadIdx.x / 32;
   if (row >= rows) return;
-  const int nvec = cols / W;
   const T* xr = x + row * xs;
   float v[VPL_MAX][W];
   float sum = 0.f;
