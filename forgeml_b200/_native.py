@@ -62,6 +62,8 @@ class neb_fusion(ctypes.Structure):
         ("ln_gamma", ctypes.c_void_p),
         ("ln_beta", ctypes.c_void_p),
         ("ln_eps", ctypes.c_float),
+        ("ln_wsum", ctypes.c_void_p),
+        ("ln_wbias", ctypes.c_void_p),
         ("k_pool", ctypes.c_void_p),
         ("v_pool", ctypes.c_void_p),
         ("slot_of", ctypes.c_void_p),

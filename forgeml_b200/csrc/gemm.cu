@@ -82,8 +82,14 @@ struct Params {
   int promote_kb;          // K slabs per TMEM chunk when partial sums are promoted to registers
   const uint8_t* p_packed; // P pre-packed as swizzled 16 KB tiles (nullptr: P comes through tmP)
   // Fused decode linear (FUSED kernels: pre-packed 16-bit weight, one tile per cluster).
-  // LayerNorm prologue: Q = LN(x) over ln_k columns, computed by the epilogue warps.
-  const void* ln_x;        // nullptr: Q comes through tmQ
+  // LayerNorm over ln_k columns of x (the Q operand), by the epilogue warps:
+  //   ln_mode 1 (prologue): Q = LN(x) written into the stages (no Q loads);
+  //   ln_mode 2 (fold): Q = x through tmQ, P = W diag(gamma) packed, and the
+  //     epilogue applies out = rstd * (acc - mean * fold_s[n]) + fold_c[n].
+  int ln_mode;
+  const float* fold_s;     // sum over k of the packed (gamma-scaled) weight row
+  const float* fold_c;     // W . beta per feature (nullptr: zero)
+  const void* ln_x;
   long long ln_ldx;
   const void* ln_g;
   const void* ln_b;
@@ -359,11 +365,8 @@ __device__ __forceinline__ uint4 pack8_16(const float (&x)[8], bool bf) {
 // load) and one 16-byte store; GELU runs in a rolled loop that rotates the
 // eight registers (one copy of its code, nothing indexed dynamically, so
 // nothing goes to local memory).  Other cases store element by element.
-__device__ __forceinline__ void epilogue_store8(const Params& p, int m, int n0, uint32_t red, int src_stride,
-                                                int e_stride, int nsrc) {
+__device__ __forceinline__ void epilogue_store8(const Params& p, int m, int n0, float (&x)[8]) {
   if (m >= p.rows_out || n0 >= p.cols_out) return;
-  float x[8];
-  red_sum8(red, src_stride, e_stride, nsrc, x);
   const int od = p.out_dtype;
   const long long off = (long long)m * p.ldo + n0;
   const long long roff = (long long)m * p.ldr + n0;
@@ -503,8 +506,8 @@ __device__ __forceinline__ bool epi_bar_and(bool v) {
 // handed to the UMMA warp like a TMA stage (one arrival on its full barrier).
 // All 128 threads run every barrier; a timed-out wait only clears the result.
 template <int BN>
-__device__ bool ln_prologue(const Params& p, const Smem& s, int ksplit, uint32_t crank, int kb_begin,
-                            int kb_end, int tid) {
+__device__ bool ln_stats(const Params& p, const Smem& s, int ksplit, uint32_t crank, int kb_begin, int kb_end,
+                         int tid) {
   constexpr int TPR = 128 / BN;  // threads per row
   const int r = tid / TPR, q = tid % TPR;
   const bool bf = p.fmt == 1;
@@ -559,7 +562,19 @@ __device__ bool ln_prologue(const Params& p, const Smem& s, int ksplit, uint32_t
     st_shared_v2(rowst + r * 8, shift + md, 1.0f / sqrtf(var + p.ln_eps));
   }
   epi_bar_sync();
-  const float2 ms = ld_shared_v2(rowst + r * 8);
+  return ok;
+}
+
+template <int BN>
+__device__ bool ln_prologue(const Params& p, const Smem& s, int ksplit, uint32_t crank, int kb_begin,
+                            int kb_end, int tid) {
+  constexpr int TPR = 128 / BN;  // threads per row
+  const int r = tid / TPR, q = tid % TPR;
+  const bool bf = p.fmt == 1;
+  const bool valid = r < p.J;
+  const uint16_t* xr = static_cast<const uint16_t*>(p.ln_x) + (long long)(valid ? r : 0) * p.ln_ldx;
+  bool ok = ln_stats<BN>(p, s, ksplit, crank, kb_begin, kb_end, tid);
+  const float2 ms = ld_shared_v2(s.aux + aux_rowst(BN) + r * 8);
   const uint16_t* g = static_cast<const uint16_t*>(p.ln_g);
   const uint16_t* b = static_cast<const uint16_t*>(p.ln_b);
   int stage = 0;
@@ -603,11 +618,8 @@ __device__ bool ln_prologue(const Params& p, const Smem& s, int ksplit, uint32_t
 // out of range raises DEV_ERR_ATTN_RANGE like neb_kv_append.
 // Eight consecutive features n0..n0+7 of token m (one head, same K or V
 // pool: q_cols and head_dim are multiples of 8) as one 16-byte store.
-__device__ __forceinline__ void kv_store8(const Params& p, int n0, int m, uint32_t red, int src_stride,
-                                          int e_stride, int nsrc) {
+__device__ __forceinline__ void kv_store8(const Params& p, int n0, int m, const float (&x)[8]) {
   if (n0 >= p.cols_out || m >= p.J) return;
-  float x[8];
-  red_sum8(red, src_stride, e_stride, nsrc, x);
   const int nn = n0 - p.kv_q_cols;
   const bool is_v = nn >= p.kv_cols;
   const int c = is_v ? nn - p.kv_cols : nn;
@@ -625,6 +637,21 @@ __device__ __forceinline__ void kv_store8(const Params& p, int n0, int m, uint32
 }
 __device__ __forceinline__ void st_shared_u16(uint32_t addr, uint32_t v) {
   asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"((unsigned short)v) : "memory");
+}
+
+// LayerNorm folded into the product (ln_mode 2): with P = W diag(gamma),
+//   LN(x) W^T = rstd * (x P^T - mean * sum_k P[n][k]) + W beta
+// for eight consecutive features n0.. of token row r of this tile; the row's
+// mean and rstd come from ln_stats.  (The reference rounds LN(x) to the model
+// dtype before the product; here the product sees it unrounded.)
+__device__ __forceinline__ void ln_fold8(const Params& p, const Smem& s, int BNv, int r, int n0, float (&x)[8]) {
+  const float2 ms = ld_shared_v2(s.aux + (uint32_t)(8 * BNv * 8) + (uint32_t)(r * 8));
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int n = min(n0 + e, p.cols_out - 1);
+    const float c = p.fold_c != nullptr ? p.fold_c[n] : 0.f;
+    x[e] = ms.y * (x[e] - ms.x * p.fold_s[n]) + c;
+  }
 }
 
 // All-reduce epilogue of one owner CTA: its rows_per features (rows r0.. of
@@ -810,7 +837,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
     const uint32_t slab_bytes = (uint32_t)rows * kSlab;
     const bool packed = !is_q && p.p_packed != nullptr;
     // FUSED with the LayerNorm prologue: the epilogue warps write Q.
-    const bool idle = FUSED && is_q && p.ln_x != nullptr;
+    const bool idle = FUSED && is_q && p.ln_mode == 1;
     const int nbox = mn ? rows / mn_box : 1;
     int stage = 0;
     uint32_t phase = 0;
@@ -993,8 +1020,11 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
     constexpr bool kRedAlways = FUSED;
     const bool use_red = ksplit > 1 || kRedAlways || (BN <= 32 && p.swap);
     if constexpr (FUSED) {
-      if (p.ln_x != nullptr && cluster_id < p.num_tiles)
+      if (p.ln_mode == 1 && cluster_id < p.num_tiles)
         ok = epi_bar_and(ln_prologue<BN>(p, s, ksplit, crank, kb_begin, kb_end, ep_tid));
+      // fold: the statistics are computed while the main loop runs
+      if (p.ln_mode == 2 && cluster_id < p.num_tiles)
+        ok = epi_bar_and(ln_stats<BN>(p, s, ksplit, crank, kb_begin, kb_end, ep_tid));
     }
     for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
       int ti, tj;
@@ -1090,25 +1120,28 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
           if constexpr (FUSED) {
             const int n0 = ti * kBM + r0 + rr0;  // first feature (the fused kernels are swapped)
             const int m = tj * BN + c0;
+            float x[8];
+            red_sum8(base, src_stride, row_bytes, ksplit, x);
+            if (p.ln_mode == 2) ln_fold8(p, s, BN, c0, n0, x);
             if (p.ar_on) {
               // rounded partial -> staging block [feature][token] for the exchange
               const bool bf = p.fmt == 1;
-              float x[8];
-              red_sum8(base, src_stride, row_bytes, ksplit, x);
 #pragma unroll
               for (int e = 0; e < 8; ++e)
                 st_shared_u16(s.aux + aux_stage(BN) + (uint32_t)(((rr0 + e) * peer::kSubTokens + c0) * 2), f2h(x[e], bf));
               continue;
             }
             if (p.kv_k != nullptr && n0 >= p.kv_q_cols) {
-              kv_store8(p, n0, m, base, src_stride, row_bytes, ksplit);
+              kv_store8(p, n0, m, x);
               continue;
             }
-            epilogue_store8(p, m, n0, base, src_stride, row_bytes, ksplit);
+            epilogue_store8(p, m, n0, x);
             continue;
           }
-          if (p.swap) epilogue_store8(p, tj * BN + c0, ti * kBM + r0 + rr0, base, src_stride, row_bytes, ksplit);
-          else epilogue_store8(p, ti * kBM + r0 + rr0, tj * BN + c0, base, src_stride, 4, ksplit);
+          float x[8];
+          red_sum8(base, src_stride, p.swap ? row_bytes : 4, ksplit, x);
+          if (p.swap) epilogue_store8(p, tj * BN + c0, ti * kBM + r0 + rr0, x);
+          else epilogue_store8(p, ti * kBM + r0 + rr0, tj * BN + c0, x);
         }
         if (ksplit == 1) epi_bar_sync();  // the buffer is refilled by this CTA's next tile
         if constexpr (FUSED) {
@@ -1906,12 +1939,26 @@ extern "C" int neb_linear_fused(const void* x, int64_t ldx, const void* packed, 
   Params fz = {};
   const bool kv = fu->k_pool != nullptr;
   const bool ar = fu->ar_ctx != nullptr;
+  if (fu->ln_gamma && fu->ln_wsum) return fail(FML_EINVAL, "linear_fused: give ln_gamma (prologue) or ln_wsum (fold), not both");
+  if (fu->ln_wsum) {
+    if (k % 64 != 0) return fail(FML_EUNSUPPORTED, "linear_fused: LayerNorm fold needs k a multiple of 64");
+    if (reinterpret_cast<uintptr_t>(x) % 16 || (ldx * 2) % 16)
+      return fail(FML_EUNSUPPORTED, "linear_fused: LayerNorm operands must be 16-byte aligned");
+    fz.ln_mode = 2;
+    fz.fold_s = fu->ln_wsum;
+    fz.fold_c = fu->ln_wbias;
+    fz.ln_x = x;
+    fz.ln_ldx = ldx;
+    fz.ln_eps = fu->ln_eps;
+    fz.ln_k = (int)k;
+  }
   if (fu->ln_gamma) {
     if (!fu->ln_beta) return fail(FML_EINVAL, "linear_fused: LayerNorm needs gamma and beta");
     if (k % 64 != 0) return fail(FML_EUNSUPPORTED, "linear_fused: LayerNorm prologue needs k a multiple of 64");
     if (reinterpret_cast<uintptr_t>(x) % 16 || (ldx * 2) % 16 || reinterpret_cast<uintptr_t>(fu->ln_gamma) % 16 ||
         reinterpret_cast<uintptr_t>(fu->ln_beta) % 16)
       return fail(FML_EUNSUPPORTED, "linear_fused: LayerNorm operands must be 16-byte aligned");
+    fz.ln_mode = 1;
     fz.ln_x = x;
     fz.ln_ldx = ldx;
     fz.ln_g = fu->ln_gamma;

@@ -55,11 +55,15 @@ class PackedLinear:
         return bool(_native.load().neb_linear_fused_ok(self.n, self.k, m, self.code))
 
     def fused(self, x: torch.Tensor, out: torch.Tensor, *, act: int = 0, residual: torch.Tensor | None = None,
-              ln: tuple | None = None, kv: tuple | None = None, ar_ctx=None, rows: int | None = None) -> torch.Tensor:
+              ln: tuple | None = None, ln_fold: tuple | None = None, kv: tuple | None = None, ar_ctx=None,
+              rows: int | None = None) -> torch.Tensor:
         """Decode-step linear with its neighbours fused into the one launch
         (``neb_linear_fused``):
 
         ``ln=(gamma, beta, eps)``: the product reads LayerNorm(x) instead of x.
+        ``ln_fold=(wsum, wbias, eps)``: this weight is W diag(gamma) (see
+        ``ln_fold_vectors``) and the result is LayerNorm(x) W^T, the row
+        statistics computed while the product runs.
         ``kv=(k_pool, v_pool, slot_of, start_pos, q_cols, tq)``: output
         features from ``q_cols`` on are appended to the KV pools
         [slots, heads, max_seq, head_dim] at (slot_of[b], start_pos[b] + t).
@@ -71,6 +75,11 @@ class PackedLinear:
         if ln is not None:
             g, b, eps = ln
             fz.ln_gamma, fz.ln_beta, fz.ln_eps = g.data_ptr(), b.data_ptr(), float(eps)
+        if ln_fold is not None:
+            wsum, wbias, eps = ln_fold
+            fz.ln_wsum = wsum.data_ptr()
+            fz.ln_wbias = wbias.data_ptr() if wbias is not None else None
+            fz.ln_eps = float(eps)
         if kv is not None:
             kp, vp, slots, starts, q_cols, tq = kv
             fz.k_pool, fz.v_pool = kp.data_ptr(), vp.data_ptr()
@@ -86,3 +95,17 @@ class PackedLinear:
             ctypes.byref(fz), _native.stream_ptr(x.device),
         )
         return out
+
+
+def ln_fold_vectors(weight: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor):
+    """For LayerNorm(x) W^T folded into one product (``PackedLinear.fused``
+    with ``ln_fold``): returns (W', wsum, wbias) with W' = W diag(gamma) in
+    W's dtype, wsum[n] = sum_k W'[n][k] and wbias[n] = sum_k W[n][k] beta[k]
+    (fp32; None when beta is zero).  W' is W itself when gamma is all ones."""
+    if bool((gamma == 1).all()):
+        wp = weight
+    else:
+        wp = (weight.float() * gamma.float()[None, :]).to(weight.dtype).contiguous()
+    wsum = wp.float().sum(dim=1).contiguous()
+    wbias = None if bool((beta == 0).all()) else (weight.float() @ beta.float()).contiguous()
+    return wp, wsum, wbias

@@ -8,15 +8,18 @@ a MAX all-reduce; poisoning on any failure -- runtime.py:19-27,192-516).
 The decoder runs every layer on native kernels (no torch compute on the hot
 path).  A layer of at most 32 tokens (every decode step of configs 4 and 5)
 runs as fused launches of the tcgen05 GEMM (neb_linear_fused) plus the
-attention and LayerNorm kernels:
+attention kernel:
 
-  LN1 -> QKV GEMM + KV append -> attention -> o GEMM (+ TP all-reduce) + residual
-  -> LN2 -> up GEMM + tanh-GELU -> down GEMM (+ TP all-reduce) + residual
+  LN1-folded QKV GEMM + KV append -> attention -> o GEMM (+ TP all-reduce)
+  + residual -> LN2-folded up GEMM + tanh-GELU -> down GEMM (+ TP all-reduce)
+  + residual
 
 with the K/V columns written into the pools by the GEMM epilogue and (TP = 2)
 the partials exchanged over NVLink from the GEMM epilogue (larger TP groups use
-the standalone NVLink all-reduce kernel after the GEMM); the LayerNorms can
-also run in the GEMM prologue (FORGEML_FUSED_LN=1).  Larger steps (prefill) run the unfused chain:
+the standalone NVLink all-reduce kernel after the GEMM).  The two LayerNorms
+are folded into the QKV / up products (decode_ln_mode): gamma is folded into
+the packed weight and the GEMM corrects its accumulator with the row
+statistics it computes while streaming the weight.  Larger steps (prefill) run the unfused chain:
 
   LN -> fused QKV GEMM (one [3*h_local*hd, h] weight per rank)
      -> KV append into the slot pool -> attention over the pool (no prefix copy)
@@ -48,7 +51,7 @@ from torch import nn
 from torch.profiler import record_function
 
 from forgeml_b200 import _native
-from forgeml_b200.linear import PackedLinear
+from forgeml_b200.linear import PackedLinear, ln_fold_vectors
 from forgeml_b200.nebula import ops
 from forgeml_b200.nebula.cache import CacheError, KVCache
 from forgeml_b200.nebula.model import DecoderConfig, TinyDecoder
@@ -126,6 +129,14 @@ class _Layer:
         self.o = _linear(wo, ws)
         self.up = _linear(wup, ws)
         self.down = _linear(wdown, ws)
+        # LayerNorm folded into the QKV / up products of the decode step:
+        # W diag(gamma) packed (the same packed weight when gamma is all ones)
+        # plus the per-feature sums the epilogue needs.
+        self.qkv_ln = self.up_ln = None
+        if isinstance(self.qkv, PackedLinear):
+            for name, w, g, b, lin in (("qkv_ln", wqkv, ln1_w, ln1_b, self.qkv), ("up_ln", wup, ln2_w, ln2_b, self.up)):
+                wp, wsum, wbias = ln_fold_vectors(w, g, b)
+                setattr(self, name, (lin if wp is w else PackedLinear(wp), wsum, wbias))
 
 
 def _ln(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, out: torch.Tensor, rows: int,
@@ -260,8 +271,12 @@ class ShardedDecoder(nn.Module):
         hl, hd, hl_hd = self.num_heads_local, self.head_dim, self._hl_hd
         dev = x.device
         kp, vp = self.cache.k_pool[lid], self.cache.v_pool[lid]
-        fuse_ln = fused_ln_enabled()
-        if fuse_ln:
+        ln_mode = decode_ln_mode()
+        if ln_mode == "fold":
+            lin, wsum, wbias = L.qkv_ln
+            q = lin.fused(x, torch.empty((bt, hl_hd), dtype=self.dtype, device=dev), ln_fold=(wsum, wbias, 1e-5),
+                          kv=(kp, vp, slots, starts, hl_hd, t))
+        elif ln_mode == "prologue":
             q = L.qkv.fused(x, torch.empty((bt, hl_hd), dtype=self.dtype, device=dev), ln=(L.ln1_w, L.ln1_b, 1e-5),
                             kv=(kp, vp, slots, starts, hl_hd, t))
         else:
@@ -277,7 +292,11 @@ class ShardedDecoder(nn.Module):
                           ar_ctx=self._peer_ar.handle)
         else:
             x = self._tp_sum_add(L.o(attn, torch.empty((bt, h), dtype=self.dtype, device=dev)), x)
-        if fuse_ln:
+        if ln_mode == "fold":
+            lin, wsum, wbias = L.up_ln
+            mid = lin.fused(x, torch.empty((bt, L.wup.shape[0]), dtype=self.dtype, device=dev),
+                            act=_native.ACT_GELU_TANH, ln_fold=(wsum, wbias, 1e-5))
+        elif ln_mode == "prologue":
             mid = L.up.fused(x, torch.empty((bt, L.wup.shape[0]), dtype=self.dtype, device=dev),
                              act=_native.ACT_GELU_TANH, ln=(L.ln2_w, L.ln2_b, 1e-5))
         else:
@@ -462,12 +481,18 @@ def fused_ar_enabled(tp: int) -> bool:
     return tp <= 2
 
 
-def fused_ln_enabled() -> bool:
-    """LayerNorm inside the QKV / up GEMM prologue (FORGEML_FUSED_LN=1).  Off
-    by default: measured on B200 the prologue (statistics exchange, then a
-    second read of x, gamma and beta) lengthens the GEMM's critical path by
-    more than the separate LayerNorm launch costs in the PDL chain."""
-    return os.environ.get("FORGEML_FUSED_LN", "0") == "1"
+def decode_ln_mode() -> str:
+    """How the decode step's pre-QKV / pre-up LayerNorms run
+    (FORGEML_DECODE_LN):
+      "fold"     folded into the QKV / up products (gamma in the packed
+                 weight, statistics computed by the GEMM while its main loop
+                 runs, correction in the epilogue): no LayerNorm launch;
+      "prologue" normalised by the GEMM's epilogue warps into the operand
+                 stages before the main loop (slower on B200: it lengthens
+                 the GEMM's critical path);
+      "kernel"   a separate LayerNorm launch before the GEMM."""
+    v = os.environ.get("FORGEML_DECODE_LN", "fold")
+    return v if v in ("fold", "prologue", "kernel") else "fold"
 
 
 def _validate_prompt(config: DecoderConfig, prompt: list[int], max_new: int) -> None:

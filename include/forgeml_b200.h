@@ -264,6 +264,12 @@ FML_API int neb_ar_destroy(void* ctx);
  * different order.
  *   LayerNorm prologue (ln_gamma != NULL): the GEMM reads LN(x) over x's k
  *     columns (eps ln_eps, ln_beta required); k a multiple of 64.
+ *   LayerNorm fold (ln_wsum != NULL, ln_gamma NULL): the packed weight is
+ *     W diag(gamma); the GEMM reads x itself and returns
+ *     rstd * (x W'^T - mean * ln_wsum[n]) + ln_wbias[n]  (= LN(x) W^T with
+ *     ln_wsum[n] = sum_k W'[n][k], ln_wbias[n] = sum_k W[n][k] beta[k], fp32
+ *     vectors of n; ln_wbias may be NULL), the row statistics computed while
+ *     the product runs; k a multiple of 64.
  *   KV epilogue (k_pool != NULL): output features [0, q_cols) go to out (row
  *     stride ldo >= q_cols); features q_cols + [0, kv_heads*head_dim) go to
  *     K and the next kv_heads*head_dim to V, at pool[slot_of[b], head,
@@ -282,6 +288,8 @@ typedef struct neb_fusion {
   const void* ln_gamma;
   const void* ln_beta;
   float ln_eps;
+  const float* ln_wsum;
+  const float* ln_wbias;
   void* k_pool;
   void* v_pool;
   const int32_t* slot_of;

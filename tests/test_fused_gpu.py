@@ -5,6 +5,9 @@
   an LN output may land on the neighbouring bf16 value; with an identity
   weight the product returns LN(x) itself, which must match fml_layernorm to
   one bf16 step (and exactly for nearly every element).
+* LayerNorm fold (gamma in the packed weight, statistics by the GEMM,
+  rstd * (acc - mean * sum W') + W beta in the epilogue): against the unfused
+  chain within bf16 tolerance, and no further from an fp32 LN(x) W^T.
 * KV epilogue: bit-exact against the same kernel writing every feature to
   `out` (the pools receive exactly the K and V columns; other pool rows stay
   untouched).
@@ -70,6 +73,36 @@ def test_ln_prologue_identity_weight_is_layernorm(cuda, k, m):
     step = torch.maximum(want.float().abs(), torch.full_like(want.float(), 1e-3)) * 2.0 ** -7
     assert torch.all((got.float() - want.float()).abs() <= step * 1.01)
     assert (got == want).float().mean() > 0.98
+
+
+@pytest.mark.parametrize("n,k,m,identity", [(6144, 2048, 32, False), (8192, 2048, 7, False), (768, 2048, 32, True),
+                                            (2048, 4096, 1, False), (256, 128, 18, True)])
+def test_ln_fold_matches_unfused(cuda, n, k, m, identity):
+    """LayerNorm folded into the product: LN(x) W^T = rstd (x W'^T - mean sum W') + W beta.
+    Against the unfused chain within bf16 tolerance, and no further from an
+    fp32 evaluation of LN(x) W^T than the unfused chain (which rounds LN(x))."""
+    from forgeml_b200.linear import ln_fold_vectors
+
+    w, x, gam, bet = _data(n, k, m, cuda, 3 * n + k + m)
+    if identity:
+        gam, bet = torch.ones_like(gam), torch.zeros_like(bet)
+    wp, wsum, wbias = ln_fold_vectors(w, gam, bet)
+    assert (wp is w) == identity and (wbias is None) == identity
+    act = _native.ACT_GELU_TANH if n == 8192 else 0
+    lin = PackedLinear(w)
+    lin_f = lin if wp is w else PackedLinear(wp)
+    got = lin_f.fused(x, torch.empty(m, n, dtype=BF, device=cuda), act=act, ln_fold=(wsum, wbias, 1e-5))
+    want = lin(_ln_ref(x, gam, bet), torch.empty(m, n, dtype=BF, device=cuda), act=act)
+    assert _native.device_status() == 0
+    scale = float(want.float().abs().max())
+    torch.testing.assert_close(got.float(), want.float(), rtol=2e-2, atol=2e-2 * scale)
+    ln32 = torch.nn.functional.layer_norm(x.float(), (k,), gam.float(), bet.float(), 1e-5)
+    ref = ln32 @ w.float().t()
+    if act:
+        ref = torch.nn.functional.gelu(ref, approximate="tanh")
+    err_f = (got.float() - ref).abs().mean()
+    err_u = (want.float() - ref).abs().mean()
+    assert err_f <= 1.5 * err_u + 1e-6 * scale
 
 
 @pytest.mark.parametrize("b,t,heads", [(32, 1, 16), (4, 3, 2), (1, 1, 8)])
