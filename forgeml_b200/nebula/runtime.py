@@ -14,9 +14,9 @@ attention kernel:
   + residual -> LN2-folded up GEMM + tanh-GELU -> down GEMM (+ TP all-reduce)
   + residual
 
-with the K/V columns written into the pools by the GEMM epilogue and (TP = 2)
-the partials exchanged over NVLink from the GEMM epilogue (larger TP groups use
-the standalone NVLink all-reduce kernel after the GEMM).  The two LayerNorms
+with the K/V columns written into the pools by the GEMM epilogue and the TP
+partials summed over NVLink by the standalone peer all-reduce kernel (or, opt
+in, exchanged from the GEMM epilogue itself).  The two LayerNorms
 are folded into the QKV / up products (decode_ln_mode): gamma is folded into
 the packed weight and the GEMM corrects its accumulator with the row
 statistics it computes while streaming the weight.  Larger steps (prefill) run the unfused chain:
@@ -469,16 +469,13 @@ def fused_enabled() -> bool:
 
 
 def fused_ar_enabled(tp: int) -> bool:
-    """TP all-reduce inside the o / down GEMM epilogue, or the standalone peer
-    all-reduce kernel after the GEMM.  FORGEML_FUSED_AR=1/0 forces either;
-    by default the epilogue exchange is used for two ranks and the standalone
-    kernel for more (measured on B200 at config 4: TP2 1.30 vs 1.35 ms per
-    step in favour of the epilogue, TP8 1.38 vs 1.13 ms in favour of the
-    standalone kernel)."""
-    v = os.environ.get("FORGEML_FUSED_AR")
-    if v is not None:
-        return v == "1"
-    return tp <= 2
+    """TP all-reduce inside the o / down GEMM epilogue (FORGEML_FUSED_AR=1),
+    or the standalone peer all-reduce kernel after the GEMM (default).
+    Measured on B200 at config 4 with the current GEMM epilogue: TP2 1.006 ms
+    per step standalone vs 1.046 ms in the epilogue, TP8 1.13 vs 1.38 ms: the
+    exchange waits inside the GEMM's critical path, while the standalone
+    kernel's prologue overlaps the GEMM's tail."""
+    return os.environ.get("FORGEML_FUSED_AR", "0") == "1"
 
 
 def decode_ln_mode() -> str:
