@@ -27,6 +27,7 @@
 //
 // The same buffer carries a second region for the all-reduce fused into the
 // decode GEMM's epilogue (gemm.cu); its layout is in peer_layout.cuh.
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -125,6 +126,112 @@ __global__ void __launch_bounds__(kThreads) ar_kernel(const Args a, const T* __r
   if (tid == 0) epochs[blk] = e;
 }
 
+// Low-latency (LL) variant.  Each 4-byte word of a rank's partial travels
+// with the launch's epoch in one 8-byte store, (epoch << 32) | word, into
+// slot `rank` of every peer's LL region; a reader polls the pairs of its
+// chunk until every epoch matches, so neither a system fence nor a separate
+// flag round trip sits on the critical path (8-byte aligned accesses are
+// single-copy atomic).  Sums, rounding, epochs (one per CTA index, advanced
+// on the device) and the two buffer sets by epoch parity are those of
+// ar_kernel: CTA b of rank r writes set e&1 of a peer only after it has read
+// that peer's epoch e-1 words of chunk b, written by the peer's next launch
+// after it finished reading set e&1 in epoch e-2.  Twice the bytes of the
+// flag protocol cross NVLink, negligible at decode sizes.
+__device__ __forceinline__ void st_volatile_v2u64(uint64_t* p, uint64_t a, uint64_t b) {
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ void ld_volatile_v2u64(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) ar_ll_kernel(const Args a, const T* __restrict__ part,
+                                                         const T* __restrict__ residual, T* __restrict__ out,
+                                                         long long nvec) {
+  constexpr int VE = 16 / sizeof(T);
+  pdl_wait();
+  pdl_trigger();
+  const int blk = blockIdx.x, tid = threadIdx.x;
+  const int W = a.lay.world, r = a.rank;
+  uint32_t* epochs = reinterpret_cast<uint32_t*>(a.base[r] + a.lay.ll_epoch_off(0));
+  __shared__ uint32_t s_epoch;
+  if (tid == 0) s_epoch = epochs[blk] + 1u;
+  __syncthreads();
+  const uint32_t e = s_epoch;
+  const int set = (int)(e & 1u);
+  const uint64_t tag = (uint64_t)e << 32;
+  const long long per = (nvec + kBlocks - 1) / kBlocks;
+  const long long v0 = (long long)blk * per, v1 = min(nvec, v0 + per);
+  const uint4* src = reinterpret_cast<const uint4*>(part);
+  // 1. push this chunk into slot r of every peer (16 data bytes -> 32 LL bytes)
+  for (long long i = v0 + tid; i < v1; i += kThreads) {
+    const uint4 v = src[i];
+    for (int q = 0; q < W; ++q) {
+      if (q == r) continue;
+      uint64_t* dst = reinterpret_cast<uint64_t*>(a.base[q] + a.lay.ll_data_off(set, r)) + 4 * i;
+      st_volatile_v2u64(dst, tag | v.x, tag | v.y);
+      st_volatile_v2u64(dst + 2, tag | v.z, tag | v.w);
+    }
+  }
+  // 2. gather every rank's words of this chunk in rank order, sum, add the residual
+  bool ok = true;
+  for (long long i = v0 + tid; i < v1; i += kThreads) {
+    float acc[VE];
+#pragma unroll
+    for (int k = 0; k < VE; ++k) acc[k] = 0.f;
+    for (int q = 0; q < W; ++q) {
+      uint4 words;
+      if (q == r) {
+        words = src[i];
+      } else {
+        const uint64_t* ps = reinterpret_cast<const uint64_t*>(a.base[r] + a.lay.ll_data_off(set, q)) + 4 * i;
+        uint64_t w0, w1, w2, w3;
+        ld_volatile_v2u64(ps, w0, w1);
+        ld_volatile_v2u64(ps + 2, w2, w3);
+        if (ok && ((w0 >> 32) != e || (w1 >> 32) != e || (w2 >> 32) != e || (w3 >> 32) != e)) {
+          const long long t0 = clock64();
+          while (true) {
+            ld_volatile_v2u64(ps, w0, w1);
+            ld_volatile_v2u64(ps + 2, w2, w3);
+            if ((w0 >> 32) == e && (w1 >> 32) == e && (w2 >> 32) == e && (w3 >> 32) == e) break;
+            if (clock64() - t0 > a.timeout_cycles) {
+              raise_device_error(DEV_ERR_AR_TIMEOUT);
+              ok = false;
+              break;
+            }
+          }
+        }
+        words = make_uint4((uint32_t)w0, (uint32_t)w1, (uint32_t)w2, (uint32_t)w3);
+      }
+      add_vec<T>(acc, words);
+    }
+    float res[VE];
+    if (residual != nullptr) {
+      const uint4 rv = reinterpret_cast<const uint4*>(residual)[i];
+      const T* re = reinterpret_cast<const T*>(&rv);
+#pragma unroll
+      for (int k = 0; k < VE; ++k) res[k] = to_f32<T>(re[k]);
+    }
+    uint4 o;
+    T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+    for (int k = 0; k < VE; ++k) {
+      float x = to_f32<T>(from_f32<T>(acc[k]));
+      if (residual != nullptr) x = x + res[k];
+      oe[k] = from_f32<T>(x);
+    }
+    reinterpret_cast<uint4*>(out)[i] = o;
+  }
+  __syncthreads();
+  if (tid == 0) epochs[blk] = e;
+}
+
+// Protocol of neb_ar_all_reduce: LL unless FORGEML_AR_PROTO=flag.
+static bool use_ll() {
+  const char* v = getenv("FORGEML_AR_PROTO");
+  return !(v && std::string(v) == "flag");
+}
+
 }  // namespace ar
 }  // namespace fml
 
@@ -217,16 +324,19 @@ int neb_ar_all_reduce(void* ctx, const void* part, const void* residual, void* o
   const long long nvec = bytes / 16;
   cudaError_t e;
   const dim3 grid(fml::ar::kBlocks), block(fml::ar::kThreads);
+  const bool ll = fml::ar::use_ll();
   if (dtype == FML_F32)
-    e = fml::launch_pdl(fml::ar::ar_kernel<float>, grid, block, 0, st, 1, c->v, static_cast<const float*>(part),
-                        static_cast<const float*>(residual), static_cast<float*>(out), nvec);
+    e = fml::launch_pdl(ll ? fml::ar::ar_ll_kernel<float> : fml::ar::ar_kernel<float>, grid, block, 0, st, 1, c->v,
+                        static_cast<const float*>(part), static_cast<const float*>(residual),
+                        static_cast<float*>(out), nvec);
   else if (dtype == FML_BF16)
-    e = fml::launch_pdl(fml::ar::ar_kernel<__nv_bfloat16>, grid, block, 0, st, 1, c->v,
-                        static_cast<const __nv_bfloat16*>(part), static_cast<const __nv_bfloat16*>(residual),
-                        static_cast<__nv_bfloat16*>(out), nvec);
+    e = fml::launch_pdl(ll ? fml::ar::ar_ll_kernel<__nv_bfloat16> : fml::ar::ar_kernel<__nv_bfloat16>, grid, block, 0,
+                        st, 1, c->v, static_cast<const __nv_bfloat16*>(part),
+                        static_cast<const __nv_bfloat16*>(residual), static_cast<__nv_bfloat16*>(out), nvec);
   else
-    e = fml::launch_pdl(fml::ar::ar_kernel<__half>, grid, block, 0, st, 1, c->v, static_cast<const __half*>(part),
-                        static_cast<const __half*>(residual), static_cast<__half*>(out), nvec);
+    e = fml::launch_pdl(ll ? fml::ar::ar_ll_kernel<__half> : fml::ar::ar_kernel<__half>, grid, block, 0, st, 1, c->v,
+                        static_cast<const __half*>(part), static_cast<const __half*>(residual),
+                        static_cast<__half*>(out), nvec);
   fml::count_launch();
   return fml::check_cuda(e, "neb_ar_all_reduce launch");
 }

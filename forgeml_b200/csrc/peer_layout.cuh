@@ -1,14 +1,17 @@
 // Symmetric NVLink peer buffer of the tensor-parallel SUM all-reduce: one per
 // TP rank, opened by every peer through CUDA IPC (allreduce.cu), and read and
-// written by two kinds of kernel:
+// written by three kinds of kernel:
 //
 //   * the standalone all-reduce (allreduce.cu), which splits a message into
 //     kArBlocks fixed chunks, one per CTA index;
 //   * the GEMM epilogue of the fused decode linear (gemm.cu), which exchanges
-//     16-feature sub-blocks of a [features x 32 tokens] partial.
+//     16-feature sub-blocks of a [features x 32 tokens] partial;
+//   * the low-latency (LL) all-reduce (allreduce.cu), whose data words carry
+//     their epoch: [2 sets][world slots][2 * slot_bytes] of 8-byte
+//     (4 data bytes, 4 epoch bytes) pairs, plus kArBlocks epochs.
 //
-// Each kind owns its own data slots, flags and epochs, so the two never
-// share a buffer region or an epoch counter.  Per region, data is
+// Each kind owns its own data slots, flags and epochs, so they never
+// share a buffer region or an epoch counter.  Per flag region, data is
 // [2 sets][world slots][slot_bytes], flags [2 sets][world sources][units]
 // (u32 epochs raised by the source rank), epochs [units] (this rank's count
 // of completed exchanges per unit).
@@ -44,7 +47,15 @@ struct Layout {
   __host__ __device__ long long epoch_off(int region, int unit) const {
     return base(region) + 2LL * world * slot_bytes + 2LL * world * units(region) * 4 + (long long)unit * 4;
   }
-  __host__ __device__ long long total() const { return region_bytes(kArBlocks) + region_bytes(nsub); }
+  // region 2: LL all-reduce
+  __host__ __device__ long long ll_base() const { return region_bytes(kArBlocks) + region_bytes(nsub); }
+  __host__ __device__ long long ll_data_off(int set, int slot) const {
+    return ll_base() + ((long long)set * world + slot) * 2 * slot_bytes;
+  }
+  __host__ __device__ long long ll_epoch_off(int unit) const {
+    return ll_base() + 2LL * world * 2 * slot_bytes + (long long)unit * 4;
+  }
+  __host__ __device__ long long total() const { return ll_base() + 4LL * world * slot_bytes + kArBlocks * 4; }
 };
 
 // What a kernel needs to reach every rank's buffer.

@@ -109,12 +109,13 @@ def test_tp8_bf16():
     _run(8, 8, 1, "bfloat16")
 
 
-def _ar_worker(rank, world, store, dtype_name):
+def _ar_worker(rank, world, store, dtype_name, proto="ll"):
     import os
 
     from forgeml_b200.nebula import ParallelContext
     from forgeml_b200.nebula.peer import PeerAllReduce
 
+    os.environ["FORGEML_AR_PROTO"] = proto
     os.environ["LOCAL_RANK"] = str(rank)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     torch.cuda.set_device(rank)
@@ -170,11 +171,11 @@ def _ar_worker(rank, world, store, dtype_name):
             dist.destroy_process_group()
 
 
-def _run_ar(world, dtype_name):
+def _run_ar(world, dtype_name, proto="ll"):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     with tempfile.TemporaryDirectory() as d:
-        procs = mp.start_processes(_ar_worker, args=(world, f"{d}/store", dtype_name), nprocs=world,
+        procs = mp.start_processes(_ar_worker, args=(world, f"{d}/store", dtype_name, proto), nprocs=world,
                                    join=False, start_method="spawn")
         deadline = time.time() + 180
         while time.time() < deadline and not all(p.exitcode is not None for p in procs.processes):
@@ -189,6 +190,10 @@ def _run_ar(world, dtype_name):
 
 def test_peer_all_reduce_2_bf16():
     _run_ar(2, "bfloat16")
+
+
+def test_peer_all_reduce_2_bf16_flag_protocol():
+    _run_ar(2, "bfloat16", "flag")
 
 
 def test_peer_all_reduce_2_fp32():
