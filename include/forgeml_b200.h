@@ -234,7 +234,10 @@ FML_API int neb_add(const void* a, const void* b, void* y, int64_t n, int dtype,
  * exchanges the IPC handles with its TP group, opens the peers' buffers, then
  * every rank calls neb_ar_all_reduce with the same sizes in the same order
  * (stream-ordered, CUDA-graph capturable).  A wait that exceeds timeout_ms
- * raises bit 32 of fml_device_status() instead of hanging.
+ * raises bit 32 of fml_device_status() instead of hanging.  Protocol: each
+ * 4-byte word travels with the call's epoch in one 8-byte store and readers
+ * poll the words (low latency; FORGEML_AR_PROTO=flag selects data stores,
+ * a system fence and per-chunk epoch flags instead).
  * ------------------------------------------------------------------------- */
 /* Bytes of one IPC handle (cudaIpcMemHandle_t). */
 FML_API int64_t neb_ar_handle_bytes(void);
