@@ -226,10 +226,124 @@ __global__ void __launch_bounds__(kThreads) ar_ll_kernel(const Args a, const T* 
   if (tid == 0) epochs[blk] = e;
 }
 
-// Protocol of neb_ar_all_reduce: LL unless FORGEML_AR_PROTO=flag.
-static bool use_ll() {
+// Two-shot LL variant for larger groups: chunk b (one per CTA index) is cut
+// into `world` contiguous sub-shards, sub-shard q owned by rank q.
+//   1. reduce-scatter: each rank sends every vector it does not own to the
+//      owner's area (slot = sender), as (epoch << 32) | word pairs;
+//   2. the owner polls the other ranks' words of its vectors, sums all ranks
+//      in rank order in fp32 (the one-shot kernels' arithmetic, so results
+//      are bit-identical), adds the residual, writes its output and sends the
+//      finished 16-bit words to every rank's all-gather area (one writer per
+//      position);
+//   3. every rank polls the all-gather words of the vectors it does not own.
+// A rank sends 2 (W-1)/W of the message (x2 for the pairs) instead of W-1
+// copies, for one more NVLink hop.  No wait precedes a send that another rank
+// waits for (sends of step 1 come first; step 2's sends need only step 1's
+// data), so the steps cannot deadlock.  Reuse of a buffer set follows the LL
+// argument: rank r writes a rank's set e&1 in epoch e only for positions it
+// had, in epoch e-1, read words of that rank's epoch e-1 launch about (its
+// all-gather words for the reduce-scatter area, its reduce-scatter words for
+// the all-gather area), so that rank had finished epoch e-2.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) ar_ts_kernel(const __grid_constant__ Args a, const T* __restrict__ part,
+                                                         const T* __restrict__ residual, T* __restrict__ out,
+                                                         long long nvec) {
+  constexpr int VE = 16 / sizeof(T);
+  pdl_wait();
+  pdl_trigger();
+  const int blk = blockIdx.x, tid = threadIdx.x;
+  const int W = a.lay.world, r = a.rank;
+  uint32_t* epochs = reinterpret_cast<uint32_t*>(a.base[r] + a.lay.ts_epoch_off(0));
+  __shared__ uint32_t s_epoch;
+  if (tid == 0) s_epoch = epochs[blk] + 1u;
+  __syncthreads();
+  const uint32_t e = s_epoch;
+  const int set = (int)(e & 1u);
+  const uint64_t tag = (uint64_t)e << 32;
+  const long long per = (nvec + kBlocks - 1) / kBlocks;
+  const long long v0 = (long long)blk * per, v1 = min(nvec, v0 + per);
+  const long long len = v1 - v0;
+  const uint4* src = reinterpret_cast<const uint4*>(part);
+  auto owner = [&](long long i) { return (int)(((i - v0) * W) / len); };
+  auto poll4 = [&](const uint64_t* ps, bool& ok) {
+    uint64_t w0, w1, w2, w3;
+    ld_volatile_v2u64(ps, w0, w1);
+    ld_volatile_v2u64(ps + 2, w2, w3);
+    if (ok && ((w0 >> 32) != e || (w1 >> 32) != e || (w2 >> 32) != e || (w3 >> 32) != e)) {
+      const long long t0 = clock64();
+      while (true) {
+        ld_volatile_v2u64(ps, w0, w1);
+        ld_volatile_v2u64(ps + 2, w2, w3);
+        if ((w0 >> 32) == e && (w1 >> 32) == e && (w2 >> 32) == e && (w3 >> 32) == e) break;
+        if (clock64() - t0 > a.timeout_cycles) {
+          raise_device_error(DEV_ERR_AR_TIMEOUT);
+          ok = false;
+          break;
+        }
+      }
+    }
+    return make_uint4((uint32_t)w0, (uint32_t)w1, (uint32_t)w2, (uint32_t)w3);
+  };
+  // 1. reduce-scatter sends
+  for (long long i = v0 + tid; i < v1; i += kThreads) {
+    const int o = owner(i);
+    if (o == r) continue;
+    const uint4 v = src[i];
+    uint64_t* dst = reinterpret_cast<uint64_t*>(a.base[o] + a.lay.ts_rs_off(set, r)) + 4 * i;
+    st_volatile_v2u64(dst, tag | v.x, tag | v.y);
+    st_volatile_v2u64(dst + 2, tag | v.z, tag | v.w);
+  }
+  bool ok = true;
+  // 2. owned vectors: reduce in rank order, add the residual, all-gather sends
+  for (long long i = v0 + tid; i < v1; i += kThreads) {
+    if (owner(i) != r) continue;
+    float acc[VE];
+#pragma unroll
+    for (int k = 0; k < VE; ++k) acc[k] = 0.f;
+    for (int q = 0; q < W; ++q) {
+      const uint4 words =
+          q == r ? src[i] : poll4(reinterpret_cast<const uint64_t*>(a.base[r] + a.lay.ts_rs_off(set, q)) + 4 * i, ok);
+      add_vec<T>(acc, words);
+    }
+    float res[VE];
+    if (residual != nullptr) {
+      const uint4 rv = reinterpret_cast<const uint4*>(residual)[i];
+      const T* re = reinterpret_cast<const T*>(&rv);
+#pragma unroll
+      for (int k = 0; k < VE; ++k) res[k] = to_f32<T>(re[k]);
+    }
+    uint4 o;
+    T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+    for (int k = 0; k < VE; ++k) {
+      float x = to_f32<T>(from_f32<T>(acc[k]));
+      if (residual != nullptr) x = x + res[k];
+      oe[k] = from_f32<T>(x);
+    }
+    reinterpret_cast<uint4*>(out)[i] = o;
+    for (int q = 0; q < W; ++q) {
+      if (q == r) continue;
+      uint64_t* dst = reinterpret_cast<uint64_t*>(a.base[q] + a.lay.ts_ag_off(set)) + 4 * i;
+      st_volatile_v2u64(dst, tag | o.x, tag | o.y);
+      st_volatile_v2u64(dst + 2, tag | o.z, tag | o.w);
+    }
+  }
+  // 3. all-gather receives
+  for (long long i = v0 + tid; i < v1; i += kThreads) {
+    if (owner(i) == r) continue;
+    reinterpret_cast<uint4*>(out)[i] = poll4(reinterpret_cast<const uint64_t*>(a.base[r] + a.lay.ts_ag_off(set)) + 4 * i, ok);
+  }
+  __syncthreads();
+  if (tid == 0) epochs[blk] = e;
+}
+
+// Protocol of neb_ar_all_reduce (FORGEML_AR_PROTO): "ll" one-shot LL
+// (default), "ll2" two-shot LL, "flag" stores + system fence + epoch flags.
+static int ar_proto() {
   const char* v = getenv("FORGEML_AR_PROTO");
-  return !(v && std::string(v) == "flag");
+  if (v && std::string(v) == "flag") return 0;
+  if (v && std::string(v) == "ll2") return 2;
+  return 1;
 }
 
 }  // namespace ar
@@ -324,19 +438,22 @@ int neb_ar_all_reduce(void* ctx, const void* part, const void* residual, void* o
   const long long nvec = bytes / 16;
   cudaError_t e;
   const dim3 grid(fml::ar::kBlocks), block(fml::ar::kThreads);
-  const bool ll = fml::ar::use_ll();
+  const int proto = fml::ar::ar_proto();
   if (dtype == FML_F32)
-    e = fml::launch_pdl(ll ? fml::ar::ar_ll_kernel<float> : fml::ar::ar_kernel<float>, grid, block, 0, st, 1, c->v,
-                        static_cast<const float*>(part), static_cast<const float*>(residual),
-                        static_cast<float*>(out), nvec);
+    e = fml::launch_pdl(proto == 2 ? fml::ar::ar_ts_kernel<float>
+                        : proto == 1 ? fml::ar::ar_ll_kernel<float> : fml::ar::ar_kernel<float>,
+                        grid, block, 0, st, 1, c->v, static_cast<const float*>(part),
+                        static_cast<const float*>(residual), static_cast<float*>(out), nvec);
   else if (dtype == FML_BF16)
-    e = fml::launch_pdl(ll ? fml::ar::ar_ll_kernel<__nv_bfloat16> : fml::ar::ar_kernel<__nv_bfloat16>, grid, block, 0,
-                        st, 1, c->v, static_cast<const __nv_bfloat16*>(part),
+    e = fml::launch_pdl(proto == 2 ? fml::ar::ar_ts_kernel<__nv_bfloat16>
+                        : proto == 1 ? fml::ar::ar_ll_kernel<__nv_bfloat16> : fml::ar::ar_kernel<__nv_bfloat16>,
+                        grid, block, 0, st, 1, c->v, static_cast<const __nv_bfloat16*>(part),
                         static_cast<const __nv_bfloat16*>(residual), static_cast<__nv_bfloat16*>(out), nvec);
   else
-    e = fml::launch_pdl(ll ? fml::ar::ar_ll_kernel<__half> : fml::ar::ar_kernel<__half>, grid, block, 0, st, 1, c->v,
-                        static_cast<const __half*>(part), static_cast<const __half*>(residual),
-                        static_cast<__half*>(out), nvec);
+    e = fml::launch_pdl(proto == 2 ? fml::ar::ar_ts_kernel<__half>
+                        : proto == 1 ? fml::ar::ar_ll_kernel<__half> : fml::ar::ar_kernel<__half>,
+                        grid, block, 0, st, 1, c->v, static_cast<const __half*>(part),
+                        static_cast<const __half*>(residual), static_cast<__half*>(out), nvec);
   fml::count_launch();
   return fml::check_cuda(e, "neb_ar_all_reduce launch");
 }

@@ -8,7 +8,10 @@
 //     16-feature sub-blocks of a [features x 32 tokens] partial;
 //   * the low-latency (LL) all-reduce (allreduce.cu), whose data words carry
 //     their epoch: [2 sets][world slots][2 * slot_bytes] of 8-byte
-//     (4 data bytes, 4 epoch bytes) pairs, plus kArBlocks epochs.
+//     (4 data bytes, 4 epoch bytes) pairs, plus kArBlocks epochs;
+//   * the two-shot LL all-reduce (allreduce.cu): a reduce-scatter area like
+//     the LL one, an all-gather area [2 sets][2 * slot_bytes] (each position
+//     has one writer, its owner rank), plus kArBlocks epochs.
 //
 // Each kind owns its own data slots, flags and epochs, so they never
 // share a buffer region or an epoch counter.  Per flag region, data is
@@ -55,7 +58,20 @@ struct Layout {
   __host__ __device__ long long ll_epoch_off(int unit) const {
     return ll_base() + 2LL * world * 2 * slot_bytes + (long long)unit * 4;
   }
-  __host__ __device__ long long total() const { return ll_base() + 4LL * world * slot_bytes + kArBlocks * 4; }
+  // region 3: two-shot LL all-reduce
+  __host__ __device__ long long ts_base() const { return ll_base() + 4LL * world * slot_bytes + kArBlocks * 4; }
+  __host__ __device__ long long ts_rs_off(int set, int slot) const {
+    return ts_base() + ((long long)set * world + slot) * 2 * slot_bytes;
+  }
+  __host__ __device__ long long ts_ag_off(int set) const {
+    return ts_base() + 4LL * world * slot_bytes + (long long)set * 2 * slot_bytes;
+  }
+  __host__ __device__ long long ts_epoch_off(int unit) const {
+    return ts_base() + 4LL * world * slot_bytes + 4LL * slot_bytes + (long long)unit * 4;
+  }
+  __host__ __device__ long long total() const {
+    return ts_base() + 4LL * world * slot_bytes + 4LL * slot_bytes + kArBlocks * 4;
+  }
 };
 
 // What a kernel needs to reach every rank's buffer.

@@ -196,6 +196,14 @@ def test_peer_all_reduce_2_bf16_flag_protocol():
     _run_ar(2, "bfloat16", "flag")
 
 
+def test_peer_all_reduce_2_bf16_two_shot():
+    _run_ar(2, "bfloat16", "ll2")
+
+
+def test_peer_all_reduce_8_bf16_two_shot():
+    _run_ar(8, "bfloat16", "ll2")
+
+
 def test_peer_all_reduce_2_fp32():
     _run_ar(2, "float32")
 

@@ -1,8 +1,8 @@
 """Layout of the NVLink peer buffer (forgeml_b200/csrc/peer_layout.cuh), checked
 on the CPU: the header is compiled with g++ into a small program that prints
 every region's byte ranges, and the test asserts that the flag-protocol
-all-reduce, the GEMM-epilogue exchange and the LL all-reduce regions (data
-sets, flags, epochs) are pairwise disjoint, aligned as their kernels access
+all-reduce, the GEMM-epilogue exchange, the LL and the two-shot LL
+all-reduce regions (data sets, flags, epochs) are pairwise disjoint, aligned as their kernels access
 them, and inside the allocation neb_ar_create makes (Layout::total)."""
 
 import shutil
@@ -39,6 +39,10 @@ int main(int argc, char** argv) {
   for (int set = 0; set < 2; ++set)
     for (int s = 0; s < l.world; ++s) printf("lldata %lld %lld\n", l.ll_data_off(set, s), 2 * l.slot_bytes);
   printf("llepochs %lld %lld\n", l.ll_epoch_off(0), (long long)fml::peer::kArBlocks * 4);
+  for (int set = 0; set < 2; ++set)
+    for (int s = 0; s < l.world; ++s) printf("tsrs %lld %lld\n", l.ts_rs_off(set, s), 2 * l.slot_bytes);
+  for (int set = 0; set < 2; ++set) printf("tsag %lld %lld\n", l.ts_ag_off(set), 2 * l.slot_bytes);
+  printf("tsepochs %lld %lld\n", l.ts_epoch_off(0), (long long)fml::peer::kArBlocks * 4);
   return 0;
 }
 """
@@ -70,7 +74,7 @@ def test_regions_disjoint_and_inside_the_buffer(layout_bin, slot_bytes, world):
         off, size = int(off), int(size)
         assert off >= 0 and off + size <= total, (name, off, size, total)
         # data slots are read and written with 16-byte vectors, flags/epochs as u32
-        assert off % (16 if name.startswith(("data", "lldata")) else 4) == 0, (name, off)
+        assert off % (16 if name.startswith(("data", "lldata", "tsrs", "tsag")) else 4) == 0, (name, off)
         spans.append((off, off + size, name))
     spans.sort()
     for (a0, a1, an), (b0, b1, bn) in zip(spans, spans[1:]):
