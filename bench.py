@@ -259,8 +259,16 @@ def gemm_headline(dev) -> dict:
     ms = s.elapsed_time(e) / reps
     tf = 2 * m * n * k / (ms * 1e-3) / 1e12
     pk = _peaks()
+    # the timed output, checked on 16 seeded rows against torch fp32 on the device
+    rows = torch.randperm(m, generator=torch.Generator().manual_seed(8))[:16].to(dev)
+    want = torch.nn.functional.gelu((a[rows].float() @ b.float() + bias.float()).to(torch.bfloat16).float())
+    got = out[rows].float()
+    err = float(((got - want).abs() - 2e-2 * want.abs()).max())
+    check = {"rows": 16, "vs": "torch fp32 matmul + bias + erf GELU on the device",
+             "max_abs_err": float((got - want).abs().max()), "tol": "2e-2 rel + 2e-2 abs", "pass": err <= 2e-2}
     return {"shape": "8192x8192x8192 bf16 +bias +gelu(erf), B [K,N] N-major", "ms": ms, "tflops": tf,
-            "peak_tflops": pk["bf16_tflops"], "frac": tf / pk["bf16_tflops"], "peak_source": pk["source"]}
+            "peak_tflops": pk["bf16_tflops"], "frac": tf / pk["bf16_tflops"], "peak_source": pk["source"],
+            "check": check}
 
 
 def forgeml_cases(dev) -> dict:
@@ -465,6 +473,105 @@ def kernel_rooflines(engine, dev, ctx_len: int, ms_per_step: float) -> dict:
     return {"roofline": dominant, "roofline_other": other, "roofline_step": step}
 
 
+def full_normal_weights(cfg, dev, dtype) -> dict:
+    """The whole model of the synthetic initialisation (every rank's shards
+    together) rounded to ``dtype``, as fp32 CPU tensors keyed like the
+    reference TinyDecoder's state dict."""
+    from forgeml_b200.nebula.model import normal_weight
+
+    h = cfg.hidden_size
+
+    def full(key):
+        return normal_weight(cfg, key, dev).to(dtype).float().cpu()
+
+    sd = {"token_embedding.weight": full("tok"), "position_embedding.weight": full("pos"),
+          "lm_head.weight": full("head"), "final_norm.weight": torch.ones(h), "final_norm.bias": torch.zeros(h)}
+    for i in range(cfg.num_layers):
+        for n in ("q", "k", "v", "o", "up", "down"):
+            sd[f"blocks.{i}.{n}.weight"] = full(f"{i}.{n}")
+        for n in ("ln1", "ln2"):
+            sd[f"blocks.{i}.{n}.weight"], sd[f"blocks.{i}.{n}.bias"] = torch.ones(h), torch.zeros(h)
+    return sd
+
+
+def reference_logits(cfg, state_dict: dict, tokens: torch.Tensor) -> tuple[torch.Tensor, str]:
+    """Logits [B, T, V] of the whole model over ``tokens`` on the host cores in
+    fp32: the reference's own TinyDecoder (baseline/_ref) loaded with
+    ``state_dict``, or the CPU oracle restatement when the reference is not
+    installed.  Returns (logits, which)."""
+    ref_root = REPO / "baseline" / "_ref"
+    torch.set_num_threads(os.cpu_count() or 1)
+    if (ref_root / "nebula").is_dir():
+        sys.path.insert(0, str(ref_root))
+        try:
+            from nebula.model import DecoderConfig as RefConfig
+            from nebula.model import TinyDecoder as RefDecoder
+
+            rc = RefConfig(**{f: getattr(cfg, f) for f in ("vocab_size", "hidden_size", "num_heads", "num_layers",
+                                                            "intermediate_size", "max_seq_len", "seed")})
+            with torch.device("meta"):
+                model = RefDecoder(rc)
+            model.load_state_dict(state_dict, assign=True)
+            with torch.inference_mode():
+                return model.eval()(tokens), "reference TinyDecoder (baseline/_ref), fp32 CPU"
+        finally:
+            sys.path.remove(str(ref_root))
+    from oracle import nebula as orc
+
+    w = orc.weights_from_state_dict(state_dict, cfg.num_layers)
+    return orc.forward(w, tokens, cfg.num_heads, cfg.num_layers), "CPU oracle (oracle/nebula.py), fp32"
+
+
+def decode_parity(dec, dev, *, batch: int = BATCH, prompt_len: int = 16, steps: int = 16, tol: float = 2e-2,
+                  min_agree: float = 0.9, ids_base: int = 900, checker: bool = True) -> dict | None:
+    """Greedy decode on the native decoder checked against the reference's
+    own CPU forward.
+
+    Every rank runs the same steps (SPMD: a prefill of ``batch`` seeded
+    prompts of ``prompt_len`` tokens, then ``steps - 1`` single-token greedy
+    steps through the decoder's own path, CUDA graphs and TP collectives
+    included).  On the checking rank the whole model then runs in fp32 on the
+    host (reference_logits) with the bf16-rounded weights over the same token
+    sequence (teacher-forced with the engine's own greedy tokens), and the
+    logits of every step are compared:
+      max_rel_err   max |got - want| / max |want| over the step's logits
+      greedy_agree  fraction of (request, step) whose argmax agrees
+    Returns the summary on the checking rank, None elsewhere."""
+    from forgeml_b200.nebula import ops
+
+    cfg = dec.config
+    g = torch.Generator().manual_seed(7)
+    prompts = torch.randint(0, cfg.vocab_size, (batch, prompt_len), generator=g)
+    ids = tuple(range(ids_base, ids_base + batch))
+    got, toks = [], []
+    with torch.inference_mode():
+        logits = dec.forward(prompts.to(dev), ids, 0, last_only=True)
+        for s_ in range(steps):
+            if s_:
+                logits = dec.forward(toks[-1].view(-1, 1), ids, prompt_len + s_ - 1, last_only=True)
+            got.append(logits[:, -1].float().cpu())
+            toks.append(ops.argmax(logits[:, -1]))
+        dec.cache.release(ids)
+    torch.cuda.synchronize(dev)
+    if not checker:
+        return None
+    t0 = time.perf_counter()
+    sd = full_normal_weights(cfg, dev, dec.dtype)
+    seq = torch.cat([prompts, torch.stack([t.cpu() for t in toks[:-1]], 1)], 1)
+    want_all, which = reference_logits(cfg, sd, seq)
+    del sd
+    errs, agree = [], []
+    for s_ in range(steps):
+        want = want_all[:, prompt_len - 1 + s_].float()
+        errs.append(float((got[s_] - want).abs().max() / want.abs().max()))
+        agree.append((got[s_].argmax(-1) == want.argmax(-1)).float().mean().item())
+    rel, ag = max(errs), sum(agree) / len(agree)
+    return {"max_rel_err": rel, "greedy_agree": ag, "tol": f"{tol:g}", "min_agree": min_agree,
+            "steps": steps, "batch": batch, "prompt_len": prompt_len, "layers": cfg.num_layers,
+            "vs": which + " on the bf16-rounded weights, teacher-forced with the engine's greedy tokens",
+            "check_s": time.perf_counter() - t0, "pass": bool(rel <= tol and ag >= min_agree)}
+
+
 def run_native(args) -> None:
     import torch.distributed as dist
 
@@ -492,6 +599,12 @@ def run_native(args) -> None:
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
+
+    # ---- parity before the timed region: the full model at this N against the CPU oracle
+    parity = None
+    if not args.no_parity:
+        parity = decode_parity(dec, dev, checker=rank == 0)
+        sync_all()
 
     # ---- device-timed decode (SPMD: every rank runs the same steps) ----
     with torch.inference_mode():
@@ -595,7 +708,7 @@ def run_native(args) -> None:
                        "parallelism": f"tp{world}", "cuda_graph": bool(dec.use_cuda_graphs and ctx.pp_size == 1),
                        "l2": "inputs larger than L2 (>3 GB streamed per step)"},
             "e2e": e2e, "gpu_launches": int(per_step_launches * K), "clocks": clk.summary(),
-            "cpu_baseline": cpu, **extra,
+            "cpu_baseline": cpu, "parity": parity, **extra,
         }
         print(json.dumps(line), flush=True)
     if rank == 0:
@@ -606,6 +719,8 @@ def run_native(args) -> None:
         torch.cuda.synchronize(dev)
         dist.barrier()
         ctx.close()
+    if rank == 0 and parity is not None and not parity["pass"]:
+        raise SystemExit(f"decode parity failed: {parity}")
 
 
 C5 = dict(vocab_size=32000, hidden_size=4096, num_heads=32, num_layers=32, intermediate_size=16384,
@@ -744,6 +859,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=("native", "reference"), default="native")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU oracle baseline")
     ap.add_argument("--no-gemm", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the decode before timing")
     ap.add_argument("--cpu-steps", type=int, default=3)
     ap.add_argument("--cpu-layers", type=int, default=None, help="time this many layers of the CPU oracle")
     ap.add_argument("--case", choices=("attention", "gemm-decode", "gemm"), default=None,

@@ -125,6 +125,7 @@ _SIGNATURES = {
     "neb_linear_fused_ok": (_I, [_I64, _I64, _I64, _I]),
     "fml_last_error": (ctypes.c_char_p, []),
     "fml_device_status": (_I, []),
+    "fml_device_status_async": (_I, [_P, _P]),
     "fml_launch_count": (_I64, []),
     "fml_version": (ctypes.c_char_p, []),
 }
@@ -193,6 +194,12 @@ def call(name: str, *args) -> None:
 def device_status() -> int:
     """Read and clear the device error word (synchronises the current device)."""
     return int(load().fml_device_status())
+
+
+def device_status_async(host_dst: torch.Tensor, stream: int) -> None:
+    """Queue a copy of the device error word into ``host_dst`` (a pinned
+    int32 host tensor) on ``stream``; read it once the stream has passed."""
+    call("fml_device_status_async", host_dst.data_ptr(), stream)
 
 
 def launch_count() -> int:

@@ -82,8 +82,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         return lib
     cmd = [nvcc, *ARCH, "-rdc=true", "-shared", "-Xcompiler", "-fPIC", "-o", str(lib)]
     cmd += [str(o) for o in objs]
-    cmd += ["-cudart", "static", "-lcuda" if False else "", "-ldl", "-lpthread", "-lrt"]
-    cmd = [c for c in cmd if c]
+    cmd += ["-cudart", "static", "-ldl", "-lpthread", "-lrt"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -42,7 +42,7 @@ using peer::Ctx;
 using peer::kMaxWorld;
 using peer::ld_acquire_sys;
 using peer::st_release_sys;
-constexpr int kBlocks = peer::kArBlocks;  // fixed grid (one chunk per CTA index)
+constexpr int kBlocks = peer::kArBlocks;  // fixed grid (one chunk per CTA index, every call)
 constexpr int kThreads = 256;
 using Args = peer::View;
 
@@ -131,21 +131,82 @@ __global__ void __launch_bounds__(kThreads) ar_kernel(const Args a, const T* __r
 // slot `rank` of every peer's LL region; a reader polls the pairs of its
 // chunk until every epoch matches, so neither a system fence nor a separate
 // flag round trip sits on the critical path (8-byte aligned accesses are
-// single-copy atomic).  Sums, rounding, epochs (one per CTA index, advanced
-// on the device) and the two buffer sets by epoch parity are those of
-// ar_kernel: CTA b of rank r writes set e&1 of a peer only after it has read
-// that peer's epoch e-1 words of chunk b, written by the peer's next launch
-// after it finished reading set e&1 in epoch e-2.  Twice the bytes of the
-// flag protocol cross NVLink, negligible at decode sizes.
+// single-copy atomic).  Sums, rounding and the two buffer sets by epoch
+// parity are those of ar_kernel.  A reader issues the loads of every peer's
+// words of a vector before it checks any of them, so one memory latency, not
+// one per peer, precedes the sum.
+//
+// Reuse of a buffer set.  The grid is always kBlocks CTAs, so after N calls
+// every CTA index's epoch is N on every rank and a call's epoch parity is the
+// same in all its CTAs.  Call N writes set N&1 of a peer.  Before any write,
+// every CTA of call N has passed griddepcontrol.wait, so this rank's call
+// N-1 has completed; in it CTA 0 (whose chunk is never empty) read words of
+// every peer's call N-1, and each peer wrote those only after its own
+// griddepcontrol.wait, i.e. after the peer's call N-2 -- the last reader of
+// set N&1 -- had completed.  Sizes may change from call to call.
 __device__ __forceinline__ void st_volatile_v2u64(uint64_t* p, uint64_t a, uint64_t b) {
   asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
 }
 __device__ __forceinline__ void ld_volatile_v2u64(const uint64_t* p, uint64_t& a, uint64_t& b) {
   asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
+// Four (epoch, word) pairs = one 16-byte vector of the message.
+__device__ __forceinline__ void ll_load(const uint64_t* p, uint64_t (&w)[4]) {
+  ld_volatile_v2u64(p, w[0], w[1]);
+  ld_volatile_v2u64(p + 2, w[2], w[3]);
+}
+__device__ __forceinline__ bool ll_ready(const uint64_t (&w)[4], uint32_t e) {
+  return ((uint32_t)(w[0] >> 32) == e) & ((uint32_t)(w[1] >> 32) == e) & ((uint32_t)(w[2] >> 32) == e) &
+         ((uint32_t)(w[3] >> 32) == e);
+}
+// Re-reads the pairs at p until all four carry epoch e (bounded: on expiry
+// raises DEV_ERR_AR_TIMEOUT and clears ok, after which nothing waits).
+__device__ __forceinline__ void ll_settle(const uint64_t* p, uint64_t (&w)[4], uint32_t e, long long budget,
+                                          bool& ok) {
+  if (!ok || ll_ready(w, e)) return;
+  const long long t0 = clock64();
+  while (true) {
+    ll_load(p, w);
+    if (ll_ready(w, e)) return;
+    if (clock64() - t0 > budget) {
+      raise_device_error(DEV_ERR_AR_TIMEOUT);
+      ok = false;
+      return;
+    }
+  }
+}
+__device__ __forceinline__ void ll_store(uint64_t* p, uint64_t tag, const uint4& v) {
+  st_volatile_v2u64(p, tag | v.x, tag | v.y);
+  st_volatile_v2u64(p + 2, tag | v.z, tag | v.w);
+}
+__device__ __forceinline__ uint4 ll_words(const uint64_t (&w)[4]) {
+  return make_uint4((uint32_t)w[0], (uint32_t)w[1], (uint32_t)w[2], (uint32_t)w[3]);
+}
+
+// out vector = round(round(sum) + residual) of one 16-byte vector.
+template <typename T>
+__device__ __forceinline__ uint4 finish_vec(const float (&acc)[16 / sizeof(T)], const T* residual, long long i) {
+  constexpr int VE = 16 / sizeof(T);
+  float res[VE];
+  if (residual != nullptr) {
+    const uint4 rv = reinterpret_cast<const uint4*>(residual)[i];
+    const T* re = reinterpret_cast<const T*>(&rv);
+#pragma unroll
+    for (int k = 0; k < VE; ++k) res[k] = to_f32<T>(re[k]);
+  }
+  uint4 o;
+  T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+  for (int k = 0; k < VE; ++k) {
+    float x = to_f32<T>(from_f32<T>(acc[k]));  // the all-reduced partial in the model dtype
+    if (residual != nullptr) x = x + res[k];   // x + part, rounded once more below
+    oe[k] = from_f32<T>(x);
+  }
+  return o;
+}
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads) ar_ll_kernel(const Args a, const T* __restrict__ part,
+__global__ void __launch_bounds__(kThreads) ar_ll_kernel(const __grid_constant__ Args a, const T* __restrict__ part,
                                                          const T* __restrict__ residual, T* __restrict__ out,
                                                          long long nvec) {
   constexpr int VE = 16 / sizeof(T);
@@ -166,61 +227,29 @@ __global__ void __launch_bounds__(kThreads) ar_ll_kernel(const Args a, const T* 
   // 1. push this chunk into slot r of every peer (16 data bytes -> 32 LL bytes)
   for (long long i = v0 + tid; i < v1; i += kThreads) {
     const uint4 v = src[i];
-    for (int q = 0; q < W; ++q) {
-      if (q == r) continue;
-      uint64_t* dst = reinterpret_cast<uint64_t*>(a.base[q] + a.lay.ll_data_off(set, r)) + 4 * i;
-      st_volatile_v2u64(dst, tag | v.x, tag | v.y);
-      st_volatile_v2u64(dst + 2, tag | v.z, tag | v.w);
-    }
+#pragma unroll
+    for (int q = 0; q < kMaxWorld; ++q)
+      if (q < W && q != r) ll_store(reinterpret_cast<uint64_t*>(a.base[q] + a.lay.ll_data_off(set, r)) + 4 * i, tag, v);
   }
-  // 2. gather every rank's words of this chunk in rank order, sum, add the residual
+  // 2. gather every rank's words of this chunk, sum in rank order, add the residual
   bool ok = true;
   for (long long i = v0 + tid; i < v1; i += kThreads) {
+    uint64_t w[kMaxWorld][4];
+#pragma unroll
+    for (int q = 0; q < kMaxWorld; ++q)
+      if (q < W && q != r) ll_load(reinterpret_cast<const uint64_t*>(a.base[r] + a.lay.ll_data_off(set, q)) + 4 * i, w[q]);
+#pragma unroll
+    for (int q = 0; q < kMaxWorld; ++q)
+      if (q < W && q != r)
+        ll_settle(reinterpret_cast<const uint64_t*>(a.base[r] + a.lay.ll_data_off(set, q)) + 4 * i, w[q], e,
+                  a.timeout_cycles, ok);
     float acc[VE];
 #pragma unroll
     for (int k = 0; k < VE; ++k) acc[k] = 0.f;
-    for (int q = 0; q < W; ++q) {
-      uint4 words;
-      if (q == r) {
-        words = src[i];
-      } else {
-        const uint64_t* ps = reinterpret_cast<const uint64_t*>(a.base[r] + a.lay.ll_data_off(set, q)) + 4 * i;
-        uint64_t w0, w1, w2, w3;
-        ld_volatile_v2u64(ps, w0, w1);
-        ld_volatile_v2u64(ps + 2, w2, w3);
-        if (ok && ((w0 >> 32) != e || (w1 >> 32) != e || (w2 >> 32) != e || (w3 >> 32) != e)) {
-          const long long t0 = clock64();
-          while (true) {
-            ld_volatile_v2u64(ps, w0, w1);
-            ld_volatile_v2u64(ps + 2, w2, w3);
-            if ((w0 >> 32) == e && (w1 >> 32) == e && (w2 >> 32) == e && (w3 >> 32) == e) break;
-            if (clock64() - t0 > a.timeout_cycles) {
-              raise_device_error(DEV_ERR_AR_TIMEOUT);
-              ok = false;
-              break;
-            }
-          }
-        }
-        words = make_uint4((uint32_t)w0, (uint32_t)w1, (uint32_t)w2, (uint32_t)w3);
-      }
-      add_vec<T>(acc, words);
-    }
-    float res[VE];
-    if (residual != nullptr) {
-      const uint4 rv = reinterpret_cast<const uint4*>(residual)[i];
-      const T* re = reinterpret_cast<const T*>(&rv);
 #pragma unroll
-      for (int k = 0; k < VE; ++k) res[k] = to_f32<T>(re[k]);
-    }
-    uint4 o;
-    T* oe = reinterpret_cast<T*>(&o);
-#pragma unroll
-    for (int k = 0; k < VE; ++k) {
-      float x = to_f32<T>(from_f32<T>(acc[k]));
-      if (residual != nullptr) x = x + res[k];
-      oe[k] = from_f32<T>(x);
-    }
-    reinterpret_cast<uint4*>(out)[i] = o;
+    for (int q = 0; q < kMaxWorld; ++q)
+      if (q < W) add_vec<T>(acc, q == r ? src[i] : ll_words(w[q]));
+    reinterpret_cast<uint4*>(out)[i] = finish_vec<T>(acc, residual, i);
   }
   __syncthreads();
   if (tid == 0) epochs[blk] = e;
@@ -239,11 +268,12 @@ __global__ void __launch_bounds__(kThreads) ar_ll_kernel(const Args a, const T* 
 // A rank sends 2 (W-1)/W of the message (x2 for the pairs) instead of W-1
 // copies, for one more NVLink hop.  No wait precedes a send that another rank
 // waits for (sends of step 1 come first; step 2's sends need only step 1's
-// data), so the steps cannot deadlock.  Reuse of a buffer set follows the LL
-// argument: rank r writes a rank's set e&1 in epoch e only for positions it
-// had, in epoch e-1, read words of that rank's epoch e-1 launch about (its
-// all-gather words for the reduce-scatter area, its reduce-scatter words for
-// the all-gather area), so that rank had finished epoch e-2.
+// data), so the steps cannot deadlock.  Buffer-set reuse follows the
+// one-shot kernel's argument: every output vector of chunk 0 in call N-1 is
+// a sum of words that every rank wrote in call N-1 after its
+// griddepcontrol.wait (directly for the owner, through the owner's
+// all-gather words for the others), so each peer's call N-2 had completed
+// before this rank's call N-1 could finish.
 template <typename T>
 __global__ void __launch_bounds__(kThreads) ar_ts_kernel(const __grid_constant__ Args a, const T* __restrict__ part,
                                                          const T* __restrict__ residual, T* __restrict__ out,
@@ -265,73 +295,45 @@ __global__ void __launch_bounds__(kThreads) ar_ts_kernel(const __grid_constant__
   const long long len = v1 - v0;
   const uint4* src = reinterpret_cast<const uint4*>(part);
   auto owner = [&](long long i) { return (int)(((i - v0) * W) / len); };
-  auto poll4 = [&](const uint64_t* ps, bool& ok) {
-    uint64_t w0, w1, w2, w3;
-    ld_volatile_v2u64(ps, w0, w1);
-    ld_volatile_v2u64(ps + 2, w2, w3);
-    if (ok && ((w0 >> 32) != e || (w1 >> 32) != e || (w2 >> 32) != e || (w3 >> 32) != e)) {
-      const long long t0 = clock64();
-      while (true) {
-        ld_volatile_v2u64(ps, w0, w1);
-        ld_volatile_v2u64(ps + 2, w2, w3);
-        if ((w0 >> 32) == e && (w1 >> 32) == e && (w2 >> 32) == e && (w3 >> 32) == e) break;
-        if (clock64() - t0 > a.timeout_cycles) {
-          raise_device_error(DEV_ERR_AR_TIMEOUT);
-          ok = false;
-          break;
-        }
-      }
-    }
-    return make_uint4((uint32_t)w0, (uint32_t)w1, (uint32_t)w2, (uint32_t)w3);
-  };
   // 1. reduce-scatter sends
   for (long long i = v0 + tid; i < v1; i += kThreads) {
     const int o = owner(i);
     if (o == r) continue;
-    const uint4 v = src[i];
-    uint64_t* dst = reinterpret_cast<uint64_t*>(a.base[o] + a.lay.ts_rs_off(set, r)) + 4 * i;
-    st_volatile_v2u64(dst, tag | v.x, tag | v.y);
-    st_volatile_v2u64(dst + 2, tag | v.z, tag | v.w);
+    ll_store(reinterpret_cast<uint64_t*>(a.base[o] + a.lay.ts_rs_off(set, r)) + 4 * i, tag, src[i]);
   }
   bool ok = true;
   // 2. owned vectors: reduce in rank order, add the residual, all-gather sends
   for (long long i = v0 + tid; i < v1; i += kThreads) {
     if (owner(i) != r) continue;
+    uint64_t w[kMaxWorld][4];
+#pragma unroll
+    for (int q = 0; q < kMaxWorld; ++q)
+      if (q < W && q != r) ll_load(reinterpret_cast<const uint64_t*>(a.base[r] + a.lay.ts_rs_off(set, q)) + 4 * i, w[q]);
+#pragma unroll
+    for (int q = 0; q < kMaxWorld; ++q)
+      if (q < W && q != r)
+        ll_settle(reinterpret_cast<const uint64_t*>(a.base[r] + a.lay.ts_rs_off(set, q)) + 4 * i, w[q], e,
+                  a.timeout_cycles, ok);
     float acc[VE];
 #pragma unroll
     for (int k = 0; k < VE; ++k) acc[k] = 0.f;
-    for (int q = 0; q < W; ++q) {
-      const uint4 words =
-          q == r ? src[i] : poll4(reinterpret_cast<const uint64_t*>(a.base[r] + a.lay.ts_rs_off(set, q)) + 4 * i, ok);
-      add_vec<T>(acc, words);
-    }
-    float res[VE];
-    if (residual != nullptr) {
-      const uint4 rv = reinterpret_cast<const uint4*>(residual)[i];
-      const T* re = reinterpret_cast<const T*>(&rv);
 #pragma unroll
-      for (int k = 0; k < VE; ++k) res[k] = to_f32<T>(re[k]);
-    }
-    uint4 o;
-    T* oe = reinterpret_cast<T*>(&o);
-#pragma unroll
-    for (int k = 0; k < VE; ++k) {
-      float x = to_f32<T>(from_f32<T>(acc[k]));
-      if (residual != nullptr) x = x + res[k];
-      oe[k] = from_f32<T>(x);
-    }
+    for (int q = 0; q < kMaxWorld; ++q)
+      if (q < W) add_vec<T>(acc, q == r ? src[i] : ll_words(w[q]));
+    const uint4 o = finish_vec<T>(acc, residual, i);
     reinterpret_cast<uint4*>(out)[i] = o;
-    for (int q = 0; q < W; ++q) {
-      if (q == r) continue;
-      uint64_t* dst = reinterpret_cast<uint64_t*>(a.base[q] + a.lay.ts_ag_off(set)) + 4 * i;
-      st_volatile_v2u64(dst, tag | o.x, tag | o.y);
-      st_volatile_v2u64(dst + 2, tag | o.z, tag | o.w);
-    }
+#pragma unroll
+    for (int q = 0; q < kMaxWorld; ++q)
+      if (q < W && q != r) ll_store(reinterpret_cast<uint64_t*>(a.base[q] + a.lay.ts_ag_off(set)) + 4 * i, tag, o);
   }
   // 3. all-gather receives
   for (long long i = v0 + tid; i < v1; i += kThreads) {
     if (owner(i) == r) continue;
-    reinterpret_cast<uint4*>(out)[i] = poll4(reinterpret_cast<const uint64_t*>(a.base[r] + a.lay.ts_ag_off(set)) + 4 * i, ok);
+    const uint64_t* p = reinterpret_cast<const uint64_t*>(a.base[r] + a.lay.ts_ag_off(set)) + 4 * i;
+    uint64_t w[4];
+    ll_load(p, w);
+    ll_settle(p, w, e, a.timeout_cycles, ok);
+    reinterpret_cast<uint4*>(out)[i] = ll_words(w);
   }
   __syncthreads();
   if (tid == 0) epochs[blk] = e;

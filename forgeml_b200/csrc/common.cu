@@ -76,6 +76,13 @@ int fml_device_status(void) {
   return v;
 }
 
+int fml_device_status_async(int32_t* host_dst, void* stream) {
+  if (!host_dst) return fml::fail(FML_EINVAL, "fml_device_status_async: null destination");
+  return fml::check_cuda(cudaMemcpyFromSymbolAsync(host_dst, fml::g_device_error, sizeof(int), 0,
+                                                   cudaMemcpyDeviceToHost, reinterpret_cast<cudaStream_t>(stream)),
+                         "fml_device_status_async");
+}
+
 int64_t fml_launch_count(void) { return fml::g_launches.load(); }
 
 const char* fml_version(void) { return "forgeml_b200 0.1.0 (sm_100a)"; }

@@ -26,7 +26,7 @@ namespace fml {
 namespace peer {
 
 constexpr int kMaxWorld = 8;
-constexpr int kArBlocks = 32;      // chunks (and CTAs) of the standalone all-reduce
+constexpr int kArBlocks = 128;     // chunks (and CTAs) of the standalone all-reduce
 constexpr int kSubFeatures = 16;   // features per sub-block of the fused exchange
 constexpr int kSubTokens = 32;     // token capacity of a sub-block (the decode GEMM's BN)
 

@@ -1,17 +1,31 @@
-"""Contiguous per-request KV cache backed by one pool per layer.
+"""Per-request KV cache of the Nebula decoder, held in one slot pool per layer.
 
-Same API, validation and error behaviour as the reference KVCache
-(src/nebula/cache.py:10-172).  Storage differs: instead of allocating two
-fresh [heads, max_seq_len, head_dim] tensors per request per layer at
-``reserve`` time, each owned layer has one pool [max_requests, heads,
-max_seq_len, head_dim] for K and one for V, allocated once; a request owns a
-pool slot.  A request's per-layer buffer is therefore a view with exactly the
-reference's [heads, max_seq_len, head_dim] layout and indexing, and the
-decode kernels address every request of a batch through the slot table
-without the reference's per-step ``torch.stack`` of the whole prefix.
+Public surface of the reference KVCache (src/nebula/cache.py:10-172): the
+keyword constructor, ``reserve`` / ``validate`` / ``append`` / ``release`` /
+``clear`` / ``active_requests``, CacheError with the same conditions and
+message texts.  The storage is designed for the decode kernels instead:
+
+* every owned layer has one K pool and one V pool of shape
+  [max_requests, heads, max_seq_len, head_dim], allocated once; a request is
+  given a pool slot at ``reserve`` and keeps it until ``release``.  The slot's
+  [heads, max_seq_len, head_dim] block has the reference's per-request buffer
+  layout, so position p of head h lives where the reference puts it;
+* the kernels address a whole batch through an int32 slot table (``slots``)
+  and the step's start positions, reading keys in place -- no per-step stack
+  of the prefix;
+* bookkeeping is one ``_Ticket`` per request: its slot and the number of
+  positions held for each owned layer.  The fused decode step writes K/V of
+  every layer inside its kernels and records the new length of all layers at
+  once (``advance``).
+
+``append`` keeps the reference's contract (write [B, heads, T, hd] at
+``start_pos``, return the stacked prefixes [B, heads, end, hd] as a copy) for
+callers of the reference API; the decoder itself never uses it.
 """
 
 from __future__ import annotations
+
+import heapq
 
 import torch
 
@@ -20,115 +34,155 @@ class CacheError(RuntimeError):
     pass
 
 
-def _is_int(v) -> bool:
+_ID_LIMIT = 1 << 63
+
+
+def _plain_int(v) -> bool:
     return isinstance(v, int) and not isinstance(v, bool)
 
 
+class _Ticket:
+    """A reserved request: its pool slot and positions held per owned layer."""
+
+    __slots__ = ("slot", "held")
+
+    def __init__(self, slot: int, layer_ids: tuple[int, ...]):
+        self.slot = slot
+        self.held = dict.fromkeys(layer_ids, 0)
+
+
 class KVCache:
-    def __init__(
-        self,
-        *,
-        layer_ids: tuple[int, ...],
-        num_heads: int,
-        head_dim: int,
-        max_seq_len: int,
-        max_requests: int,
-        device: torch.device,
-        dtype: torch.dtype,
-    ):
-        for name, v in (("num_heads", num_heads), ("head_dim", head_dim), ("max_seq_len", max_seq_len),
-                        ("max_requests", max_requests)):
-            if not _is_int(v) or v <= 0:
-                raise CacheError(f"{name} must be a positive integer")
-        if not layer_ids or any(not _is_int(i) or i < 0 for i in layer_ids) or len(set(layer_ids)) != len(layer_ids):
+    def __init__(self, *, layer_ids: tuple[int, ...], num_heads: int, head_dim: int, max_seq_len: int,
+                 max_requests: int, device: torch.device, dtype: torch.dtype):
+        sizes = {"num_heads": num_heads, "head_dim": head_dim, "max_seq_len": max_seq_len,
+                 "max_requests": max_requests}
+        bad = next((k for k, v in sizes.items() if not _plain_int(v) or v <= 0), None)
+        if bad is not None:
+            raise CacheError(f"{bad} must be a positive integer")
+        ids = tuple(layer_ids) if layer_ids else ()
+        if not ids or len(set(ids)) != len(ids) or not all(_plain_int(i) and i >= 0 for i in ids):
             raise CacheError("layer_ids must be unique non-negative integers")
         if not isinstance(device, torch.device):
             raise CacheError("device must be a torch.device")
         if not isinstance(dtype, torch.dtype):
             raise CacheError("dtype must be a torch.dtype")
-        self.layer_ids = tuple(layer_ids)
-        self.num_heads = num_heads
-        self.head_dim = head_dim
-        self.max_seq_len = max_seq_len
-        self.max_requests = max_requests
-        self.device = device
-        self.dtype = dtype
-        shape = (max_requests, num_heads, max_seq_len, head_dim)
-        self.k_pool = {lid: torch.empty(shape, device=device, dtype=dtype) for lid in self.layer_ids}
-        self.v_pool = {lid: torch.empty(shape, device=device, dtype=dtype) for lid in self.layer_ids}
-        # request id -> {layer id -> [k view, v view, length]} (reference bookkeeping shape)
-        self._entries: dict[int, dict[int, list]] = {}
-        self._slot: dict[int, int] = {}
-        self._free = list(range(max_requests - 1, -1, -1))  # pop() yields the lowest slot
+        self.layer_ids = ids
+        self.num_heads, self.head_dim = num_heads, head_dim
+        self.max_seq_len, self.max_requests = max_seq_len, max_requests
+        self.device, self.dtype = device, dtype
+        pool_shape = (max_requests, num_heads, max_seq_len, head_dim)
+        self.k_pool = {lid: torch.empty(pool_shape, device=device, dtype=dtype) for lid in ids}
+        self.v_pool = {lid: torch.empty(pool_shape, device=device, dtype=dtype) for lid in ids}
+        self._tickets: dict[int, _Ticket] = {}
+        self._free_slots = list(range(max_requests))  # min-heap: the lowest free slot goes first
 
+    # ----------------------------------------------------------- inspection
     @property
     def active_requests(self) -> int:
-        return len(self._entries)
+        return len(self._tickets)
 
-    def _check_ids(self, request_ids: tuple[int, ...]) -> None:
+    def holds(self, request_id: int) -> bool:
+        return request_id in self._tickets
+
+    def slots(self, request_ids: tuple[int, ...]) -> list[int]:
+        """Pool slot of each request, in batch order (the kernels' slot table)."""
+        return [self._tickets[r].slot for r in request_ids]
+
+    # ---------------------------------------------------------- validation
+    @staticmethod
+    def check_ids(request_ids: tuple[int, ...]) -> None:
         if not request_ids:
             raise CacheError("request_ids must be non-empty")
-        if len(set(request_ids)) != len(request_ids):
-            raise CacheError("duplicate request ids")
+        seen = set()
         for r in request_ids:
-            if not _is_int(r) or r < 0 or r >= 1 << 63:
+            if not _plain_int(r) or not 0 <= r < _ID_LIMIT:
                 raise CacheError(f"invalid request id {r!r}")
+            if r in seen:
+                raise CacheError("duplicate request ids")
+            seen.add(r)
 
-    def reserve(self, request_ids: tuple[int, ...]) -> None:
-        self._check_ids(request_ids)
-        for r in request_ids:
-            if r in self._entries:
-                raise CacheError(f"request id {r} already reserved")
-        if len(self._entries) + len(request_ids) > self.max_requests:
+    def check_admission(self, request_ids: tuple[int, ...]) -> None:
+        """Raise CacheError unless ``reserve(request_ids)`` would succeed."""
+        self.check_ids(request_ids)
+        taken = next((r for r in request_ids if r in self._tickets), None)
+        if taken is not None:
+            raise CacheError(f"request id {taken} already reserved")
+        if len(self._tickets) + len(request_ids) > self.max_requests:
             raise CacheError("cache capacity exceeded")
-        for r in request_ids:
-            s = self._free.pop()
-            self._slot[r] = s
-            self._entries[r] = {lid: [self.k_pool[lid][s], self.v_pool[lid][s], 0] for lid in self.layer_ids}
+
+    def _tickets_of(self, request_ids: tuple[int, ...]) -> list[_Ticket]:
+        self.check_ids(request_ids)
+        missing = next((r for r in request_ids if r not in self._tickets), None)
+        if missing is not None:
+            raise CacheError(f"request id {missing} is not reserved")
+        return [self._tickets[r] for r in request_ids]
 
     def validate(self, request_ids: tuple[int, ...], start_pos: int, count: int) -> None:
-        self._check_ids(request_ids)
-        for r in request_ids:
-            if r not in self._entries:
-                raise CacheError(f"request id {r} is not reserved")
-        for name, v in (("start_pos", start_pos), ("count", count)):
-            if not _is_int(v):
-                raise CacheError(f"{name} must be an integer")
+        """Raise CacheError unless every owned layer of every request holds
+        exactly ``start_pos`` positions and ``count`` more fit."""
+        tickets = self._tickets_of(request_ids)
+        if not _plain_int(start_pos):
+            raise CacheError("start_pos must be an integer")
+        if not _plain_int(count):
+            raise CacheError("count must be an integer")
         if count <= 0:
             raise CacheError("count must be positive")
         if start_pos < 0 or start_pos + count > self.max_seq_len:
             raise CacheError("positions out of range")
-        for r in request_ids:
-            for lid, (_, _, length) in self._entries[r].items():
-                if length != start_pos:
-                    raise CacheError(f"layer {lid} for request {r} at {length}, expected {start_pos}")
+        for r, tk in zip(request_ids, tickets):
+            for lid, n in tk.held.items():
+                if n != start_pos:
+                    raise CacheError(f"layer {lid} for request {r} at {n}, expected {start_pos}")
 
-    def slots(self, request_ids: tuple[int, ...]) -> list[int]:
-        """Pool slot of each request (the kernels' slot table)."""
-        return [self._slot[r] for r in request_ids]
+    # -------------------------------------------------------------- updates
+    def reserve(self, request_ids: tuple[int, ...]) -> None:
+        self.check_admission(request_ids)
+        for r in request_ids:
+            self._tickets[r] = _Ticket(heapq.heappop(self._free_slots), self.layer_ids)
 
     def advance(self, request_ids: tuple[int, ...], end: int) -> None:
-        """Record that every owned layer of these requests now holds ``end`` positions
-        (after a fused forward wrote them through the native append kernel)."""
+        """Record that every owned layer of these requests now holds ``end``
+        positions (the decode kernels wrote them)."""
         for r in request_ids:
-            for e in self._entries[r].values():
-                e[2] = end
+            held = self._tickets[r].held
+            for lid in held:
+                held[lid] = end
 
-    def _check_append(self, layer_id, request_ids, key, value, start_pos) -> int:
-        if layer_id not in self.layer_ids:
+    def append(self, layer_id: int, request_ids: tuple[int, ...], key: torch.Tensor, value: torch.Tensor,
+               start_pos: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """Reference-compatible append: write [B, heads, T, hd] at ``start_pos``
+        and return the stacked prefixes [B, heads, start_pos+T, hd] (a copy)."""
+        tickets = self._check_append(layer_id, request_ids, key, value, start_pos)
+        end = start_pos + key.shape[2]
+        kp, vp = self.k_pool[layer_id], self.v_pool[layer_id]
+        if self.device.type == "cuda":
+            from forgeml_b200.nebula import ops
+
+            b = len(request_ids)
+            slot_t = torch.tensor([tk.slot for tk in tickets], dtype=torch.int32, device=self.device)
+            start_t = torch.full((b,), start_pos, dtype=torch.int32, device=self.device)
+            ops.kv_append(key.transpose(1, 2), value.transpose(1, 2), kp, vp, slot_t, start_t)
+        else:
+            for i, tk in enumerate(tickets):
+                kp[tk.slot, :, start_pos:end].copy_(key[i])
+                vp[tk.slot, :, start_pos:end].copy_(value[i])
+        for tk in tickets:
+            tk.held[layer_id] = end
+        index = torch.tensor([tk.slot for tk in tickets], device=self.device)
+        return kp.index_select(0, index)[:, :, :end], vp.index_select(0, index)[:, :, :end]
+
+    def _check_append(self, layer_id, request_ids, key, value, start_pos) -> list[_Ticket]:
+        if layer_id not in self.k_pool:
             raise CacheError(f"layer {layer_id} not owned by this cache")
-        self._check_ids(request_ids)
-        for r in request_ids:
-            if r not in self._entries:
-                raise CacheError(f"request id {r} is not reserved")
+        tickets = self._tickets_of(request_ids)
         if not isinstance(key, torch.Tensor) or not isinstance(value, torch.Tensor):
             raise CacheError("key/value must be torch.Tensor")
-        if not _is_int(start_pos):
+        if not _plain_int(start_pos):
             raise CacheError("start_pos must be an integer")
         if key.dim() != 4 or value.dim() != 4:
             raise CacheError("key/value must be [B, heads, T, head_dim]")
         b, heads, count, hd = key.shape
-        if b != len(request_ids) or heads != self.num_heads or hd != self.head_dim or value.shape != key.shape:
+        if (b, heads, hd) != (len(request_ids), self.num_heads, self.head_dim) or value.shape != key.shape:
             raise CacheError(f"bad key/value shape {tuple(key.shape)}")
         if count <= 0 or start_pos < 0 or start_pos + count > self.max_seq_len:
             raise CacheError("positions out of range")
@@ -136,50 +190,23 @@ class KVCache:
             raise CacheError("key/value dtype mismatch")
         if key.device != self.device or value.device != self.device:
             raise CacheError("key/value device mismatch")
-        for r in request_ids:
-            for lid, (_, _, length) in self._entries[r].items():
-                if lid == layer_id:
-                    if length != start_pos:
-                        raise CacheError(f"layer {layer_id} request {r} at {length}, expected {start_pos}")
-                elif length not in (start_pos, start_pos + count):
+        # Layers are appended one after another within a step: the layer being
+        # written must be at start_pos, the others at start_pos or already past it.
+        for r, tk in zip(request_ids, tickets):
+            for lid, n in tk.held.items():
+                if lid == layer_id and n != start_pos:
+                    raise CacheError(f"layer {layer_id} request {r} at {n}, expected {start_pos}")
+                if lid != layer_id and n not in (start_pos, start_pos + count):
                     raise CacheError(
-                        f"layer {lid} request {r} at {length} while appending layer {layer_id} at {start_pos}+{count}"
-                    )
-        return count
-
-    def append(self, layer_id: int, request_ids: tuple[int, ...], key: torch.Tensor, value: torch.Tensor,
-               start_pos: int) -> tuple[torch.Tensor, torch.Tensor]:
-        """Reference-compatible append: write [B, heads, T, hd] at ``start_pos`` and
-        return the stacked prefixes [B, heads, end, hd] (a copy, as the reference)."""
-        count = self._check_append(layer_id, request_ids, key, value, start_pos)
-        end = start_pos + count
-        if self.device.type == "cuda":
-            from forgeml_b200.nebula import ops
-
-            slot_t = torch.tensor(self.slots(request_ids), dtype=torch.int32, device=self.device)
-            start_t = torch.full((len(request_ids),), start_pos, dtype=torch.int32, device=self.device)
-            ops.kv_append(key.transpose(1, 2), value.transpose(1, 2), self.k_pool[layer_id],
-                          self.v_pool[layer_id], slot_t, start_t)
-        else:
-            for i, r in enumerate(request_ids):
-                kbuf, vbuf, _ = self._entries[r][layer_id]
-                kbuf[:, start_pos:end].copy_(key[i])
-                vbuf[:, start_pos:end].copy_(value[i])
-        ks, vs = [], []
-        for r in request_ids:
-            ent = self._entries[r][layer_id]
-            ent[2] = end
-            ks.append(ent[0][:, :end])
-            vs.append(ent[1][:, :end])
-        return torch.stack(ks), torch.stack(vs)
+                        f"layer {lid} request {r} at {n} while appending layer {layer_id} at {start_pos}+{count}")
+        return tickets
 
     def release(self, request_ids: tuple[int, ...]) -> None:
         for r in request_ids:
-            if self._entries.pop(r, None) is not None:
-                self._free.append(self._slot.pop(r))
-        self._free.sort(reverse=True)
+            tk = self._tickets.pop(r, None)
+            if tk is not None:
+                heapq.heappush(self._free_slots, tk.slot)
 
     def clear(self) -> None:
-        self._entries.clear()
-        self._slot.clear()
-        self._free = list(range(self.max_requests - 1, -1, -1))
+        self._tickets.clear()
+        self._free_slots = list(range(self.max_requests))

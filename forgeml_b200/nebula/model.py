@@ -97,3 +97,35 @@ class TinyDecoder(nn.Module):
         for block in self.blocks:
             x = block(x)
         return self.lm_head(self.final_norm(x))
+
+
+def _normal_index(key: str) -> int:
+    """Generator stream of weight ``key`` in the synthetic initialisation."""
+    fixed = {"tok": 0, "pos": 1, "head": 2}
+    if key in fixed:
+        return fixed[key]
+    layer, name = key.split(".")
+    return 16 + 8 * int(layer) + ("q", "k", "v", "o", "up", "down").index(name)
+
+
+def normal_weight_shape(config: DecoderConfig, key: str) -> tuple[int, int]:
+    h, f, v = config.hidden_size, config.intermediate_size, config.vocab_size
+    if key in ("tok", "head"):
+        return (v, h)
+    if key == "pos":
+        return (config.max_seq_len, h)
+    name = key.split(".")[1]
+    return {"up": (f, h), "down": (h, f)}.get(name, (h, h))
+
+
+def normal_weight(config: DecoderConfig, key: str, device, std: float = 0.02) -> torch.Tensor:
+    """Full fp32 weight ``key`` of the synthetic benchmark initialisation:
+    every matrix ~ N(0, std), drawn on ``device`` from its own generator seeded
+    with ``seed * 1_000_003 + stream`` (keys: tok, pos, head, and per layer l
+    "l.q", "l.k", "l.v", "l.o", "l.up", "l.down" in nn.Linear [out, in]
+    layout).  Every TP rank draws the full tensor and keeps its shard, so the
+    shards of one model agree, and a checker can rebuild the whole model."""
+    g = torch.Generator(device=device)
+    g.manual_seed(config.seed * 1_000_003 + _normal_index(key))
+    return torch.empty(normal_weight_shape(config, key), device=device, dtype=torch.float32).normal_(0.0, std, generator=g)
+

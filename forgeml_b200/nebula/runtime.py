@@ -38,12 +38,8 @@ cache slots are device inputs, so one graph serves every step).
 
 from __future__ import annotations
 
-import contextlib
 import ctypes
-import hashlib
 import os
-import threading
-from dataclasses import asdict
 
 import torch
 import torch.distributed as dist
@@ -53,22 +49,10 @@ from torch.profiler import record_function
 from forgeml_b200 import _native
 from forgeml_b200.linear import PackedLinear, ln_fold_vectors
 from forgeml_b200.nebula import ops
-from forgeml_b200.nebula.cache import CacheError, KVCache
-from forgeml_b200.nebula.model import DecoderConfig, TinyDecoder
+from forgeml_b200.nebula.cache import KVCache
+from forgeml_b200.nebula.model import DecoderConfig, TinyDecoder, normal_weight
 from forgeml_b200.nebula.parallel import ParallelContext
 from forgeml_b200.nebula import peer
-
-CMD_STOP = 0
-CMD_STEP = 1
-CMD_RELEASE = 2
-_GENERATE_ID_BASE = 1 << 62
-_MAX_REQUEST_ID = (1 << 62) - 1
-_DEFAULT_CONFIG = DecoderConfig()
-
-
-class EngineFailed(RuntimeError):
-    pass
-
 
 class _Gemm:
     """Launches y = x @ W^T (+ epilogue) for a fixed nn.Linear-layout weight W [N, K]."""
@@ -211,26 +195,23 @@ class ShardedDecoder(nn.Module):
                 self.head = put(ref.lm_head.weight)
             del ref
         else:
-            def draw(shape, idx):
-                g = torch.Generator(device=dev)
-                g.manual_seed(config.seed * 1_000_003 + idx)
-                return torch.empty(shape, device=dev, dtype=torch.float32).normal_(0.0, init_std, generator=g)
+            def draw(key):
+                return normal_weight(config, key, dev, init_std)
 
             ones = torch.ones(h, device=dev, dtype=dtype)
             zeros = torch.zeros(h, device=dev, dtype=dtype)
             for lid in self.owned_layer_ids:
-                base = 16 + 8 * lid
-                q, k, v = (draw((h, h), base + i)[row_lo:row_hi] for i in range(3))
+                q, k, v = (draw(f"{lid}.{n}")[row_lo:row_hi] for n in ("q", "k", "v"))
                 self.layers.append(_Layer(
                     ones.clone(), zeros.clone(), ones.clone(), zeros.clone(), put(torch.cat([q, k, v])),
-                    put(draw((h, h), base + 3)[:, row_lo:row_hi]), put(draw((f, h), base + 4)[f_lo:f_hi]),
-                    put(draw((h, f), base + 5)[:, f_lo:f_hi]), self.workspace))
+                    put(draw(f"{lid}.o")[:, row_lo:row_hi]), put(draw(f"{lid}.up")[f_lo:f_hi]),
+                    put(draw(f"{lid}.down")[:, f_lo:f_hi]), self.workspace))
             if self.is_first:
-                self.tok_emb = put(draw((config.vocab_size, h), 0))
-                self.pos_emb = put(draw((config.max_seq_len, h), 1))
+                self.tok_emb = put(draw("tok"))
+                self.pos_emb = put(draw("pos"))
             if self.is_last:
                 self.lnf_w, self.lnf_b = ones.clone(), zeros.clone()
-                self.head = put(draw((config.vocab_size, h), 2))
+                self.head = put(draw("head"))
         if self.is_last:
             self.head_gemm = _linear(self.head, self.workspace)
         self.cache = KVCache(layer_ids=self.owned_layer_ids, num_heads=self.num_heads_local, head_dim=self.head_dim,
@@ -492,292 +473,6 @@ def decode_ln_mode() -> str:
     return v if v in ("fold", "prologue", "kernel") else "fold"
 
 
-def _validate_prompt(config: DecoderConfig, prompt: list[int], max_new: int) -> None:
-    if not isinstance(prompt, (list, tuple)) or not prompt:
-        raise ValueError("prompt must be a non-empty list of token ids")
-    for tok in prompt:
-        if not isinstance(tok, int) or isinstance(tok, bool):
-            raise TypeError("prompt token ids must be ints")
-        if tok < 0 or tok >= config.vocab_size:
-            raise ValueError(f"token id {tok} out of range")
-    if not isinstance(max_new, int) or isinstance(max_new, bool) or max_new < 0:
-        raise ValueError("max_new_tokens must be a non-negative int")
-    if len(prompt) + max_new > config.max_seq_len:
-        raise ValueError("prompt length + max_new_tokens exceeds max_seq_len")
-
-
-class Engine:
-    """Leader/worker serving engine (protocol of src/nebula/runtime.py:206-516).
-
-    ``decoder_factory(config, context, dtype=..., max_requests=...)`` builds the
-    decoder; the default is the native ``ShardedDecoder``.  Tests that exercise
-    the protocol on CPU (Gloo) inject a CPU decoder here; the product path has
-    no CPU decoder.
-    """
-
-    def __init__(self, config: DecoderConfig = _DEFAULT_CONFIG, *, context: ParallelContext | None = None,
-                 dtype: torch.dtype = torch.float32, max_requests: int = 32, decoder_factory=None,
-                 init: str = "reference"):
-        self._owns_context = context is None
-        if context is None:
-            context = ParallelContext.from_env(device="cuda" if torch.cuda.is_available() else "cpu")
-        if not isinstance(max_requests, int) or isinstance(max_requests, bool) or max_requests <= 0:
-            raise ValueError("max_requests must be a positive integer")
-        if dtype not in (torch.float32, torch.float16, torch.bfloat16):
-            raise ValueError(f"unsupported dtype {dtype}")
-        if context.device.type != "cuda" and dtype != torch.float32:
-            raise ValueError("low-precision dtype requires CUDA")
-        self.config = config
-        self.context = context
-        self.max_requests = max_requests
-        if dist.is_available() and dist.is_initialized():
-            self._comm_device = context.device if dist.get_backend() == "nccl" else torch.device("cpu")
-        else:
-            self._comm_device = torch.device("cpu")
-        if self._world():
-            digest = hashlib.sha256(repr((asdict(config), str(dtype), max_requests)).encode()).digest()
-            expected = int.from_bytes(digest[:8], "little", signed=True)
-            wire = torch.tensor([expected], dtype=torch.int64, device=self._comm_device)
-            dist.broadcast(wire, src=0)
-            if int(wire.cpu().item()) != expected:
-                raise EngineFailed("engine configuration differs across ranks")
-        if decoder_factory is None:
-            self.decoder = ShardedDecoder(config, context, dtype=dtype, max_requests=max_requests, init=init)
-        else:
-            self.decoder = decoder_factory(config, context, dtype=dtype, max_requests=max_requests)
-        self._healthy = True
-        self._closed = False
-        self._lock = threading.RLock()
-        self._gen_counter = _GENERATE_ID_BASE
-
-    @property
-    def healthy(self) -> bool:
-        return self._healthy and not self._closed
-
-    @property
-    def _is_leader(self) -> bool:
-        return self.context.rank == 0
-
-    def _world(self) -> bool:
-        return self.context.world_size > 1 and dist.is_initialized()
-
-    def _validate_request(self, tokens, request_ids, start_pos, internal=False) -> None:
-        if not isinstance(tokens, torch.Tensor):
-            raise TypeError("tokens must be a torch.Tensor")
-        if tokens.dtype != torch.long:
-            raise ValueError("tokens must be a long tensor")
-        if tokens.dim() != 2 or tokens.shape[0] == 0 or tokens.shape[1] == 0:
-            raise ValueError("tokens must have shape [B, T] with B, T >= 1")
-        if tokens.shape[0] != len(request_ids):
-            raise ValueError("request_ids must match batch size")
-        if tokens.shape[0] > self.max_requests:
-            raise ValueError("batch exceeds max_requests")
-        if not isinstance(start_pos, int) or isinstance(start_pos, bool):
-            raise TypeError("start_pos must be an integer")
-        if start_pos < 0 or start_pos + tokens.shape[1] > self.config.max_seq_len:
-            raise ValueError("sequence exceeds max_seq_len")
-        if len(set(request_ids)) != len(request_ids):
-            raise ValueError("duplicate request ids")
-        for r in request_ids:
-            if not isinstance(r, int) or isinstance(r, bool) or r < 0:
-                raise ValueError(f"invalid request id {r!r}")
-            if r >= 1 << 63:
-                raise ValueError("request id exceeds int64 range")
-            if r > _MAX_REQUEST_ID and not internal:
-                raise ValueError("request id exceeds manual range")
-        # Token values produced by the engine's own argmax are in range by
-        # construction; caller-supplied tokens are checked (a host sync).
-        if not internal and ((tokens < 0).any() or (tokens >= self.config.vocab_size).any()):
-            raise ValueError("token ids out of range")
-
-    def _bcast(self, tensor: torch.Tensor) -> None:
-        if self._world():
-            dist.broadcast(tensor, src=0)
-
-    def _invalidate(self) -> None:
-        self._healthy = False
-        self.decoder.cache.clear()
-
-    def _collective_forward(self, tokens, request_ids, start_pos, last_only=False) -> torch.Tensor:
-        err = 0
-        cache = self.decoder.cache
-        try:
-            if start_pos == 0:
-                cache._check_ids(request_ids)
-                for r in request_ids:
-                    if r in cache._entries:
-                        raise CacheError(f"request id {r} already reserved")
-                if len(cache._entries) + len(request_ids) > cache.max_requests:
-                    raise CacheError("cache capacity exceeded")
-            else:
-                cache.validate(request_ids, start_pos, tokens.shape[1])
-        except CacheError:
-            err = 1
-        if self._world():
-            flag = torch.tensor([err], dtype=torch.int64, device=self._comm_device)
-            dist.all_reduce(flag, op=dist.ReduceOp.MAX)
-            err = int(flag.item())
-        if err:
-            raise EngineFailed("cache preflight failed")
-        with torch.inference_mode():
-            return self.decoder.forward(tokens, request_ids, start_pos, last_only=last_only)
-
-    def forward(self, tokens: torch.Tensor, request_ids: tuple[int, ...], start_pos: int = 0,
-                _internal: bool = False, _last_only: bool = False) -> torch.Tensor:
-        with self._lock:
-            if not self._healthy or self._closed:
-                raise EngineFailed("engine is not healthy")
-            self._validate_request(tokens, request_ids, start_pos, internal=_internal)
-            if self._world() and not self._is_leader:
-                raise EngineFailed("forward must be invoked on rank 0")
-            try:
-                if self._world():
-                    header = torch.tensor([CMD_STEP, tokens.shape[0], tokens.shape[1], start_pos], dtype=torch.int64,
-                                          device=self._comm_device)
-                    self._bcast(header)
-                    self._bcast(torch.tensor(list(request_ids), dtype=torch.int64, device=self._comm_device))
-                    self._bcast(tokens.to(self._comm_device).contiguous())
-                    # The reference protocol has no "last position only" flag, so with
-                    # workers every rank computes (and broadcasts) full logits.
-                    _last_only = False
-                return self._collective_forward(tokens.to(self.context.device), request_ids, start_pos,
-                                                last_only=_last_only)
-            except Exception as exc:
-                self._invalidate()
-                raise EngineFailed("engine execution failed") from exc
-
-    def serve(self) -> None:
-        if self._is_leader or not self._world():
-            raise EngineFailed("serve() is for non-zero ranks")
-        try:
-            while True:
-                header = torch.zeros(4, dtype=torch.int64, device=self._comm_device)
-                dist.broadcast(header, src=0)
-                cmd, batch, time_, start_pos = (int(v) for v in header.tolist())
-                if cmd == CMD_STOP:
-                    if batch != 0 or time_ != 0 or start_pos != 0:
-                        raise EngineFailed("malformed STOP header")
-                    return
-                if cmd == CMD_STEP:
-                    if (batch <= 0 or batch > self.max_requests or time_ <= 0 or time_ > self.config.max_seq_len
-                            or start_pos < 0 or start_pos + time_ > self.config.max_seq_len):
-                        raise EngineFailed("malformed STEP header")
-                    ids = torch.zeros(batch, dtype=torch.int64, device=self._comm_device)
-                    dist.broadcast(ids, src=0)
-                    tokens = torch.zeros(batch, time_, dtype=torch.int64, device=self._comm_device)
-                    dist.broadcast(tokens, src=0)
-                    self._collective_forward(tokens.to(self.context.device), tuple(int(i) for i in ids.tolist()),
-                                             start_pos)
-                elif cmd == CMD_RELEASE:
-                    if batch < 0 or batch > self.max_requests or time_ != 0 or start_pos != 0:
-                        raise EngineFailed("malformed RELEASE header")
-                    ids = torch.zeros(batch, dtype=torch.int64, device=self._comm_device)
-                    dist.broadcast(ids, src=0)
-                    self.decoder.cache.release(tuple(int(i) for i in ids.tolist()))
-                else:
-                    raise EngineFailed(f"unknown command {cmd}")
-        except Exception as exc:
-            self._invalidate()
-            raise EngineFailed("worker execution failed") from exc
-
-    def release(self, request_ids: tuple[int, ...]) -> None:
-        with self._lock:
-            if self._closed or not self._healthy:
-                raise EngineFailed("engine is not healthy")
-            if self._world() and not self._is_leader:
-                raise EngineFailed("release must be invoked on rank 0")
-            for r in request_ids:
-                if not isinstance(r, int) or isinstance(r, bool) or r < 0 or r >= 1 << 63:
-                    raise ValueError(f"invalid request id {r!r}")
-            if len(request_ids) > self.max_requests:
-                raise ValueError("release batch exceeds max_requests")
-            if not request_ids:
-                return
-            try:
-                if self._world():
-                    header = torch.tensor([CMD_RELEASE, len(request_ids), 0, 0], dtype=torch.int64,
-                                          device=self._comm_device)
-                    self._bcast(header)
-                    self._bcast(torch.tensor(list(request_ids), dtype=torch.int64, device=self._comm_device))
-                self.decoder.cache.release(request_ids)
-            except Exception as exc:
-                self._invalidate()
-                raise EngineFailed("engine execution failed") from exc
-
-    def _next_tokens(self, logits: torch.Tensor) -> torch.Tensor:
-        last = logits[:, -1, :]
-        if last.is_cuda:
-            return ops.argmax(last)
-        return last.argmax(-1)
-
-    def generate(self, prompts: list[list[int]], max_new_tokens: int) -> list[list[int]]:
-        with self._lock:
-            if not self._healthy or self._closed:
-                raise EngineFailed("engine is not healthy")
-            if not self._is_leader and self._world():
-                raise EngineFailed("generate must be invoked on rank 0")
-            if not isinstance(max_new_tokens, int) or isinstance(max_new_tokens, bool) or max_new_tokens < 0:
-                raise ValueError("max_new_tokens must be a non-negative int")
-            for p in prompts:
-                _validate_prompt(self.config, p, max_new_tokens)
-            if len(prompts) > self.max_requests:
-                raise ValueError("batch exceeds max_requests")
-            if not prompts:
-                return []
-            if max_new_tokens == 0:
-                return [[] for _ in prompts]
-            results: list[list[int]] = [[] for _ in prompts]
-            cohorts: dict[int, list[int]] = {}
-            for i, p in enumerate(prompts):
-                cohorts.setdefault(len(p), []).append(i)
-            issued: list[int] = []
-            try:
-                for plen, idxs in cohorts.items():
-                    ids = []
-                    for _ in idxs:
-                        while self._gen_counter in self.decoder.cache._entries:
-                            self._gen_counter += 1
-                        if self._gen_counter >= 1 << 63:
-                            raise EngineFailed("request id space exhausted")
-                        ids.append(self._gen_counter)
-                        self._gen_counter += 1
-                    issued.extend(ids)
-                    tokens = torch.tensor([prompts[i] for i in idxs], dtype=torch.long)
-                    logits = self.forward(tokens, tuple(ids), 0, _internal=True, _last_only=True)
-                    nxt = self._next_tokens(logits)
-                    produced = [nxt]
-                    for step in range(1, max_new_tokens):
-                        logits = self.forward(nxt.view(-1, 1), tuple(ids), plen + step - 1, _internal=True,
-                                              _last_only=True)
-                        nxt = self._next_tokens(logits)
-                        produced.append(nxt)
-                    seqs = torch.stack(produced, dim=1).tolist()  # one device->host read per cohort
-                    for j, i in enumerate(idxs):
-                        results[i] = [int(v) for v in seqs[j]]
-            finally:
-                if issued and self._healthy:
-                    self.release(tuple(issued))
-                elif issued:
-                    self.decoder.cache.clear()
-            return results
-
-    def close(self) -> None:
-        with self._lock:
-            if self._closed:
-                return
-            self._closed = True
-            try:
-                if self._world() and self._is_leader and self._healthy:
-                    header = torch.tensor([CMD_STOP, 0, 0, 0], dtype=torch.int64, device=self._comm_device)
-                    with contextlib.suppress(Exception):
-                        self._bcast(header)
-                self.decoder.cache.clear()
-                if hasattr(self.decoder, "close"):
-                    self.decoder.close()
-                elif hasattr(self.decoder, "release_graphs"):
-                    self.decoder.release_graphs()
-                self._healthy = False
-            finally:
-                if self._owns_context:
-                    with contextlib.suppress(Exception):
-                        self.context.close()
+# The serving engine lives in engine.py; the reference exposes it from this module.
+from forgeml_b200.nebula.engine import (CMD_RELEASE, CMD_STEP, CMD_STOP, Engine, EngineFailed,  # noqa: E402,F401
+                                        _validate_prompt)

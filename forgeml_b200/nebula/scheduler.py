@@ -17,7 +17,7 @@ import logging
 import math
 from collections import deque
 
-from forgeml_b200.nebula.runtime import Engine, EngineFailed, _validate_prompt
+from forgeml_b200.nebula.engine import Engine, EngineFailed, _validate_prompt
 
 _log = logging.getLogger(__name__)
 

@@ -320,6 +320,15 @@ FML_API const char* fml_last_error(void);
  * 16 attention copy-pipeline wait expired, 32 all-reduce peer wait expired.
  * Synchronizes the current device. */
 FML_API int fml_device_status(void);
+/* Stream-ordered copy of the device error word (same bits) into host memory
+ * `host_dst` (4 bytes; pinned for the copy to stay asynchronous) once the
+ * work queued on `stream` before it has run.  Does not clear the word and
+ * does not synchronise: the caller reads *host_dst after the stream (or an
+ * event recorded after this call) has completed.  A serving engine checks
+ * every step this way without a host wait (Nebula's poisoning contract,
+ * src/nebula/runtime.py:299-301,361-363: an engine whose step failed on the
+ * device raises EngineFailed and drops its cache). */
+FML_API int fml_device_status_async(int32_t* host_dst, void* stream);
 /* Number of kernel launches issued by this library in this process. */
 FML_API int64_t fml_launch_count(void);
 /* Library version string. */

@@ -105,6 +105,10 @@ def test_tp2_pp2_bf16():
     _run(4, 2, 2, "bfloat16")
 
 
+def test_tp4_bf16():
+    _run(4, 4, 1, "bfloat16")
+
+
 def test_tp8_bf16():
     _run(8, 8, 1, "bfloat16")
 
@@ -196,17 +200,14 @@ def test_peer_all_reduce_2_bf16_flag_protocol():
     _run_ar(2, "bfloat16", "flag")
 
 
-_TWO_SHOT = pytest.mark.skipif(
-    __import__("os").environ.get("FORGEML_TEST_TWO_SHOT") != "1",
-    reason="two-shot all-reduce (FORGEML_AR_PROTO=ll2) not yet validated on GPUs; FORGEML_TEST_TWO_SHOT=1 runs it")
-
-
-@_TWO_SHOT
 def test_peer_all_reduce_2_bf16_two_shot():
     _run_ar(2, "bfloat16", "ll2")
 
 
-@_TWO_SHOT
+def test_peer_all_reduce_4_bf16_two_shot():
+    _run_ar(4, "bfloat16", "ll2")
+
+
 def test_peer_all_reduce_8_bf16_two_shot():
     _run_ar(8, "bfloat16", "ll2")
 

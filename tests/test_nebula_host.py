@@ -78,9 +78,9 @@ def test_cache_release_reuse_and_slots():
     assert c.slots((8,)) == [0]  # lowest free slot is reused
     c.clear()
     assert c.active_requests == 0
-    # a request's per-layer buffer is a view with the reference layout [heads, max_seq, hd]
+    # a request's slot block has the reference's per-request layout [heads, max_seq, hd]
     c.reserve((1,))
-    assert c._entries[1][0][0].shape == (2, 8, 4)
+    assert c.k_pool[0][c.slots((1,))[0]].shape == (2, 8, 4)
 
 
 def test_cache_validate_positions():
@@ -163,21 +163,51 @@ def test_failed_forward_poisons_engine(monkeypatch, failure):
 
 def test_broadcast_failure_poisons_and_close_skips(monkeypatch):
     e = engine()
-    calls = []
+    sent = []
 
-    def boom(t):
-        calls.append(t)
+    def dead_transport(t):
+        sent.append(t.clone())
         raise RuntimeError("transport dead")
 
-    monkeypatch.setattr(e, "_world", lambda: True)
-    monkeypatch.setattr(e, "_bcast", boom)
+    monkeypatch.setattr(e, "_multi", True)
+    monkeypatch.setattr(e._wire, "broadcast", dead_transport)
     with pytest.raises(EngineFailed):
-        e.forward(torch.tensor([[1]]), (1,), 0)
+        e.forward(torch.tensor([[5]]), (1,), 0)
     assert not e.healthy and e.decoder.cache.active_requests == 0
-    e.close()
-    assert len(calls) == 1
-    # the header that failed to go out is the reference's int64 STEP header
-    assert calls[0].dtype == torch.int64 and calls[0].tolist() == [1, 1, 1, 0]
+    e.close()  # an unhealthy leader sends no STOP
+    assert len(sent) == 1
+    # the frame that failed to go out: the reference's int64 STEP header, then
+    # the request id and the token, zero padded to 4 + 2 * max_requests words
+    frame = sent[0]
+    assert frame.dtype == torch.int64 and frame.numel() == 4 + 2 * 4
+    assert frame.tolist() == [1, 1, 1, 0, 1, 5, 0, 0, 0, 0, 0, 0]
+
+
+def test_wire_frames_split_when_the_message_is_long():
+    from forgeml_b200.nebula.engine import CMD_STEP, _CommandWire
+
+    w = _CommandWire(max_requests=2, max_seq_len=16, device=torch.device("cpu"))
+    sent = []
+    w.broadcast = lambda t: sent.append(t.clone())
+    w.send(CMD_STEP, 0, (7, 9), torch.tensor([[1, 2, 3], [4, 5, 6]]))
+    assert [t.tolist() for t in sent] == [[1, 2, 3, 0, 0, 0, 0, 0], [7, 9, 1, 2, 3, 4, 5, 6]]
+    # the receiving side rebuilds the same command from the same words
+    frames = iter(sent)
+    r = _CommandWire(max_requests=2, max_seq_len=16, device=torch.device("cpu"))
+    r.broadcast = lambda t: t.copy_(next(frames))
+    c = r.receive()
+    assert (c.cmd, c.batch, c.steps, c.start, c.ids) == (1, 2, 3, 0, (7, 9))
+    assert c.tokens.tolist() == [[1, 2, 3], [4, 5, 6]]
+
+
+def test_wire_rejects_malformed_headers():
+    from forgeml_b200.nebula.engine import _CommandWire
+
+    for words in ([0, 1, 0, 0], [1, 3, 1, 0], [1, 1, 0, 0], [1, 1, 2, 15], [2, 1, 1, 0], [7, 0, 0, 0]):
+        r = _CommandWire(max_requests=2, max_seq_len=16, device=torch.device("cpu"))
+        r.broadcast = lambda t, words=words: t[:4].copy_(torch.tensor(words))
+        with pytest.raises(EngineFailed):
+            r.receive()
 
 
 def test_closed_engine_and_release_checks():
