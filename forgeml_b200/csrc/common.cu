@@ -78,8 +78,28 @@ int fml_device_status(void) {
 
 int fml_device_status_async(int32_t* host_dst, void* stream) {
   if (!host_dst) return fml::fail(FML_EINVAL, "fml_device_status_async: null destination");
-  return fml::check_cuda(cudaMemcpyFromSymbolAsync(host_dst, fml::g_device_error, sizeof(int), 0,
-                                                   cudaMemcpyDeviceToHost, reinterpret_cast<cudaStream_t>(stream)),
+  // The word's device address, looked up once per device (a symbol copy would
+  // resolve it on every call).
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  const int dev = fml::current_device();
+  void* src = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64) {
+      if (!addr[dev]) {
+        cudaError_t e = cudaGetSymbolAddress(&addr[dev], fml::g_device_error);
+        if (e != cudaSuccess) {
+          addr[dev] = nullptr;
+          return fml::check_cuda(e, "fml_device_status_async: cudaGetSymbolAddress");
+        }
+      }
+      src = addr[dev];
+    }
+  }
+  if (!src) return fml::fail(FML_EINVAL, "fml_device_status_async: device index out of range");
+  return fml::check_cuda(cudaMemcpyAsync(host_dst, src, sizeof(int), cudaMemcpyDeviceToHost,
+                                         reinterpret_cast<cudaStream_t>(stream)),
                          "fml_device_status_async");
 }
 

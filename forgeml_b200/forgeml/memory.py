@@ -1,33 +1,42 @@
-"""Slot-arena memory planner.
+"""Slot-arena memory planner of the compiled forward pass.
 
-Produces the same plan as the reference planner (src/forgeml/memory.py:59-138)
-for the same graph -- identical slot ids, sizes, live intervals, aliases,
-naive and planned bytes -- because the compiled model's slot views are part
-of the drop-in contract.  The rules that must match:
+The plan is part of the drop-in contract: for a given graph it must come out
+exactly as the reference planner's (src/forgeml/memory.py:59-138) -- same
+slot ids, sizes, live intervals, aliases, naive and planned bytes.  The rules
+it has to share with the reference:
 
-* view ops (reshape, transpose, narrow) alias their first input, take no
-  slot, and extend the live range of what they view to their own last use;
-* graph outputs and ops without an ``out=`` writer get no slot;
-* a node may reuse a slot whose current tenant's last use is strictly before
-  the node's index, with equal dtype and device; among those it takes the
-  smallest capacity that fits (lowest slot id on ties);
-* a new slot is a flat 1-D buffer of ceil(nbytes / itemsize) elements.
+  * view ops (reshape, transpose, narrow) take no slot; they alias their
+    first input and keep it live until their own last use;
+  * graph outputs, and ops without an ``out=`` writer, take no slot;
+  * a node may take a slot whose tenant's last use is strictly earlier than
+    the node's position, of the same dtype and device; of those it takes the
+    smallest that fits, the lowest slot id on ties;
+  * otherwise it opens a new flat 1-D slot of ceil(nbytes / itemsize)
+    elements.
 
-``plan_memory(graph, out_capable=...)`` with a wider op set plans the
-extension arena that the native backend uses for LayerNorm and SDPA outputs
-(same rules, separate slots), leaving the reference-compatible plan intact.
+``plan_slots`` implements them over plain (name, op, inputs, spec) entries,
+so the native backend can plan its own execution program (fused nodes,
+LayerNorm / SDPA outputs) with the same rules; ``plan_memory`` is the
+reference-facing entry point over a validated Graph.
 """
 
 from __future__ import annotations
 
 from dataclasses import dataclass
+from typing import Iterable, NamedTuple
 
 from forgeml_b200.forgeml.ir import Graph, TensorSpec
 
 VIEW_LIKE_OPS = frozenset({"reshape", "transpose", "narrow"})
 OUT_CAPABLE_OPS = frozenset(
-    {"matmul", "linear", "add", "mul", "relu", "softmax", "gelu", "embedding", "fused_linear_gelu"}
-)
+    {"matmul", "linear", "add", "mul", "relu", "softmax", "gelu", "embedding", "fused_linear_gelu"})
+
+
+class Entry(NamedTuple):
+    name: str
+    op: str
+    inputs: tuple
+    spec: TensorSpec
 
 
 @dataclass(frozen=True)
@@ -49,63 +58,77 @@ class MemoryPlan:
     def to_dict(self) -> dict:
         return {
             "aliases": dict(self.aliases),
-            "allocations": {
-                k: {"slot": a.slot, "size_bytes": a.size_bytes, "first": a.first, "last": a.last}
-                for k, a in self.allocations.items()
-            },
+            "allocations": {k: {"slot": a.slot, "size_bytes": a.size_bytes, "first": a.first, "last": a.last}
+                            for k, a in self.allocations.items()},
             "slot_specs": {str(k): v.to_dict() for k, v in self.slot_specs.items()},
             "naive_bytes": self.naive_bytes,
             "planned_bytes": self.planned_bytes,
         }
 
 
-def _last_uses(graph: Graph) -> dict[str, int]:
-    """Index of the last node that reads each value, looking through views.
+def last_reads(entries: list[Entry]) -> dict[str, int]:
+    """Position of the last entry that reads each value, through views: a view
+    read at position j keeps what it views alive until j as well.  A value
+    nobody reads ends at its own position."""
+    pos = {e.name: i for i, e in enumerate(entries)}
+    end = dict(pos)
+    for e in reversed(entries):  # a view's own end is final before its inputs are visited
+        reach = end[e.name] if e.op in VIEW_LIKE_OPS else pos[e.name]
+        for src in e.inputs:
+            if src in end and end[src] < reach:
+                end[src] = reach
+    return end
 
-    Computed in one reverse sweep: a consumer that is a view op contributes the
-    last use of the view itself (already known, since it comes later).
-    """
-    index = {n.name: i for i, n in enumerate(graph.nodes)}
-    last = {n.name: i for i, n in enumerate(graph.nodes)}
-    for node in reversed(graph.nodes):
-        through = last[node.name] if node.op in VIEW_LIKE_OPS else index[node.name]
-        for src in set(node.inputs):
-            if src in last and through > last[src]:
-                last[src] = through
-    return last
+
+class _Slots:
+    """Open slots with the position until which each one is taken."""
+
+    def __init__(self):
+        self.specs: dict[int, TensorSpec] = {}
+        self.taken_until: dict[int, int] = {}
+
+    def fit(self, spec: TensorSpec, nbytes: int, at: int) -> int:
+        best, best_cap = None, None
+        for sid, s in self.specs.items():
+            if self.taken_until[sid] >= at or s.dtype != spec.dtype or s.device != spec.device:
+                continue
+            cap = s.shape[0] * s.dtype.itemsize
+            if cap >= nbytes and (best is None or cap < best_cap):
+                best, best_cap = sid, cap
+        if best is None:
+            best = len(self.specs)
+            self.specs[best] = TensorSpec((-(-nbytes // spec.dtype.itemsize),), spec.dtype, spec.device)
+        return best
+
+
+def plan_slots(entries: Iterable[Entry], outputs: Iterable[str],
+               out_capable: frozenset = OUT_CAPABLE_OPS) -> MemoryPlan:
+    entries = list(entries)
+    outs = set(outputs)
+    ends = last_reads(entries)
+    slots = _Slots()
+    allocations: dict[str, Allocation] = {}
+    aliases: dict[str, str] = {}
+    naive = 0
+    for i, e in enumerate(entries):
+        if e.name in outs:
+            continue
+        naive += e.spec.nbytes
+        if e.op in VIEW_LIKE_OPS:
+            aliases[e.name] = e.inputs[0]
+        elif e.op in out_capable:
+            sid = slots.fit(e.spec, e.spec.nbytes, i)
+            slots.taken_until[sid] = ends[e.name]
+            allocations[e.name] = Allocation(sid, e.spec.nbytes, i, ends[e.name])
+    planned = sum(s.shape[0] * s.dtype.itemsize for s in slots.specs.values())
+    return MemoryPlan(allocations, aliases, slots.specs, naive, planned)
+
+
+def graph_entries(graph: Graph) -> list[Entry]:
+    return [Entry(n.name, n.op, tuple(n.inputs), n.spec) for n in graph.nodes]
 
 
 def plan_memory(graph: Graph, out_capable: frozenset = OUT_CAPABLE_OPS) -> MemoryPlan:
+    """The reference-compatible slot plan of a (validated) graph."""
     graph.validate()
-    outputs = set(graph.outputs)
-    last_use = _last_uses(graph)
-    aliases: dict[str, str] = {}
-    allocations: dict[str, Allocation] = {}
-    slot_specs: dict[int, TensorSpec] = {}
-    busy_until: dict[int, int] = {}
-    naive = 0
-    for i, node in enumerate(graph.nodes):
-        if node.name in outputs:
-            continue
-        naive += node.spec.nbytes
-        if node.op in VIEW_LIKE_OPS:
-            aliases[node.name] = node.inputs[0]
-            continue
-        if node.op not in out_capable:
-            continue
-        need = node.spec.nbytes
-        itemsize = node.spec.dtype.itemsize
-        chosen, chosen_cap = None, None
-        for slot, spec in slot_specs.items():  # insertion order == slot id order
-            if busy_until[slot] >= i or spec.dtype != node.spec.dtype or spec.device != node.spec.device:
-                continue
-            cap = spec.shape[0] * spec.dtype.itemsize
-            if cap >= need and (chosen is None or cap < chosen_cap):
-                chosen, chosen_cap = slot, cap
-        if chosen is None:
-            chosen = len(slot_specs)
-            slot_specs[chosen] = TensorSpec((-(-need // itemsize),), node.spec.dtype, node.spec.device)
-        busy_until[chosen] = last_use[node.name]
-        allocations[node.name] = Allocation(chosen, need, i, last_use[node.name])
-    planned = sum(s.shape[0] * s.dtype.itemsize for s in slot_specs.values())
-    return MemoryPlan(allocations, aliases, slot_specs, naive, planned)
+    return plan_slots(graph_entries(graph), graph.outputs, out_capable)

@@ -3,13 +3,13 @@
 from forgeml_b200.nebula.cache import CacheError, KVCache
 from forgeml_b200.nebula.model import DecoderConfig, TinyDecoder
 from forgeml_b200.nebula.parallel import ParallelContext
-from forgeml_b200.nebula.runtime import Engine, EngineFailed, ShardedDecoder
-from forgeml_b200.nebula.scheduler import AsyncBatcher, QueueFull, RequestRouter, ServiceClosed
+from forgeml_b200.nebula.engine import Engine, EngineFailed
+from forgeml_b200.nebula.runtime import ShardedDecoder
+from forgeml_b200.nebula.scheduler import AsyncBatcher, QueueFull, ServiceClosed
 
 __all__ = [
     "AsyncBatcher",
     "QueueFull",
-    "RequestRouter",
     "ServiceClosed",
     "CacheError",
     "DecoderConfig",

@@ -10,9 +10,11 @@ any failure leaves the engine unhealthy with an empty cache.
 Command wire.  The words are the reference protocol's int64 values in its
 order: the header [cmd, B, T, start_pos], then the B request ids, then the
 B x T tokens (STEP), the B ids (RELEASE) or nothing (STOP).  They travel in one
-broadcast of a fixed frame of 4 + 2 * max_requests words when the message fits
+broadcast of a fixed frame of 4 + 3 * max_requests words when the message fits
 (every decode step), otherwise as the header frame followed by one broadcast
-of ids and tokens.  On an NCCL world the frame is assembled on the device, so
+of ids and tokens.  One command extends the reference's set: STEP_AT, a
+single-token step whose requests each sit at their own position (the decode
+phase of ``generate_mixed``).  On an NCCL world the frame is assembled on the device, so
 the leader's tokens (on the device during ``generate``) never pass through the
 host.
 
@@ -50,6 +52,10 @@ from forgeml_b200.nebula.parallel import ParallelContext
 CMD_STOP = 0
 CMD_STEP = 1
 CMD_RELEASE = 2
+# Extension of the reference protocol (generate_mixed): a single-token step in
+# which every request sits at its own position.  Header [3, B, 1, 0], then the
+# B ids, the B tokens and the B positions.
+CMD_STEP_AT = 3
 _GENERATE_ID_BASE = 1 << 62  # engine-issued request ids start here
 _MAX_REQUEST_ID = _GENERATE_ID_BASE - 1  # caller-chosen ids stay at or below this
 _ID_LIMIT = 1 << 63
@@ -86,13 +92,14 @@ class _Command(NamedTuple):
     start: int
     ids: tuple
     tokens: torch.Tensor | None
+    positions: tuple = ()
 
 
 class _CommandWire:
     """The leader -> worker command channel over the default process group."""
 
     def __init__(self, max_requests: int, max_seq_len: int, device: torch.device):
-        self.frame_words = 4 + 2 * max_requests
+        self.frame_words = 4 + 3 * max_requests
         self.max_requests, self.max_seq_len = max_requests, max_seq_len
         self.device = device
 
@@ -101,26 +108,28 @@ class _CommandWire:
         dist.broadcast(t, src=0)
 
     # ------------------------------------------------------------ leader
-    def send(self, cmd: int, start: int = 0, ids: tuple = (), tokens: torch.Tensor | None = None) -> None:
+    def send(self, cmd: int, start: int = 0, ids: tuple = (), tokens: torch.Tensor | None = None,
+             positions: tuple = ()) -> None:
         b = len(ids)
         t = 0 if tokens is None else int(tokens.shape[1])
         head = torch.tensor([cmd, b, t, start, *ids], dtype=torch.int64)
-        body_words = b + b * t
+        tail = torch.tensor(list(positions), dtype=torch.int64)
+        body_words = b + b * t + len(positions)
         nb = self.device.type == "cuda"  # host-asynchronous copies only into device memory
         frame = torch.zeros(self.frame_words, dtype=torch.int64, device=self.device)
         if 4 + body_words <= self.frame_words:
-            frame[:4 + b].copy_(head, non_blocking=nb)
-            if t:
-                frame[4 + b:4 + body_words].copy_(tokens.reshape(-1), non_blocking=nb)
+            body = frame[4:4 + body_words]
+            frame[:4].copy_(head[:4], non_blocking=nb)
+        else:
+            frame[:4].copy_(head[:4], non_blocking=nb)
             self.broadcast(frame)
-            return
-        frame[:4].copy_(head[:4], non_blocking=nb)
-        self.broadcast(frame)
-        body = torch.empty(body_words, dtype=torch.int64, device=self.device)
+            frame = body = torch.empty(body_words, dtype=torch.int64, device=self.device)
         body[:b].copy_(head[4:], non_blocking=nb)
         if t:
-            body[b:].copy_(tokens.reshape(-1), non_blocking=nb)
-        self.broadcast(body)
+            body[b:b + b * t].copy_(tokens.reshape(-1), non_blocking=nb)
+        if positions:
+            body[b + b * t:].copy_(tail, non_blocking=nb)
+        self.broadcast(frame)
 
     # ------------------------------------------------------------ worker
     def receive(self) -> _Command:
@@ -135,19 +144,24 @@ class _CommandWire:
             if not (0 < b <= self.max_requests and 0 < t <= self.max_seq_len and start >= 0
                     and start + t <= self.max_seq_len):
                 raise EngineFailed("malformed STEP header")
+        elif cmd == CMD_STEP_AT:
+            if not (0 < b <= self.max_requests and t == 1 and start == 0):
+                raise EngineFailed("malformed STEP_AT header")
         elif cmd == CMD_RELEASE:
             if not (0 <= b <= self.max_requests and t == 0 and start == 0):
                 raise EngineFailed("malformed RELEASE header")
         else:
             raise EngineFailed(f"unknown command {cmd}")
-        body_words = b + b * t
+        extra = b if cmd == CMD_STEP_AT else 0
+        body_words = b + b * t + extra
         if 4 + body_words <= self.frame_words:
             body = frame[4:4 + body_words]
         else:
             body = torch.zeros(body_words, dtype=torch.int64, device=self.device)
             self.broadcast(body)
-        ids = tuple(body[:b].tolist())
-        return _Command(cmd, b, t, start, ids, body[b:].view(b, t) if t else None)
+        head = body[:b].tolist() + (body[b + b * t:].tolist() if extra else [])
+        tokens = body[b:b + b * t].view(b, t) if t else None
+        return _Command(cmd, b, t, start, tuple(head[:b]), tokens, tuple(head[b:]))
 
 
 class _StepHealth:
@@ -172,9 +186,7 @@ class _StepHealth:
 
         stream = torch.cuda.current_stream(self.device)
         _native.device_status_async(self.status, stream.cuda_stream)
-        if agreed is None:
-            self.agreed.zero_()
-        else:
+        if agreed is not None:
             self.agreed.copy_(agreed.view(1), non_blocking=True)
         self.event.record(stream)
         self.pending = True
@@ -292,20 +304,24 @@ class Engine:
         if not internal and bool(((tokens < 0) | (tokens >= self.config.vocab_size)).any()):
             raise ValueError("token ids out of range")
 
-    def _preflight_error(self, request_ids: tuple, start_pos: int, steps: int) -> int:
+    def _preflight_error(self, request_ids: tuple, start_pos, steps: int) -> int:
         cache = self.decoder.cache
         try:
-            if start_pos == 0:
+            if not isinstance(start_pos, int):  # per-request positions (STEP_AT)
+                for r, p in zip(request_ids, start_pos, strict=True):
+                    cache.validate((r,), p, steps)
+            elif start_pos == 0:
                 cache.check_admission(request_ids)
             else:
                 cache.validate(request_ids, start_pos, steps)
-        except CacheError:
+        except (CacheError, ValueError):
             return 1
         return 0
 
     # ------------------------------------------------------------ steps
-    def _run_step(self, tokens: torch.Tensor, request_ids: tuple, start_pos: int, last_only: bool):
-        """One STEP on this rank: preflight, agreement, decoder, health reads."""
+    def _run_step(self, tokens: torch.Tensor, request_ids: tuple, start_pos, last_only: bool):
+        """One step on this rank: preflight, agreement, decoder, health reads.
+        ``start_pos`` is an int, or a tuple of per-request positions."""
         err = self._preflight_error(request_ids, start_pos, tokens.shape[1])
         agreed = None
         if self._multi:
@@ -347,6 +363,8 @@ class Engine:
                     return
                 if c.cmd == CMD_STEP:
                     self._run_step(c.tokens.to(self.context.device), c.ids, c.start, False)
+                elif c.cmd == CMD_STEP_AT:
+                    self._run_step(c.tokens.to(self.context.device), c.ids, c.positions, False)
                 else:
                     self.decoder.cache.release(c.ids)
         except Exception as exc:
@@ -441,6 +459,66 @@ class Engine:
                     else:
                         self.decoder.cache.clear()
             return results
+
+    def _step_at(self, tokens: torch.Tensor, ids: tuple, positions: tuple) -> torch.Tensor:
+        """One single-token step of ``ids`` at their own ``positions`` (leader)."""
+        try:
+            self._health.check(wait=False)
+            if self._multi:
+                self._wire.send(CMD_STEP_AT, 0, ids, tokens, positions)
+            return self._run_step(tokens.to(self.context.device), ids, positions, not self._multi)
+        except Exception as exc:
+            self._invalidate()
+            raise EngineFailed("engine execution failed") from exc
+
+    def generate_mixed(self, prompts: list[list[int]], max_new_tokens: int) -> list[list[int]]:
+        """``generate`` for prompts of different lengths in one decode batch.
+
+        The prompts are prefilled in groups of equal length (as ``generate``
+        does), then every later greedy step decodes all of them together, each
+        request at its own position (STEP_AT).  Each request's tokens are
+        those ``generate`` would produce for it, up to the GEMMs' summation
+        order at another batch size.  Not part of the reference API."""
+        with self._lock:
+            self._require_healthy()
+            self._require_leader("generate")
+            if not _plain_int(max_new_tokens) or max_new_tokens < 0:
+                raise ValueError("max_new_tokens must be a non-negative int")
+            for p in prompts:
+                _validate_prompt(self.config, p, max_new_tokens)
+            if len(prompts) > self.max_requests:
+                raise ValueError("batch exceeds max_requests")
+            if not prompts or max_new_tokens == 0:
+                return [[] for _ in prompts]
+            groups: dict[int, list[int]] = {}
+            for i, p in enumerate(prompts):
+                groups.setdefault(len(p), []).append(i)
+            ids = self._fresh_ids(len(prompts))
+            try:
+                dev = self.context.device
+                cur = torch.empty(len(prompts), dtype=torch.long, device=dev)
+                for plen, members in groups.items():
+                    logits = self.forward(torch.tensor([prompts[i] for i in members], dtype=torch.long),
+                                          tuple(ids[i] for i in members), 0, _internal=True, _last_only=True)
+                    cur.index_copy_(0, torch.tensor(members, device=dev), self._argmax(logits))
+                produced = [cur]
+                positions = tuple(len(p) for p in prompts)
+                for _ in range(1, max_new_tokens):
+                    logits = self._step_at(produced[-1].view(-1, 1), ids, positions)
+                    produced.append(self._argmax(logits))
+                    positions = tuple(p + 1 for p in positions)
+                rows = torch.stack(produced, dim=1).tolist()
+                try:
+                    self._health.check(wait=True)
+                except EngineFailed:
+                    self._invalidate()
+                    raise
+                return [[int(v) for v in row] for row in rows]
+            finally:
+                if self._healthy:
+                    self.release(ids)
+                else:
+                    self.decoder.cache.clear()
 
     def close(self) -> None:
         with self._lock:

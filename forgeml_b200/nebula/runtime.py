@@ -355,27 +355,38 @@ class ShardedDecoder(nn.Module):
         return logits
 
     # ------------------------------------------------------------------ API
-    def forward(self, tokens: torch.Tensor, request_ids: tuple[int, ...], start_pos: int,
+    def forward(self, tokens: torch.Tensor, request_ids: tuple[int, ...], start_pos,
                 last_only: bool = False) -> torch.Tensor:
+        """Logits [B, T or 1, V] of one step.  ``start_pos`` is the position of
+        the batch's first token (0 reserves the requests), or -- for
+        single-token steps of requests already in the cache -- a sequence with
+        each request's own position (the kernels take per-request positions)."""
         ctx = self.context
         b, t = tokens.shape
         v = self.config.vocab_size
-        if start_pos == 0:
-            self.cache.reserve(request_ids)
+        if isinstance(start_pos, int):
+            if start_pos == 0:
+                self.cache.reserve(request_ids)
+            positions = [start_pos] * b
+        else:
+            positions = [int(p) for p in start_pos]
+            if t != 1 or len(positions) != b:
+                raise ValueError("per-request positions need single-token steps, one position per request")
         slots_host = torch.tensor(self.cache.slots(request_ids), dtype=torch.int32)
+        starts_host = torch.tensor(positions, dtype=torch.int32)
         if tokens.device != ctx.device:
             tokens = tokens.to(ctx.device)
         # Single-token steps replay a captured graph.  With tensor parallelism the
-        # graph also holds the NCCL all-reduces (every TP rank captures and
-        # replays the same step in lockstep); pipeline stages run eagerly.
+        # graph also holds the TP reductions (every TP rank captures and replays
+        # the same step in lockstep); pipeline stages run eagerly.
         graphable = (t == 1 and ctx.pp_size == 1 and self.use_cuda_graphs
                      and not torch.cuda.is_current_stream_capturing()
                      and (last_only or ctx.world_size > 1))
         if graphable:
-            logits = self._replay(tokens, slots_host, start_pos, b)
+            logits = self._replay(tokens, slots_host, starts_host, b)
         else:
             slots = slots_host.to(ctx.device, non_blocking=True)
-            starts = torch.full((b,), start_pos, dtype=torch.int32, device=ctx.device)
+            starts = starts_host.to(ctx.device, non_blocking=True)
             logits = self._core(tokens.contiguous(), slots, starts, b, t, last_only)
         tt = 1 if last_only else t
         if logits is None:
@@ -387,23 +398,32 @@ class ShardedDecoder(nn.Module):
             # lm_head runs on identical inputs, so the reference's broadcast
             # (runtime.py:188) would copy equal values.)
             dist.broadcast(logits, src=(ctx.pp_size - 1) * ctx.tp_size)
-        self.cache.advance(request_ids, start_pos + t)
+        if len(set(positions)) == 1:
+            self.cache.advance(request_ids, positions[0] + t)
+        else:
+            for r, p in zip(request_ids, positions):
+                self.cache.advance((r,), p + t)
         return logits.view(b, tt, v)
 
-    def _replay(self, tokens: torch.Tensor, slots_host: torch.Tensor, start_pos: int, b: int) -> torch.Tensor:
+    def _replay(self, tokens: torch.Tensor, slots_host: torch.Tensor, starts_host: torch.Tensor,
+                b: int) -> torch.Tensor:
         g = self._graphs.get(b)
         if g is None:
-            return self._capture(tokens, slots_host, start_pos, b)["logits"]
+            return self._capture(tokens, slots_host, starts_host, b)["logits"]
         g["tokens"].copy_(tokens.view(b, 1), non_blocking=True)
         key = tuple(slots_host.tolist())
         if key != g["slot_key"]:
             g["slots"].copy_(slots_host.to(g["slots"].device))
             g["slot_key"] = key
-        g["starts"].fill_(start_pos)
+        first = int(starts_host[0])
+        if bool((starts_host == first).all()):
+            g["starts"].fill_(first)
+        else:
+            g["starts"].copy_(starts_host, non_blocking=True)
         g["graph"].replay()
         return g["logits"]
 
-    def _capture(self, tokens: torch.Tensor, slots_host: torch.Tensor, start_pos: int, b: int) -> dict:
+    def _capture(self, tokens: torch.Tensor, slots_host: torch.Tensor, starts_host: torch.Tensor, b: int) -> dict:
         """Capture the single-token step for batch size ``b``.
 
         The static inputs are loaded with this step's real tokens, slots and
@@ -417,7 +437,7 @@ class ShardedDecoder(nn.Module):
             "tokens": tokens.view(b, 1).clone(),
             "slots": slots_host.to(dev),
             "slot_key": tuple(slots_host.tolist()),
-            "starts": torch.full((b,), start_pos, dtype=torch.int32, device=dev),
+            "starts": starts_host.to(dev),
         }
         s = torch.cuda.Stream(device=dev)
         s.wait_stream(torch.cuda.current_stream(dev))

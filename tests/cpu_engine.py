@@ -51,6 +51,9 @@ class CpuShardedDecoder:
 
     @torch.inference_mode()
     def forward(self, tokens, request_ids, start_pos, last_only=False):
+        if not isinstance(start_pos, int):  # per-request positions: one request at a time
+            return torch.cat([self.forward(tokens[i:i + 1], (r,), int(p), last_only)
+                              for i, (r, p) in enumerate(zip(request_ids, start_pos))])
         ctx = self.context
         b, t = tokens.shape
         h = self.config.hidden_size

@@ -57,6 +57,10 @@ def _worker(rank, world, tp, pp, store):
             prompts = [[1, 2, 3], [5, 6]]
             assert engine.generate(prompts, 3) == [_ref_generate(ref, p, 3) for p in prompts]
             assert engine.decoder.cache.active_requests == 0
+            # prompts of different lengths decoded in one batch (STEP_AT on the wire)
+            mixed = [[1, 2, 3, 4], [5, 6], [7]]
+            assert engine.generate_mixed(mixed, 4) == [_ref_generate(ref, p, 4) for p in mixed]
+            assert engine.decoder.cache.active_requests == 0
         else:
             engine.serve()
             assert engine.decoder.cache.active_requests == 0

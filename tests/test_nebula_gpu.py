@@ -133,6 +133,56 @@ def test_invalid_request_does_not_poison(cuda):
     e.close()
 
 
+def test_device_error_poisons_engine(cuda):
+    from forgeml_b200 import _native
+
+    e = engine()
+    e.forward(torch.tensor([[1, 2]]), (1,), 0)
+    # An engine-internal call skips the host check of token ids: the embedding
+    # kernel finds id 99 out of range, sets the token bit of the device error
+    # word and writes zeros.  The engine reads the word after the step and
+    # fails the next call, dropping its cache.
+    e.forward(torch.tensor([[99]]), (1,), 2, _internal=True)
+    torch.cuda.synchronize()
+    with pytest.raises(EngineFailed):
+        e.forward(torch.tensor([[3]]), (1,), 3)
+    assert not e.healthy and e.decoder.cache.active_requests == 0
+    assert _native.device_status() == 0  # the engine cleared the word
+    e.close()
+
+
+def test_peer_timeout_reaches_the_engine_health_check(cuda):
+    """A peer wait that expires (rank 1 never launches; no fault) raises the
+    all-reduce bit; the engine's step-health check turns it into EngineFailed."""
+    import ctypes
+
+    from forgeml_b200 import _native
+    from forgeml_b200.nebula.engine import _StepHealth
+
+    lib = _native.load()
+    hb = int(lib.neb_ar_handle_bytes())
+    ctxs = []
+    for rank in range(2):
+        c = ctypes.c_void_p()
+        _native.call("neb_ar_create", 1 << 16, 2, rank, 200.0, ctypes.byref(c), (ctypes.c_uint8 * hb)())
+        ctxs.append(c)
+    try:
+        bases = (ctypes.c_void_p * 2)(lib.neb_ar_buffer(ctxs[0]), lib.neb_ar_buffer(ctxs[1]))
+        _native.call("neb_ar_set_peers", ctxs[0], bases)
+        part = torch.ones(1024, dtype=torch.bfloat16, device=cuda)
+        out = torch.empty_like(part)
+        health = _StepHealth(cuda)
+        _native.call("neb_ar_all_reduce", ctxs[0], part.data_ptr(), None, out.data_ptr(), 1024,
+                     _native.dtype_code(torch.bfloat16), torch.cuda.current_stream().cuda_stream)
+        health.after_step(None)
+        with pytest.raises(EngineFailed, match="device error 0x20"):
+            health.check(wait=True)
+        assert _native.device_status() == 0
+    finally:
+        for c in ctxs:
+            _native.call("neb_ar_destroy", c)
+
+
 def test_cache_capacity_enforced(cuda):
     e = engine()
     e.forward(torch.tensor([[1], [2], [3], [4]]), (1, 2, 3, 4), 0)

@@ -128,6 +128,10 @@ def test_engine_protocol_matches_reference_outputs():
     assert e.generate(gold["generate_prompts"], 3) == gold["generate_tokens"]
     assert e.decoder.cache.active_requests == 0
     assert e.generate([[1, 2]], 0) == [[]]
+    prompts = gold["generate_prompts"] + [[3, 1, 4, 1, 5]]
+    want = [e.generate([p], 3)[0] for p in prompts]
+    assert e.generate_mixed(prompts, 3) == want
+    assert e.decoder.cache.active_requests == 0
     e.close()
 
 
@@ -179,8 +183,8 @@ def test_broadcast_failure_poisons_and_close_skips(monkeypatch):
     # the frame that failed to go out: the reference's int64 STEP header, then
     # the request id and the token, zero padded to 4 + 2 * max_requests words
     frame = sent[0]
-    assert frame.dtype == torch.int64 and frame.numel() == 4 + 2 * 4
-    assert frame.tolist() == [1, 1, 1, 0, 1, 5, 0, 0, 0, 0, 0, 0]
+    assert frame.dtype == torch.int64 and frame.numel() == 4 + 3 * 4
+    assert frame.tolist() == [1, 1, 1, 0, 1, 5] + [0] * 10
 
 
 def test_wire_frames_split_when_the_message_is_long():
@@ -190,7 +194,7 @@ def test_wire_frames_split_when_the_message_is_long():
     sent = []
     w.broadcast = lambda t: sent.append(t.clone())
     w.send(CMD_STEP, 0, (7, 9), torch.tensor([[1, 2, 3], [4, 5, 6]]))
-    assert [t.tolist() for t in sent] == [[1, 2, 3, 0, 0, 0, 0, 0], [7, 9, 1, 2, 3, 4, 5, 6]]
+    assert [t.tolist() for t in sent] == [[1, 2, 3, 0] + [0] * 6, [7, 9, 1, 2, 3, 4, 5, 6]]
     # the receiving side rebuilds the same command from the same words
     frames = iter(sent)
     r = _CommandWire(max_requests=2, max_seq_len=16, device=torch.device("cpu"))

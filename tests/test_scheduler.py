@@ -1,14 +1,14 @@
-"""AsyncBatcher / RequestRouter host logic with a fake engine (the reference's
+"""AsyncBatcher host logic with a fake engine (the reference's
 tests/test_nebula_scheduler.py approach): coalescing by (prompt length,
-max_new), no mixing of cohorts, bounded admission, failure fan-out without
-retry, close semantics, least-pending routing."""
+max_new), no mixing of cohorts unless asked for, bounded admission, failure
+fan-out without retry, close semantics."""
 
 import asyncio
 import threading
 
 import pytest
 
-from forgeml_b200.nebula import AsyncBatcher, DecoderConfig, EngineFailed, QueueFull, RequestRouter, ServiceClosed
+from forgeml_b200.nebula import AsyncBatcher, DecoderConfig, EngineFailed, QueueFull, ServiceClosed
 
 
 class FakeEngine:
@@ -114,15 +114,35 @@ def test_close_rejects_and_validation():
         AsyncBatcher(FakeEngine(), max_batch_size=65)
 
 
-def test_router_prefers_least_pending():
+class MixingEngine(FakeEngine):
+    def generate_mixed(self, prompts, max_new_tokens):
+        return self.generate(prompts, max_new_tokens)
+
+
+def test_mixed_prompt_lengths_share_a_batch():
     async def go():
-        e1, e2 = FakeEngine(), FakeEngine()
-        r = RequestRouter([AsyncBatcher(e1, batch_window_ms=0), AsyncBatcher(e2, batch_window_ms=0)])
-        outs = await asyncio.gather(*(r.generate([1, 2], 1) for _ in range(4)))
-        assert outs == [[2]] * 4
-        assert e1.batches and e2.batches
-        await r.close()
+        e = MixingEngine()
+        b = AsyncBatcher(e, max_batch_size=4, batch_window_ms=10, mix_prompt_lengths=True)
+        outs = await asyncio.gather(b.submit([1, 2], 2), b.submit([1, 2, 3], 2), b.submit([1], 5))
+        assert outs == [[2, 2], [3, 3], [1] * 5]
+        assert sorted(len(batch[0]) for batch in e.batches) == [1, 2]  # max_new still splits cohorts
+        await b.close()
 
     run(go())
     with pytest.raises(ValueError):
-        RequestRouter([])
+        AsyncBatcher(FakeEngine(), mix_prompt_lengths=True)
+
+
+def test_oldest_request_goes_first():
+    async def go():
+        gate = threading.Event()
+        e = FakeEngine(delay=gate)
+        b = AsyncBatcher(e, max_batch_size=1, batch_window_ms=0)
+        tasks = [asyncio.create_task(b.submit(p, 1)) for p in ([1], [1, 2], [3], [1, 2, 3])]
+        await asyncio.sleep(0.05)
+        gate.set()
+        await asyncio.gather(*tasks)
+        assert [batch[0][0] for batch in e.batches] == [(1,), (1, 2), (3,), (1, 2, 3)]
+        await b.close()
+
+    run(go())
