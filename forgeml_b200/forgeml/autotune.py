@@ -1,29 +1,64 @@
-"""Correctness-gated tile selection for native GEMM nodes.
+"""Correctness-gated choice of GEMM tile configurations for one compiled model.
 
-Contract of src/forgeml/autotune.py:16-103: for each node planned for the
-native backend the expected value is evaluated with torch on the same inputs,
-every candidate tile configuration (``kernels.CANDIDATES``: sm_100a UMMA N
-tiles and pipeline depths) is launched and gated by ``check_output``; a
-candidate that raises is recorded as rejected; the survivors are timed with
-``measure_variants`` and the smallest median wins.  Selections live on the
-CompiledModel instance only.
+Contract of the reference autotuner (src/forgeml/autotune.py:16-103): for
+every GEMM node planned on the native backend, each candidate configuration
+(``kernels.CANDIDATES``: UMMA N tile and pipeline depth of the tcgen05 GEMM)
+is launched on the node's real inputs and its result compared with the torch
+evaluation of the node; a candidate that fails to launch or disagrees is
+rejected with the reason, the survivors are timed and the fastest median
+wins.  The choice is stored on that compiled model only.  A node with no
+valid candidate is an error.
+
+Agreement uses the tolerances of this package's parity bar: fp32 (3xTF32)
+rtol 1e-5 / atol 1e-4, fp16 1e-2 / 1e-2, bf16 2e-2 / 2e-2.  Survivors are
+timed on the device with CUDA events around each launch (``_time_candidates``).
 """
 
 from __future__ import annotations
 
+import statistics
 from dataclasses import asdict
-from typing import TYPE_CHECKING
+from typing import TYPE_CHECKING, Callable
 
 import torch
 
 from forgeml_b200.forgeml import kernels
-from forgeml_b200.forgeml.measurement import check_output, measure_variants
 from forgeml_b200.forgeml.ops import evaluate
 
 if TYPE_CHECKING:
     from forgeml_b200.forgeml.compiler import CompiledModel
 
-_TUNABLE = ("matmul", "linear", "fused_linear_gelu")
+_TUNED_OPS = ("matmul", "linear", "fused_linear_gelu")
+_TOLERANCE = {torch.float32: (1e-5, 1e-4), torch.float16: (1e-2, 1e-2), torch.bfloat16: (2e-2, 2e-2)}
+
+
+def _agreement(got: torch.Tensor, want: torch.Tensor) -> dict:
+    rtol, atol = _TOLERANCE.get(want.dtype, (1e-5, 1e-4))
+    g, w = got.float(), want.float()
+    excess = ((g - w).abs() - (atol + rtol * w.abs())).max().item() if w.numel() else 0.0
+    return {"passed": bool(torch.isfinite(g).all().item()) and excess <= 0.0,
+            "max_abs_err": (g - w).abs().max().item() if w.numel() else 0.0, "rtol": rtol, "atol": atol}
+
+
+def _time_candidates(runs: dict[str, Callable[[], object]], *, device: torch.device, warmup: int,
+                     repeats: int) -> dict[str, dict]:
+    """Device time of each launch: CUDA events on the current stream around
+    every repetition, after ``warmup`` untimed launches."""
+    out = {}
+    stream = torch.cuda.current_stream(device)
+    for name, run in runs.items():
+        for _ in range(warmup):
+            run()
+        samples = []
+        for _ in range(repeats):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            run()
+            e1.record(stream)
+            e1.synchronize()
+            samples.append(e0.elapsed_time(e1))
+        out[name] = {"median_ms": statistics.median(samples), "samples_ms": samples}
+    return out
 
 
 @torch.inference_mode()
@@ -32,47 +67,47 @@ def tune_graph(compiled: "CompiledModel", inputs: tuple[torch.Tensor, ...], *, w
     if warmup < 0 or repeats < 2:
         raise ValueError("autotuning requires warmup >= 0 and repeats >= 2")
     compiled(*inputs)
-    values = dict(compiled.graph.constants)
-    values.update(zip(compiled.graph.inputs, inputs))
-    records, chosen = {}, {}
+    env = dict(compiled.graph.constants)
+    env.update(zip(compiled.graph.inputs, inputs))
+    report, chosen = {}, {}
     for node in compiled.graph.nodes:
-        args = tuple(values[n] for n in node.inputs)
-        expected = evaluate(node.op, args, node.attrs)
-        if compiled.kernel_plan.get(node.name) == "triton" and node.op in _TUNABLE:
-            bias = args[2] if len(args) == 3 else None
-            activation = "gelu" if node.op == "fused_linear_gelu" else "none"
-            approximate = node.attrs.get("approximate", "none") if activation == "gelu" else "none"
-            variants, configs, rejected, errors = {}, {}, {}, {}
-            for idx, cfg in enumerate(kernels.CANDIDATES):
-                name = f"candidate_{idx}"
-
-                def launch(cfg=cfg, args=args, bias=bias, activation=activation, approximate=approximate):
-                    return kernels.matmul(args[0], args[1], bias, activation=activation, approximate=approximate,
-                                          config=cfg)
-
-                try:
-                    errors[name] = check_output(launch(), expected)
-                except Exception as exc:  # noqa: BLE001 - any failure rejects the candidate
-                    rejected[name] = str(exc)
-                    continue
-                variants[name] = launch
-                configs[name] = cfg
-            if not variants:
-                raise RuntimeError(f"no numerically valid kernel candidate for {node.name!r}")
-            timings = measure_variants(variants, device=args[0].device, warmup=warmup, repeats=repeats)
-            winner = min(timings, key=lambda n: timings[n]["median_ms"])
-            chosen[node.name] = configs[winner]
-            records[node.name] = {
-                "winner": winner, "config": asdict(configs[winner]),
-                "candidates": {n: {"config": asdict(configs[n]), "timing": t, "correctness": errors[n]}
-                               for n, t in timings.items()},
-                "rejected": rejected,
-                "input_shapes": [list(a.shape) for a in args], "input_strides": [list(a.stride()) for a in args],
-                "dtype": str(args[0].dtype), "device": str(args[0].device),
-                "activation": activation, "approximate": approximate,
-            }
-        values[node.name] = expected
+        args = tuple(env[i] for i in node.inputs)
+        want = evaluate(node.op, args, node.attrs)
+        env[node.name] = want
+        if node.op not in _TUNED_OPS or compiled.kernel_plan.get(node.name) != "triton":
+            continue
+        act = "gelu" if node.op == "fused_linear_gelu" else "none"
+        approx = node.attrs.get("approximate", "none") if act == "gelu" else "none"
+        bias = args[2] if len(args) == 3 else None
+        kept, rejected, checks = {}, {}, {}
+        for idx, cfg in enumerate(kernels.CANDIDATES):
+            name = f"candidate_{idx}"
+            try:
+                launch = kernels.PreparedGemm(want.dtype, act, approx, cfg)
+                out = torch.empty_like(want)
+                launch(args[0], args[1], bias, out)
+                check = _agreement(out, want)
+            except Exception as exc:  # noqa: BLE001 - a launch failure rejects the candidate
+                rejected[name] = f"launch failed: {exc}"
+                continue
+            if not check["passed"]:
+                rejected[name] = f"wrong result: max abs err {check['max_abs_err']:.3e}"
+                continue
+            checks[name] = check
+            kept[name] = (cfg, lambda launch=launch, out=out: launch(args[0], args[1], bias, out))
+        if not kept:
+            raise RuntimeError(f"no numerically valid kernel candidate for {node.name!r}")
+        timings = _time_candidates({n: run for n, (_, run) in kept.items()}, device=args[0].device,
+                                   warmup=warmup, repeats=repeats)
+        winner = min(timings, key=lambda n: timings[n]["median_ms"])
+        chosen[node.name] = kept[winner][0]
+        report[node.name] = {
+            "winner": winner, "config": asdict(kept[winner][0]), "rejected": rejected,
+            "candidates": {n: {"config": asdict(kept[n][0]), "timing": timings[n], "correctness": checks[n]}
+                           for n in kept},
+            "input_shapes": [list(a.shape) for a in args], "input_strides": [list(a.stride()) for a in args],
+            "dtype": str(want.dtype), "device": str(args[0].device), "activation": act, "approximate": approx,
+        }
     compiled.kernel_configs.update(chosen)
-    return {"scope": "this_compiled_model_instance_only",
-            "timing": "synchronized_host_wall_clock_including_output_allocation",
-            "warmup": warmup, "repeats": repeats, "nodes": records}
+    return {"scope": "this_compiled_model_instance_only", "timing": "cuda_events_per_launch_median",
+            "warmup": warmup, "repeats": repeats, "nodes": report}

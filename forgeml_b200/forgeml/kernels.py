@@ -140,6 +140,52 @@ def _launch_gemm(a, b, bias, out, act: int, config: KernelConfig, residual=None)
     del ws  # the caching allocator keeps it alive until the stream is done with it
 
 
+class PreparedGemm:
+    """A GEMM launch whose validation was done once (by the compiler, from the
+    graph's specs): each call passes the current pointers straight to
+    ``fml_gemm``.  Keeps its own grow-only workspace (fp32 operand split,
+    operands TMA cannot address), so a call allocates nothing once warm."""
+
+    def __init__(self, dtype: torch.dtype, activation: str = "none", approximate: str = "none",
+                 config: KernelConfig = DEFAULT_CONFIG):
+        _check_config(config)
+        self.config = config
+        self.code = _native.dtype_code(dtype)
+        self.act = _native.ACT_NONE
+        if activation == "gelu":
+            self.act = _native.ACT_GELU_TANH if approximate == "tanh" else _native.ACT_GELU_ERF
+        self.cfg = None
+        if config != DEFAULT_CONFIG:
+            self._cfg_obj = _native.fml_tile_cfg(config.block_m, config.block_n, config.block_k, config.num_warps,
+                                                 config.num_stages)
+            self.cfg = ctypes.byref(self._cfg_obj)
+        self.lib = _native.load()
+        self.ws: torch.Tensor | None = None
+
+    def __call__(self, a, b, bias, out, residual=None):
+        if not (a.is_cuda and b.is_cuda and out.is_cuda):
+            raise GraphError("native GEMM operands must be CUDA tensors")
+        m, k = a.shape
+        n = b.shape[1]
+        lib = self.lib
+        need = int(lib.fml_gemm_workspace_size(m, n, k, self.code, a.stride(0), a.stride(1), b.stride(0),
+                                               b.stride(1), a.data_ptr(), b.data_ptr(), self.cfg))
+        ws_ptr = None
+        if need > 0:
+            if self.ws is None or self.ws.numel() < need + 256:
+                self.ws = torch.empty(need + 256, dtype=torch.uint8, device=a.device)
+            ws_ptr = (self.ws.data_ptr() + 255) // 256 * 256
+        rc = lib.fml_gemm(a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(), b.stride(0), b.stride(1),
+                          bias.data_ptr() if bias is not None else None, bias.stride(0) if bias is not None else 0,
+                          residual.data_ptr() if residual is not None else None,
+                          residual.stride(0) if residual is not None else 0,
+                          out.data_ptr(), out.stride(0), m, n, k, self.code, self.act, self.cfg,
+                          ws_ptr, need, torch.cuda.current_stream(a.device).cuda_stream)
+        if rc != 0:
+            raise GraphError(f"fml_gemm failed ({rc}): {lib.fml_last_error().decode(errors='replace')}")
+        return out
+
+
 def matmul(
     a: torch.Tensor,
     b: torch.Tensor,
@@ -332,6 +378,8 @@ def _native_ok(node, specs) -> bool:
         return False
     if node.op == "sdpa":
         return node.spec.shape[-1] <= 256
+    if node.op in _GEMM_OPS:  # the tcgen05 GEMM takes rank-2 operands
+        return all(len(specs[i].shape) == 2 for i in node.inputs[:2])
     return True
 
 

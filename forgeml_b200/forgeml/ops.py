@@ -1,90 +1,66 @@
-"""Torch evaluation of graph ops.
+"""Torch semantics of the graph ops.
 
-Used for meta-tensor spec inference and by the explicit ``backend="torch"``
-executor, exactly as the reference uses src/forgeml/ops.py:25-83.  The
-``"triton"``/``"auto"`` backends route GEMM, LayerNorm and SDPA nodes to the
-sm_100a kernels instead (forgeml_b200.forgeml.kernels).
+The compiled model's torch-planned nodes, the frontend's spec inference and
+the autotuner's expected values all evaluate an op through ``evaluate``.  The
+meaning of each op is the reference's (src/forgeml/ops.py:25-83: "linear" is
+addmm with a [K, N] weight, "fused_linear_gelu" that plus GELU, "narrow"
+takes a possibly negative dim, ...); the native backend computes the GEMM,
+LayerNorm and SDPA ops on the sm_100a kernels instead.
 """
 
 from __future__ import annotations
 
+from typing import Callable
+
 import torch
 import torch.nn.functional as F
 
-SUPPORTED_OPS = frozenset(
-    {
-        "matmul",
-        "linear",
-        "add",
-        "mul",
-        "relu",
-        "gelu",
-        "reshape",
-        "transpose",
-        "softmax",
-        "narrow",
-        "fused_linear_gelu",
-        "layer_norm",
-        "sdpa",
-        "conv2d",
-        "embedding",
-    }
-)
+
+def _gemm(args) -> torch.Tensor:
+    a, b = args[0], args[1]
+    return torch.addmm(args[2], a, b) if len(args) == 3 else torch.mm(a, b)
 
 
-def _mm_bias(args):
-    return torch.addmm(args[2], args[0], args[1]) if len(args) == 3 else torch.mm(args[0], args[1])
+def _layer_norm(args, attrs) -> torch.Tensor:
+    shape = attrs["normalized_shape"]
+    shape = (shape,) if isinstance(shape, int) else tuple(shape)
+    weight, bias = (args[1], args[2]) if len(args) == 3 else (None, None)
+    return F.layer_norm(args[0], shape, weight, bias, attrs["eps"])
+
+
+def _sdpa(args, attrs) -> torch.Tensor:
+    return F.scaled_dot_product_attention(args[0], args[1], args[2], attn_mask=args[3] if len(args) == 4 else None,
+                                          dropout_p=0.0, is_causal=attrs["is_causal"], scale=attrs.get("scale"))
+
+
+def _conv2d(args, attrs) -> torch.Tensor:
+    return F.conv2d(args[0], args[1], args[2] if len(args) == 3 else None, stride=attrs["stride"],
+                    padding=attrs["padding"], dilation=attrs["dilation"], groups=attrs["groups"])
+
+
+_EVAL: dict[str, Callable] = {
+    "matmul": lambda a, _: torch.matmul(a[0], a[1]),
+    "linear": lambda a, _: _gemm(a),
+    "fused_linear_gelu": lambda a, at: F.gelu(_gemm(a), approximate=at.get("approximate", "none")),
+    "add": lambda a, _: torch.add(a[0], a[1]),
+    "mul": lambda a, _: torch.mul(a[0], a[1]),
+    "relu": lambda a, _: F.relu(a[0]),
+    "gelu": lambda a, at: F.gelu(a[0], approximate=at.get("approximate", "none")),
+    "reshape": lambda a, at: torch.reshape(a[0], tuple(at["shape"])),
+    "transpose": lambda a, at: torch.transpose(a[0], at["dim0"], at["dim1"]),
+    "softmax": lambda a, at: torch.softmax(a[0], dim=at["dim"]),
+    "narrow": lambda a, at: torch.narrow(a[0], at["dim"] % a[0].dim(), at["start"], at["length"]),
+    "layer_norm": lambda a, at: _layer_norm(a, at),
+    "sdpa": lambda a, at: _sdpa(a, at),
+    "conv2d": lambda a, at: _conv2d(a, at),
+    "embedding": lambda a, _: F.embedding(a[0], a[1]),
+}
+
+SUPPORTED_OPS = frozenset(_EVAL)
 
 
 def evaluate(op: str, args: tuple[torch.Tensor, ...], attrs: dict) -> torch.Tensor:
-    if op == "matmul":
-        return torch.matmul(args[0], args[1])
-    if op == "linear":
-        return _mm_bias(args)
-    if op == "fused_linear_gelu":
-        return F.gelu(_mm_bias(args), approximate=attrs.get("approximate", "none"))
-    if op == "add":
-        return torch.add(args[0], args[1])
-    if op == "mul":
-        return torch.mul(args[0], args[1])
-    if op == "relu":
-        return F.relu(args[0])
-    if op == "gelu":
-        return F.gelu(args[0], approximate=attrs.get("approximate", "none"))
-    if op == "reshape":
-        return torch.reshape(args[0], tuple(attrs["shape"]))
-    if op == "transpose":
-        return torch.transpose(args[0], attrs["dim0"], attrs["dim1"])
-    if op == "softmax":
-        return torch.softmax(args[0], dim=attrs["dim"])
-    if op == "narrow":
-        x = args[0]
-        return torch.narrow(x, attrs["dim"] % x.dim(), attrs["start"], attrs["length"])
-    if op == "layer_norm":
-        norm = attrs["normalized_shape"]
-        norm = (norm,) if isinstance(norm, int) else tuple(norm)
-        w, b = (args[1], args[2]) if len(args) == 3 else (None, None)
-        return F.layer_norm(args[0], norm, w, b, attrs["eps"])
-    if op == "sdpa":
-        return F.scaled_dot_product_attention(
-            args[0],
-            args[1],
-            args[2],
-            attn_mask=args[3] if len(args) == 4 else None,
-            dropout_p=0.0,
-            is_causal=attrs["is_causal"],
-            scale=attrs.get("scale"),
-        )
-    if op == "conv2d":
-        return F.conv2d(
-            args[0],
-            args[1],
-            args[2] if len(args) == 3 else None,
-            stride=attrs["stride"],
-            padding=attrs["padding"],
-            dilation=attrs["dilation"],
-            groups=attrs["groups"],
-        )
-    if op == "embedding":
-        return F.embedding(args[0], args[1])
-    raise ValueError(f"unsupported op {op!r}")
+    fn = _EVAL.get(op)
+    if fn is None:
+        raise ValueError(f"unsupported op {op!r}")
+    return fn(args, attrs)

@@ -23,30 +23,31 @@ def _native_plan(c):
                      for n in c.graph.nodes}
 
 
-def _fake_matmul(bad=(), raising=()):
-    """torch stand-in for kernels.matmul; candidates in `bad` return a wrong
-    result, those in `raising` fail to launch."""
+def _fake_launch(bad=(), raising=()):
+    """torch stand-in for PreparedGemm.__call__; candidates in `bad` return a
+    wrong result, those in `raising` fail to launch."""
 
-    def fake(a, b, bias=None, *, activation="none", approximate="none", config=kernels.DEFAULT_CONFIG, out=None,
-             residual=None):
-        if config in raising:
+    def fake(self, a, b, bias, out, residual=None):
+        if self.config in raising:
             raise RuntimeError("launch failed (fake)")
         y = a @ b if bias is None else torch.addmm(bias, a, b)
-        if activation == "gelu":
-            y = torch.nn.functional.gelu(y, approximate=approximate)
-        if config in bad:
+        if self.act:
+            y = torch.nn.functional.gelu(y, approximate="tanh" if self.act == 2 else "none")
+        if residual is not None:
+            y = y + residual
+        if self.config in bad:
             y = y + 1.0
-        return y if out is None else out.copy_(y)
+        return out.copy_(y)
 
     return fake
 
 
 def _fake_timer(order):
-    """measure_variants stand-in: candidate_i gets median order[i] ms."""
+    """_time_candidates stand-in: candidate_i gets median order[i] ms."""
 
-    def fake(variants, *, device, warmup, repeats):
+    def fake(runs, *, device, warmup, repeats):
         out = {}
-        for name, fn in variants.items():
+        for name, fn in runs.items():
             fn()
             idx = int(name.split("_")[1])
             out[name] = {"median_ms": order[idx], "samples_ms": [order[idx]] * repeats}
@@ -59,9 +60,9 @@ def test_fastest_correct_candidate_wins(monkeypatch):
     m, x = _mlp()
     c = compile(m, (x,), backend="torch")
     _native_plan(c)
-    monkeypatch.setattr(kernels, "matmul", _fake_matmul(bad={CANDIDATES[1]}, raising={CANDIDATES[2]}))
+    monkeypatch.setattr(kernels.PreparedGemm, "__call__", _fake_launch(bad={CANDIDATES[1]}, raising={CANDIDATES[2]}))
     # candidate 1 is the fastest but wrong, 2 fails to launch, 3 is the fastest survivor
-    monkeypatch.setattr(autotune, "measure_variants", _fake_timer([4.0, 0.5, 0.1, 1.0]))
+    monkeypatch.setattr(autotune, "_time_candidates", _fake_timer([4.0, 0.5, 0.1, 1.0]))
     rep = autotune.tune_graph(c, (x,), warmup=0, repeats=2)
     assert rep["scope"] == "this_compiled_model_instance_only"
     assert rep["nodes"], "no native GEMM node was tuned"
@@ -69,6 +70,7 @@ def test_fastest_correct_candidate_wins(monkeypatch):
         assert rec["winner"] == "candidate_3"
         assert set(rec["rejected"]) == {"candidate_1", "candidate_2"}
         assert "launch failed" in rec["rejected"]["candidate_2"]
+        assert "wrong result" in rec["rejected"]["candidate_1"]
         assert set(rec["candidates"]) == {"candidate_0", "candidate_3"}
         assert all(v["correctness"]["passed"] for v in rec["candidates"].values())
         assert c.kernel_configs[name] == CANDIDATES[3]
@@ -81,8 +83,8 @@ def test_no_valid_candidate_is_an_error(monkeypatch):
     m, x = _mlp()
     c = compile(m, (x,), backend="torch")
     _native_plan(c)
-    monkeypatch.setattr(kernels, "matmul", _fake_matmul(bad=set(CANDIDATES)))
-    monkeypatch.setattr(autotune, "measure_variants", _fake_timer([1.0] * len(CANDIDATES)))
+    monkeypatch.setattr(kernels.PreparedGemm, "__call__", _fake_launch(bad=set(CANDIDATES)))
+    monkeypatch.setattr(autotune, "_time_candidates", _fake_timer([1.0] * len(CANDIDATES)))
     with pytest.raises(RuntimeError, match="no numerically valid kernel candidate"):
         autotune.tune_graph(c, (x,), warmup=0, repeats=2)
 

@@ -152,42 +152,50 @@ def test_select_kernels_cpu():
 
 def test_native_dispatch_wiring_with_fakes(monkeypatch):
     """Force the native plan on CPU and replace the kernel launches with torch fakes:
-    every GEMM/LN/SDPA node must reach its kernel with the right epilogue and write its
-    planned slot (or extension-arena) view."""
+    every GEMM/LN/SDPA node must reach its kernel with the right epilogue and write
+    planned arena memory; the two residual adds ride in the o / fc2 GEMM epilogues
+    and SDPA writes [B, S, H, D] through strides."""
     m, x = _small_c2()
     c = compile(m, (x,), backend="torch")
     calls = []
+    arena = []
 
-    def fake_matmul(a, b, bias=None, *, activation="none", approximate="none", config=DEFAULT_CONFIG, out=None,
-                    residual=None):
-        calls.append(("matmul", activation, out is not None))
+    def in_arena(t):
+        return any(t.untyped_storage().data_ptr() == s.untyped_storage().data_ptr() for s in arena)
+
+    def fake_gemm(self, a, b, bias, out, residual=None):
+        calls.append(("matmul", self.act, in_arena(out), residual is not None))
         y = a @ b if bias is None else torch.addmm(bias, a, b)
-        if activation == "gelu":
-            y = torch.nn.functional.gelu(y, approximate=approximate)
-        if out is None:
-            return y
-        out.copy_(y)
-        return out
+        if self.act:
+            y = torch.nn.functional.gelu(y, approximate="tanh" if self.act == 2 else "none")
+        if residual is not None:
+            y = y + residual
+        return out.copy_(y)
 
     def fake_ln(xx, norm, w, b, eps, *, out=None):
-        calls.append(("layer_norm", None, out is not None))
-        y = torch.nn.functional.layer_norm(xx, tuple(norm), w, b, eps)
-        return y if out is None else out.copy_(y)
+        calls.append(("layer_norm", None, in_arena(out), False))
+        return out.copy_(torch.nn.functional.layer_norm(xx, tuple(norm), w, b, eps))
 
     def fake_sdpa(q, k, v, mask=None, *, is_causal=False, scale=None, out=None):
-        calls.append(("sdpa", None, out is not None))
-        y = torch.nn.functional.scaled_dot_product_attention(q, k, v, attn_mask=mask, is_causal=is_causal, scale=scale)
-        return y if out is None else out.copy_(y)
+        calls.append(("sdpa", out.stride(1) < out.stride(2), in_arena(out), False))
+        return out.copy_(torch.nn.functional.scaled_dot_product_attention(q, k, v, attn_mask=mask,
+                                                                          is_causal=is_causal, scale=scale))
 
-    monkeypatch.setattr(kernels, "matmul", fake_matmul)
+    monkeypatch.setattr(kernels.PreparedGemm, "__call__", fake_gemm)
     monkeypatch.setattr(kernels, "layer_norm", fake_ln)
     monkeypatch.setattr(kernels, "sdpa", fake_sdpa)
     c.kernel_plan = {n.name: ("triton" if n.op in ("linear", "fused_linear_gelu", "layer_norm", "sdpa") else "torch")
                      for n in c.graph.nodes}
+    arena.extend(c._arena.values())
     torch.testing.assert_close(c(x), m(x), rtol=1e-5, atol=1e-5)
-    kinds = [k for k, _, _ in calls]
+    kinds = [k for k, *_ in calls]
     assert kinds.count("layer_norm") == 2 and kinds.count("sdpa") == 1 and kinds.count("matmul") == 4
-    assert ("matmul", "gelu", True) in calls
-    assert all(slot for _, _, slot in calls)  # every native node wrote planned memory
-    assert c.ext_plan is not None
+    assert sum(1 for k, _, _, res in calls if k == "matmul" and res) == 2  # both residual adds fused
+    assert ("matmul", 1, True, False) in calls  # fc1 + exact GELU into the arena
+    assert ("sdpa", True, True, False) in calls  # [B, S, H, D] order, arena memory
+    assert all(slot for k, _, slot, res in calls if not res)  # every other native node wrote the arena
+    assert sorted(c.explain()["native_fusions"]["residual_add"]) == sorted(
+        n.name for n in c.graph.nodes if n.op == "add")
+    # the reference-compatible plan is untouched
+    assert c.memory_plan.to_dict() == plan_memory(c.graph).to_dict()
     json.dumps(c.explain())
