@@ -1,15 +1,24 @@
-"""Graph optimisation pipeline feeding the compiled forward pass.
+"""Optimisation pipeline between the frontend and the compiled program.
 
-Same pass sequence and outcomes as the reference (src/forgeml/passes.py:
-410-430): dead-node elimination, constant folding (64 MiB cap), algebraic
-simplification (identity reshapes/transposes, reshape chains, transpose
-pairs), CSE (commutative add/mul), matmul+bias -> linear, linear/matmul(+bias)
--> fused_linear_gelu, shared-input linears -> one wide linear + narrow views
-(the fused QKV GEMM; ``<leader>_shared_weight_<n>`` naming), and a
-memory-aware topological schedule chosen among six candidate orders by planned
-bytes (ties by node-name tuple).  Fusion patterns decide which GEMM epilogues
-the native kernel runs, and the final order decides the slot plan, so both
-follow the reference's rules exactly.
+The pipeline is the reference's (src/forgeml/passes.py:410-430) pass for
+pass, because its outcome is observable: the optimised graph, its pass
+records and its slot plan are compared with the reference's one to one, and
+the fusions decide which epilogues the native GEMM runs.  Passes, in order:
+
+  eliminate_dead_nodes, fold_constants (results up to 64 MiB),
+  eliminate_dead_nodes, simplify_algebra (identity reshapes and transposes,
+  reshape-of-reshape, transpose pairs), common_subexpression_elimination
+  (add / mul commutative), canonicalize_linear (matmul + 1-D bias ->
+  linear), fuse_linear_gelu (gelu(linear | matmul [+ const bias]) ->
+  fused_linear_gelu), fuse_shared_projections (constant-weight linears of one
+  input -> one wide linear + narrow views: the fused QKV GEMM, constants
+  ``<first>_shared_weight_<n>`` / ``<first>_shared_bias_<n>``, node
+  ``<first>_shared_<n>``), eliminate_dead_nodes, schedule (six candidate
+  topological orders; the one with the fewest planned bytes, ties broken by
+  the order's node names).
+
+Every pass maps a validated graph to a validated graph; ``_Edit`` carries the
+bookkeeping they share (replacing, dropping and re-pointing nodes).
 """
 
 from __future__ import annotations
@@ -32,14 +41,19 @@ class PassRecord:
     nodes_after: int
 
 
-def _rebuild(graph: Graph, nodes: list[Node], constants: dict, outputs=None) -> Graph:
-    g = Graph(inputs=dict(graph.inputs), constants=constants, nodes=nodes,
-              outputs=tuple(graph.outputs if outputs is None else outputs), output_is_tuple=graph.output_is_tuple)
+def _graph(base: Graph, nodes, constants, outputs=None) -> Graph:
+    g = Graph(dict(base.inputs), constants, list(nodes), tuple(base.outputs if outputs is None else outputs),
+              base.output_is_tuple)
     g.validate()
     return g
 
 
-def _consumers(graph: Graph) -> dict[str, list[str]]:
+def _used_constants(constants: dict, nodes, outputs) -> dict:
+    wanted = {i for n in nodes for i in n.inputs} | set(outputs)
+    return {k: v for k, v in constants.items() if k in wanted}
+
+
+def _readers(graph: Graph) -> dict[str, list[str]]:
     out: dict[str, list[str]] = {}
     for n in graph.nodes:
         for i in n.inputs:
@@ -47,270 +61,267 @@ def _consumers(graph: Graph) -> dict[str, list[str]]:
     return out
 
 
-def _follow(aliases: dict[str, str], name: str) -> str:
-    while aliases.get(name, name) != name:
-        name = aliases[name]
-    return name
+class _Renames:
+    """Values replaced by other values (a removed node points at its stand-in)."""
+
+    def __init__(self):
+        self.to: dict[str, str] = {}
+
+    def __call__(self, name: str) -> str:
+        while name in self.to and self.to[name] != name:
+            name = self.to[name]
+        return name
+
+    def node(self, n: Node) -> Node:
+        return Node(n.name, n.op, tuple(self(i) for i in n.inputs), dict(n.attrs), n.spec)
 
 
-def _keep_used(constants: dict, nodes: list[Node], extra=()) -> dict:
-    used = {i for n in nodes for i in n.inputs} | set(extra)
-    return {k: v for k, v in constants.items() if k in used}
-
-
+# ------------------------------------------------------------------ passes
 def eliminate_dead_nodes(graph: Graph) -> Graph:
-    live = set(graph.outputs)
+    needed = set(graph.outputs)
     kept = []
     for n in reversed(graph.nodes):
-        if n.name in live:
+        if n.name in needed:
             kept.append(n)
-            live.update(n.inputs)
-    kept.reverse()
-    return _rebuild(graph, kept, {k: v for k, v in graph.constants.items() if k in live})
+            needed.update(n.inputs)
+    return _graph(graph, kept[::-1], {k: v for k, v in graph.constants.items() if k in needed})
 
 
 def fold_constants(graph: Graph) -> Graph:
-    constants = dict(graph.constants)
-    env = dict(constants)
-    nodes = []
+    known = dict(graph.constants)
+    kept = []
     for n in graph.nodes:
-        if not all(i in env for i in n.inputs):
-            nodes.append(n)
-            continue
-        in_bytes = sum(env[i].numel() * env[i].element_size() for i in dict.fromkeys(n.inputs))
-        if n.op not in VIEW_LIKE_OPS and (n.spec.nbytes > FOLD_LIMIT_BYTES or in_bytes > FOLD_LIMIT_BYTES):
-            nodes.append(n)
+        foldable = all(i in known for i in n.inputs)
+        if foldable and n.op not in VIEW_LIKE_OPS:
+            in_bytes = sum(known[i].numel() * known[i].element_size() for i in dict.fromkeys(n.inputs))
+            foldable = n.spec.nbytes <= FOLD_LIMIT_BYTES and in_bytes <= FOLD_LIMIT_BYTES
+        if not foldable:
+            kept.append(n)
             continue
         try:
             with torch.inference_mode():
-                val = evaluate(n.op, tuple(env[i] for i in n.inputs), dict(n.attrs))
+                known[n.name] = evaluate(n.op, tuple(known[i] for i in n.inputs), dict(n.attrs))
         except Exception as e:  # noqa: BLE001
             raise GraphError(f"constant folding failed at node {n.name!r}: {e}") from e
-        constants[n.name] = env[n.name] = val
-    return _rebuild(graph, nodes, _keep_used(constants, nodes, graph.outputs))
+    return _graph(graph, kept, _used_constants(known, kept, graph.outputs))
+
+
+def _transpose_pair(n: Node, rank: int) -> frozenset:
+    return frozenset((n.attrs["dim0"] % rank, n.attrs["dim1"] % rank))
 
 
 def simplify_algebra(graph: Graph) -> Graph:
-    aliases: dict[str, str] = {}
-    kept: dict[str, Node] = {}
-    nodes: list[Node] = []
+    rn = _Renames()
     specs = graph.specs()
-    for n in graph.nodes:
-        n = Node(n.name, n.op, tuple(_follow(aliases, i) for i in n.inputs), dict(n.attrs), n.spec)
+    kept: dict[str, Node] = {}
+    for original in graph.nodes:
+        n = rn.node(original)
+        src = kept.get(n.inputs[0]) if n.inputs else None
         if n.op == "reshape":
-            if specs[n.inputs[0]].shape == n.spec.shape:
-                aliases[n.name] = n.inputs[0]
+            if specs[n.inputs[0]].shape == n.spec.shape:  # identity reshape
+                rn.to[n.name] = n.inputs[0]
                 continue
-            src = kept.get(n.inputs[0])
-            if src is not None and src.op == "reshape":
+            if src is not None and src.op == "reshape":  # reshape of a reshape reads the source
                 n = Node(n.name, "reshape", src.inputs, dict(n.attrs), n.spec)
-        if n.op == "transpose":
+        elif n.op == "transpose":
             rank = len(n.spec.shape)
-            dims = frozenset((n.attrs["dim0"] % rank, n.attrs["dim1"] % rank))
-            if len(dims) == 1:
-                aliases[n.name] = n.inputs[0]
+            dims = _transpose_pair(n, rank)
+            if len(dims) == 1:  # transpose(d, d)
+                rn.to[n.name] = n.inputs[0]
                 continue
-            src = kept.get(n.inputs[0])
-            if (src is not None and src.op == "transpose"
-                    and frozenset((src.attrs["dim0"] % rank, src.attrs["dim1"] % rank)) == dims):
-                aliases[n.name] = _follow(aliases, src.inputs[0])
+            if src is not None and src.op == "transpose" and _transpose_pair(src, rank) == dims:
+                rn.to[n.name] = rn(src.inputs[0])  # a transpose undoing the previous one
                 continue
-        aliases[n.name] = n.name
         kept[n.name] = n
-        nodes.append(n)
-    outputs = tuple(_follow(aliases, o) for o in graph.outputs)
-    g = Graph(inputs=dict(graph.inputs), constants=dict(graph.constants), nodes=nodes, outputs=outputs,
-              output_is_tuple=graph.output_is_tuple)
+    g = Graph(dict(graph.inputs), dict(graph.constants), list(kept.values()),
+              tuple(rn(o) for o in graph.outputs), graph.output_is_tuple)
     g.validate()
     return eliminate_dead_nodes(g)
 
 
-def _frozen(v):
+def _hashable(v):
     if isinstance(v, (tuple, list)):
-        return tuple(_frozen(x) for x in v)
+        return tuple(_hashable(x) for x in v)
     if isinstance(v, dict):
-        return tuple(sorted((k, _frozen(x)) for k, x in v.items()))
+        return tuple(sorted((k, _hashable(x)) for k, x in v.items()))
     return v
 
 
 def common_subexpression_elimination(graph: Graph) -> Graph:
-    aliases: dict[str, str] = {}
-    seen: dict[tuple, str] = {}
-    nodes = []
-    for n in graph.nodes:
-        ins = tuple(_follow(aliases, i) for i in n.inputs)
-        key = (n.op, tuple(sorted(ins)) if n.op in ("add", "mul") else ins, _frozen(n.attrs), n.spec)
-        if key in seen:
-            aliases[n.name] = seen[key]
+    rn = _Renames()
+    first: dict[tuple, str] = {}
+    kept = []
+    for original in graph.nodes:
+        n = rn.node(original)
+        operands = tuple(sorted(n.inputs)) if n.op in ("add", "mul") else n.inputs
+        key = (n.op, operands, _hashable(n.attrs), n.spec)
+        if key in first:
+            rn.to[n.name] = first[key]
             continue
-        seen[key] = n.name
-        aliases[n.name] = n.name
-        nodes.append(Node(n.name, n.op, ins, dict(n.attrs), n.spec))
-    outputs = tuple(_follow(aliases, o) for o in graph.outputs)
-    return _rebuild(graph, nodes, _keep_used(graph.constants, nodes, outputs), outputs=outputs)
+        first[key] = n.name
+        kept.append(n)
+    outputs = tuple(rn(o) for o in graph.outputs)
+    return _graph(graph, kept, _used_constants(graph.constants, kept, outputs), outputs)
 
 
 def canonicalize_linear(graph: Graph) -> Graph:
-    """add(matmul(x, W), b) with a 1-D output-width b -> linear(x, W, b)."""
-    cons = _consumers(graph)
-    by = {n.name: n for n in graph.nodes}
+    """add(matmul(x, W), b), b 1-D of the output width, the matmul read only
+    there -> linear(x, W, b)."""
+    readers = _readers(graph)
+    nodes = {n.name: n for n in graph.nodes}
     specs = graph.specs()
-    repl: dict[str, Node] = {}
-    drop: set[str] = set()
+    new, gone = {}, set()
     for n in graph.nodes:
         if n.op != "add":
             continue
         for mm_name, bias in ((n.inputs[0], n.inputs[1]), (n.inputs[1], n.inputs[0])):
-            mm = by.get(mm_name)
-            bs = specs.get(bias)
-            if (mm is None or mm.op != "matmul" or mm.name in graph.outputs or len(cons.get(mm.name, ())) != 1
-                    or bs is None or len(bs.shape) != 1 or bs.shape[0] != mm.spec.shape[1]):
-                continue
-            repl[n.name] = Node(n.name, "linear", mm.inputs + (bias,), {}, n.spec)
-            drop.add(mm.name)
-            break
-    nodes = [repl.get(n.name, n) for n in graph.nodes if n.name not in drop]
-    return _rebuild(graph, nodes, _keep_used(graph.constants, nodes, graph.outputs))
+            mm, bs = nodes.get(mm_name), specs.get(bias)
+            if (mm is not None and mm.op == "matmul" and mm.name not in graph.outputs
+                    and len(readers.get(mm.name, ())) == 1 and bs is not None and len(bs.shape) == 1
+                    and bs.shape[0] == mm.spec.shape[1]):
+                new[n.name] = Node(n.name, "linear", mm.inputs + (bias,), {}, n.spec)
+                gone.add(mm.name)
+                break
+    kept = [new.get(n.name, n) for n in graph.nodes if n.name not in gone]
+    return _graph(graph, kept, _used_constants(graph.constants, kept, graph.outputs))
 
 
 def fuse_linear_gelu(graph: Graph) -> Graph:
-    """gelu(linear|matmul) and gelu(add(matmul, const bias)) -> fused_linear_gelu."""
-    cons = _consumers(graph)
-    by = {n.name: n for n in graph.nodes}
-    fused: dict[str, Node] = {}
-    drop: set[str] = set()
+    """gelu(linear | matmul) and gelu(add(matmul, constant 1-D bias)), each
+    producer read only by the next -> fused_linear_gelu."""
+    readers = _readers(graph)
+    nodes = {n.name: n for n in graph.nodes}
 
-    def single_use(node):
-        return node.name not in graph.outputs and len(cons.get(node.name, ())) == 1
+    def private(n: Node) -> bool:
+        return n.name not in graph.outputs and len(readers.get(n.name, ())) == 1
 
+    new, gone = {}, set()
     for n in graph.nodes:
         if n.op != "gelu" or len(n.inputs) != 1:
             continue
-        approx = {"approximate": n.attrs.get("approximate", "none")}
-        p = by.get(n.inputs[0])
-        if p is not None and p.op in ("linear", "matmul") and single_use(p):
-            fused[n.name] = Node(n.name, "fused_linear_gelu", p.inputs, approx, n.spec)
-            drop.add(p.name)
+        attrs = {"approximate": n.attrs.get("approximate", "none")}
+        p = nodes.get(n.inputs[0])
+        if p is None or not private(p):
             continue
-        if p is None or p.op != "add" or not single_use(p):
+        if p.op in ("linear", "matmul"):
+            new[n.name] = Node(n.name, "fused_linear_gelu", p.inputs, attrs, n.spec)
+            gone.add(p.name)
             continue
-        mm, bias = None, None
-        for cand, other in ((p.inputs[0], p.inputs[1]), (p.inputs[1], p.inputs[0])):
-            c = by.get(cand)
-            if c is not None and c.op == "matmul" and other in graph.constants:
-                mm, bias = c, other
-                break
-        if mm is None or not single_use(mm):
+        if p.op != "add":
             continue
+        pick = next(((nodes[a], b) for a, b in ((p.inputs[0], p.inputs[1]), (p.inputs[1], p.inputs[0]))
+                     if a in nodes and nodes[a].op == "matmul" and b in graph.constants), None)
+        if pick is None or not private(pick[0]):
+            continue
+        mm, bias = pick
         bt = graph.constants[bias]
-        if bt.dim() != 1 or bt.shape[0] != mm.spec.shape[1] or len(mm.spec.shape) != 2:
-            continue
-        fused[n.name] = Node(n.name, "fused_linear_gelu", (mm.inputs[0], mm.inputs[1], bias), approx, n.spec)
-        drop.update((mm.name, p.name))
-    if not fused:
-        return _rebuild(graph, list(graph.nodes), dict(graph.constants))
-    nodes = [fused.get(n.name, n) for n in graph.nodes if n.name not in drop]
-    return _rebuild(graph, nodes, _keep_used(graph.constants, nodes, graph.outputs))
+        if bt.dim() == 1 and bt.shape[0] == mm.spec.shape[1] and len(mm.spec.shape) == 2:
+            new[n.name] = Node(n.name, "fused_linear_gelu", (mm.inputs[0], mm.inputs[1], bias), attrs, n.spec)
+            gone.update((mm.name, p.name))
+    kept = [new.get(n.name, n) for n in graph.nodes if n.name not in gone]
+    constants = _used_constants(graph.constants, kept, graph.outputs) if new else dict(graph.constants)
+    return _graph(graph, kept, constants)
 
 
 def fuse_shared_projections(graph: Graph) -> Graph:
-    """Linears with constant weights reading the same input -> one wide linear
-    followed by one narrow view per original linear (e.g. Q, K, V)."""
-    index = {n.name: i for i, n in enumerate(graph.nodes)}
-    specs = graph.specs()
-    groups: dict[tuple[str, int], list[Node]] = {}
+    """Two or more linears with constant weights (and biases) reading the same
+    input -> one wide linear over the concatenated weights, then one narrow
+    view per original linear, in graph order (the fused QKV GEMM)."""
+    position = {n.name: i for i, n in enumerate(graph.nodes)}
+    families: dict[tuple[str, int], list[Node]] = {}
     for n in graph.nodes:
-        if n.op != "linear" or n.inputs[1] not in graph.constants:
-            continue
-        if len(n.inputs) == 3 and n.inputs[2] not in graph.constants:
-            continue
-        groups.setdefault((n.inputs[0], len(n.inputs)), []).append(n)
-    groups = {k: v for k, v in groups.items() if len(v) >= 2}
-    if not groups:
-        return _rebuild(graph, list(graph.nodes), dict(graph.constants))
-    taken = set(graph.inputs) | set(graph.constants) | set(index)
-    constants = dict(graph.constants)
-    counter = [0]
+        if n.op == "linear" and all(i in graph.constants for i in n.inputs[1:]):
+            families.setdefault((n.inputs[0], len(n.inputs)), []).append(n)
+    families = {k: sorted(v, key=lambda m: position[m.name]) for k, v in families.items() if len(v) > 1}
+    if not families:
+        return _graph(graph, graph.nodes, dict(graph.constants))
+    taken = set(graph.inputs) | set(graph.constants) | set(position)
+    serial = [0]
 
-    def fresh(hint):
+    def unused(stem: str) -> str:
         while True:
-            counter[0] += 1
-            cand = f"{hint}_{counter[0]}"
-            if cand not in taken:
-                taken.add(cand)
-                return cand
+            serial[0] += 1
+            name = f"{stem}_{serial[0]}"
+            if name not in taken:
+                taken.add(name)
+                return name
 
-    emit: dict[str, list[Node]] = {}
-    drop: set[str] = set()
-    for members in groups.values():
-        members.sort(key=lambda m: index[m.name])
+    constants = dict(graph.constants)
+    specs = graph.specs()
+    replacement: dict[str, list[Node]] = {}
+    gone: set[str] = set()
+    for members in families.values():
         lead = members[0]
         if len({constants[m.inputs[1]].dtype for m in members}) != 1:
             continue
-        if len(lead.inputs) == 3 and len({constants[m.inputs[2]].dtype for m in members}) > 1:
+        with_bias = len(lead.inputs) == 3
+        if with_bias and len({constants[m.inputs[2]].dtype for m in members}) != 1:
             continue
-        xs = specs[lead.inputs[0]]
-        wname = fresh(f"{lead.name}_shared_weight")
-        constants[wname] = torch.cat([constants[m.inputs[1]] for m in members], dim=1).contiguous()
-        ins = [lead.inputs[0], wname]
-        if len(lead.inputs) == 3:
-            bname = fresh(f"{lead.name}_shared_bias")
-            constants[bname] = torch.cat([constants[m.inputs[2]] for m in members])
-            ins.append(bname)
+        w = unused(f"{lead.name}_shared_weight")
+        constants[w] = torch.cat([constants[m.inputs[1]] for m in members], dim=1).contiguous()
+        ins = (lead.inputs[0], w)
+        if with_bias:
+            b = unused(f"{lead.name}_shared_bias")
+            constants[b] = torch.cat([constants[m.inputs[2]] for m in members])
+            ins += (b,)
+        x = specs[lead.inputs[0]]
+        wide_name = unused(f"{lead.name}_shared")
         width = sum(m.spec.shape[1] for m in members)
-        wide = fresh(f"{lead.name}_shared")
-        out = [Node(wide, "linear", tuple(ins), {}, TensorSpec((xs.shape[0], width), xs.dtype, xs.device))]
-        off = 0
+        block = [Node(wide_name, "linear", ins, {}, TensorSpec((x.shape[0], width), x.dtype, x.device))]
+        start = 0
         for m in members:
-            out.append(Node(m.name, "narrow", (wide,), {"dim": 1, "start": off, "length": m.spec.shape[1]}, m.spec))
-            off += m.spec.shape[1]
-            drop.add(m.name)
-        emit[lead.name] = out
-    nodes: list[Node] = []
+            block.append(Node(m.name, "narrow", (wide_name,), {"dim": 1, "start": start, "length": m.spec.shape[1]},
+                              m.spec))
+            start += m.spec.shape[1]
+            gone.add(m.name)
+        replacement[lead.name] = block
+    out = []
     for n in graph.nodes:
-        if n.name in emit:
-            nodes.extend(emit[n.name])
-        elif n.name not in drop:
-            nodes.append(n)
-    return _rebuild(graph, nodes, constants)
+        if n.name in replacement:
+            out.extend(replacement[n.name])
+        elif n.name not in gone:
+            out.append(n)
+    return _graph(graph, out, constants)
 
 
-def _topo_order(graph: Graph, score) -> list[Node]:
+# ------------------------------------------------------------------ scheduling
+def _greedy_order(graph: Graph, priority) -> list[Node]:
+    """A topological order that repeatedly runs the ready node of highest
+    ``priority(node, original position, bytes its run frees)``."""
+    position = {n.name: i for i, n in enumerate(graph.nodes)}
+    nodes = {n.name: n for n in graph.nodes}
+    specs = graph.specs()
     outputs = set(graph.outputs)
-    index = {n.name: i for i, n in enumerate(graph.nodes)}
-    by = {n.name: n for n in graph.nodes}
-    cons: dict[str, set[str]] = {}
-    waiting: dict[str, set[str]] = {}
+    readers: dict[str, set[str]] = {}
     for n in graph.nodes:
         for i in set(n.inputs):
-            cons.setdefault(i, set()).add(n.name)
-        waiting[n.name] = {i for i in n.inputs if i in index}
-    specs = graph.specs()
-    remaining_uses = {k: len(v) for k, v in cons.items() if k in index}
+            readers.setdefault(i, set()).add(n.name)
+    blockers = {n.name: {i for i in n.inputs if i in position} for n in graph.nodes}
+    reads_left = {k: len(v) for k, v in readers.items() if k in position}
 
-    def freed(n: Node) -> int:
+    def frees(n: Node) -> int:
         return sum(specs[i].nbytes for i in set(n.inputs)
-                   if i not in outputs and i in index and remaining_uses.get(i, 0) == 1)
+                   if i in position and i not in outputs and reads_left.get(i, 0) == 1)
 
-    ready = [n for n in graph.nodes if not waiting[n.name]]
-    order: list[Node] = []
+    ready = [n for n in graph.nodes if not blockers[n.name]]
+    order = []
     while ready:
-        best = max(ready, key=lambda n: score(n, index[n.name], freed(n)))
-        ready.remove(best)
-        order.append(best)
-        for c in sorted(cons.get(best.name, ())):
-            waiting[c].discard(best.name)
-            if not waiting[c]:
-                ready.append(by[c])
-        for i in set(best.inputs):
-            if i in remaining_uses:
-                remaining_uses[i] -= 1
+        nxt = max(ready, key=lambda n: priority(n, position[n.name], frees(n)))
+        ready.remove(nxt)
+        order.append(nxt)
+        for r in sorted(readers.get(nxt.name, ())):
+            blockers[r].discard(nxt.name)
+            if not blockers[r]:
+                ready.append(nodes[r])
+        for i in set(nxt.inputs):
+            if i in reads_left:
+                reads_left[i] -= 1
     if len(order) != len(graph.nodes):
         raise GraphError("graph contains a cycle")
     return order
 
 
-_SCHEDULE_SCORES = (
+_PRIORITIES = (
     lambda n, i, fr: (fr - n.spec.nbytes, -i),
     lambda n, i, fr: (fr - 2 * n.spec.nbytes, -i),
     lambda n, i, fr: (fr - n.spec.nbytes // 2, -i),
@@ -321,16 +332,13 @@ _SCHEDULE_SCORES = (
 
 
 def schedule(graph: Graph) -> Graph:
-    orders, seen = [], set()
-    for score in _SCHEDULE_SCORES:
-        order = _topo_order(graph, score)
-        key = tuple(n.name for n in order)
-        if key not in seen:
-            seen.add(key)
-            orders.append(order)
-    best = min(orders, key=lambda o: (plan_memory(_rebuild(graph, o, dict(graph.constants))).planned_bytes,
-                                      tuple(n.name for n in o)))
-    return _rebuild(graph, best, dict(graph.constants))
+    candidates: dict[tuple, list[Node]] = {}
+    for priority in _PRIORITIES:
+        order = _greedy_order(graph, priority)
+        candidates.setdefault(tuple(n.name for n in order), order)
+    best = min(candidates.items(),
+               key=lambda kv: (plan_memory(_graph(graph, kv[1], dict(graph.constants))).planned_bytes, kv[0]))[1]
+    return _graph(graph, best, dict(graph.constants))
 
 
 PIPELINE = (
@@ -349,11 +357,11 @@ PIPELINE = (
 
 def optimize(graph: Graph) -> tuple[Graph, list[PassRecord]]:
     graph.validate()
-    work = graph.clone()
+    g = graph.clone()
     records = []
-    for name, fn in PIPELINE:
-        before = len(work.nodes)
-        work = fn(work)
-        work.validate()
-        records.append(PassRecord(name, before, len(work.nodes)))
-    return work, records
+    for name, run in PIPELINE:
+        before = len(g.nodes)
+        g = run(g)
+        g.validate()
+        records.append(PassRecord(name, before, len(g.nodes)))
+    return g, records
