@@ -227,6 +227,13 @@ class ShardedDecoder(nn.Module):
             es = torch.empty((), dtype=dtype).element_size()
             slot = max(16, (max(max_requests, 32) * h * es + 15) // 16 * 16)
             self._peer_ar = peer.PeerAllReduce(context, max_bytes=slot)
+        # Decode steps of 4 or more TP ranks run as two half-batches (_core);
+        # the second half reduces through its own peer context.
+        self.split_batches = context.tp_size >= 4
+        self._peer_ar2 = None
+        self._side_stream = None
+        if self._peer_ar is not None and context.pp_size == 1:
+            self._peer_ar2 = peer.PeerAllReduce(context, max_bytes=self._peer_ar.max_bytes)
         self._fused_cache: dict[int, bool] = {}
 
     # ------------------------------------------------------------------ math
@@ -246,7 +253,7 @@ class ShardedDecoder(nn.Module):
         return ok
 
     def _layer_fused(self, L: _Layer, lid: int, x: torch.Tensor, b: int, t: int, slots: torch.Tensor,
-                     starts: torch.Tensor) -> torch.Tensor:
+                     starts: torch.Tensor, ar) -> torch.Tensor:
         bt = b * t
         h = self.config.hidden_size
         hl, hd, hl_hd = self.num_heads_local, self.head_dim, self._hl_hd
@@ -270,9 +277,9 @@ class ShardedDecoder(nn.Module):
             x = L.o(attn, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x)
         elif fused_ar_enabled(tp):
             x = L.o.fused(attn, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x,
-                          ar_ctx=self._peer_ar.handle)
+                          ar_ctx=ar.handle)
         else:
-            x = self._tp_sum_add(L.o(attn, torch.empty((bt, h), dtype=self.dtype, device=dev)), x)
+            x = self._tp_sum_add(L.o(attn, torch.empty((bt, h), dtype=self.dtype, device=dev)), x, ar)
         if ln_mode == "fold":
             lin, wsum, wbias = L.up_ln
             mid = lin.fused(x, torch.empty((bt, L.wup.shape[0]), dtype=self.dtype, device=dev),
@@ -287,16 +294,16 @@ class ShardedDecoder(nn.Module):
             return L.down(mid, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x)
         if fused_ar_enabled(tp):
             return L.down.fused(mid, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x,
-                                ar_ctx=self._peer_ar.handle)
-        return self._tp_sum_add(L.down(mid, torch.empty((bt, h), dtype=self.dtype, device=dev)), x)
+                                ar_ctx=ar.handle)
+        return self._tp_sum_add(L.down(mid, torch.empty((bt, h), dtype=self.dtype, device=dev)), x, ar)
 
     def _layer(self, L: _Layer, lid: int, x: torch.Tensor, b: int, t: int, slots: torch.Tensor,
-               starts: torch.Tensor) -> torch.Tensor:
+               starts: torch.Tensor, ar) -> torch.Tensor:
         ctx = self.context
         bt = b * t
         if self._fused_ok(bt):
             with record_function("nebula::layer_fused"):
-                return self._layer_fused(L, lid, x, b, t, slots, starts)
+                return self._layer_fused(L, lid, x, b, t, slots, starts, ar)
         h = self.config.hidden_size
         hl, hd, hl_hd = self.num_heads_local, self.head_dim, self._hl_hd
         dev = x.device
@@ -311,26 +318,60 @@ class ShardedDecoder(nn.Module):
         if ctx.tp_size == 1:
             x = L.o(attn, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x)
         else:
-            x = self._tp_sum_add(L.o(attn, torch.empty((bt, h), dtype=self.dtype, device=dev)), x)
+            x = self._tp_sum_add(L.o(attn, torch.empty((bt, h), dtype=self.dtype, device=dev)), x, ar)
         h2 = _ln(x, L.ln2_w, L.ln2_b, torch.empty_like(x), bt)
         mid = L.up(h2, torch.empty((bt, L.wup.shape[0]), dtype=self.dtype, device=dev), act=_native.ACT_GELU_TANH)
         if ctx.tp_size == 1:
             x = L.down(mid, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x)
         else:
-            x = self._tp_sum_add(L.down(mid, torch.empty((bt, h), dtype=self.dtype, device=dev)), x)
+            x = self._tp_sum_add(L.down(mid, torch.empty((bt, h), dtype=self.dtype, device=dev)), x, ar)
         return x
 
-    def _tp_sum_add(self, part: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    def _tp_sum_add(self, part: torch.Tensor, x: torch.Tensor, ar) -> torch.Tensor:
         """x + SUM-all-reduce(part) over the TP group (reference runtime.py:146,154)."""
-        if self._peer_ar is not None and self._peer_ar.fits(part) and x.is_contiguous():
+        if ar is not None and ar.fits(part) and x.is_contiguous():
             with record_function("nebula::tp_all_reduce_add"):
-                return self._peer_ar(part, x, torch.empty_like(x))
+                return ar(part, x, torch.empty_like(x))
         self.context.all_reduce(part)
         return ops.add(x, part)
 
+    def _split_ok(self, b: int, t: int) -> bool:
+        """Whether a step runs as two half-batches on two streams (see _core)."""
+        return (self.split_batches and t == 1 and b >= 2 and self.context.pp_size == 1
+                and self._peer_ar2 is not None and self._fused_ok(b - b // 2))
+
     def _core(self, tokens: torch.Tensor, slots: torch.Tensor, starts: torch.Tensor, b: int, t: int,
               last_only: bool) -> torch.Tensor:
-        """Stage-local forward + hand-off; returns logits on the last stage, else None."""
+        """Stage-local forward + hand-off; returns logits on the last stage, else None.
+
+        With tensor parallelism a decode step is a chain of short launches
+        whose time is mostly latency (the weights a rank streams shrink with
+        the TP degree, a launch's fixed cost does not).  There the batch runs
+        as two halves on two streams, each with its own peer all-reduce
+        context: one half's GEMMs, attention and reductions fill the other's
+        waits.  Every request's arithmetic is that of an unsplit step of half
+        the batch."""
+        if not self._split_ok(b, t):
+            return self._core_rows(tokens, slots, starts, b, t, last_only, self._peer_ar)
+        dev = self.context.device
+        h0 = b // 2
+        logits = torch.empty((b, self.config.vocab_size), dtype=self.dtype, device=dev)
+        main = torch.cuda.current_stream(dev)
+        if self._side_stream is None:
+            self._side_stream = torch.cuda.Stream(device=dev)
+        side = self._side_stream
+        side.wait_stream(main)
+        self._core_rows(tokens[:h0], slots[:h0], starts[:h0], h0, 1, last_only, self._peer_ar, out=logits[:h0])
+        with torch.cuda.stream(side):
+            self._core_rows(tokens[h0:], slots[h0:], starts[h0:], b - h0, 1, last_only, self._peer_ar2,
+                            out=logits[h0:])
+        main.wait_stream(side)
+        return logits
+
+    def _core_rows(self, tokens: torch.Tensor, slots: torch.Tensor, starts: torch.Tensor, b: int, t: int,
+                   last_only: bool, ar, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Forward of these rows on this stage (all-reduce context ``ar``);
+        logits on the last stage (into ``out`` when given), else None."""
         ctx = self.context
         h = self.config.hidden_size
         dev = ctx.device
@@ -342,7 +383,7 @@ class ShardedDecoder(nn.Module):
                 dist.recv(x, src=ctx.rank - ctx.tp_size)
         for L, lid in zip(self.layers, self.owned_layer_ids):
             with record_function("nebula::layer"):
-                x = self._layer(L, lid, x, b, t, slots, starts)
+                x = self._layer(L, lid, x, b, t, slots, starts, ar)
         if not self.is_last:
             with record_function("nebula::pp_send"):
                 dist.send(x, dst=ctx.rank + ctx.tp_size)
@@ -351,8 +392,9 @@ class ShardedDecoder(nn.Module):
         stride = t * h if last_only else h
         src = x[(t - 1):] if last_only else x  # row (t-1) of each request, stride t*h
         hf = _ln(src, self.lnf_w, self.lnf_b, torch.empty((rows, h), dtype=self.dtype, device=dev), rows, x_stride=stride)
-        logits = self.head_gemm(hf, torch.empty((rows, self.config.vocab_size), dtype=self.dtype, device=dev))
-        return logits
+        if out is None:
+            out = torch.empty((rows, self.config.vocab_size), dtype=self.dtype, device=dev)
+        return self.head_gemm(hf, out)
 
     # ------------------------------------------------------------------ API
     def forward(self, tokens: torch.Tensor, request_ids: tuple[int, ...], start_pos,
@@ -458,9 +500,11 @@ class ShardedDecoder(nn.Module):
     def close(self) -> None:
         """Release the captured graphs and the peer all-reduce buffers."""
         self.release_graphs()
-        if self._peer_ar is not None:
-            self._peer_ar.close()
-            self._peer_ar = None
+        for name in ("_peer_ar", "_peer_ar2"):
+            ar = getattr(self, name)
+            if ar is not None:
+                ar.close()
+                setattr(self, name, None)
 
 
 def fused_enabled() -> bool:
