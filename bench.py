@@ -361,8 +361,8 @@ def reference_forgeml_cpu() -> dict | None:
 
 # DRAM traffic per launch over the algorithmic bytes, from one ncu capture of
 # each kernel family (dram__bytes_read.sum + dram__bytes_write.sum):
-#   attention: ncu --set full -k regex:neb_attn -s 3 -c 1 ... bench.py --case attention --steps 20
-#   gemm:      ncu --set full -k regex:gemm_kernel ... bench.py --case gemm-decode --steps 20 (down projection)
+#   attention: ncu --set full --clock-control none -k regex:neb_attn -s 3 -c 1 ... bench.py --case attention --steps 20
+#   gemm:      ncu --set full --clock-control none -k regex:gemm_kernel ... bench.py --case gemm-decode --steps 20 (down projection)
 # Traffic in the JSON line is this ratio times the launch's algorithmic bytes.
 TRAFFIC_RATIO = {"attention": (268.618240e6 + 4.372736e6) / 268697600, "gemm": (34.288384e6 + 1.28e3) / 34340864}
 

@@ -645,7 +645,7 @@ __device__ __forceinline__ void st_shared_u16(uint32_t addr, uint32_t v) {
 // mean and rstd come from ln_stats.  (The reference rounds LN(x) to the model
 // dtype before the product; here the product sees it unrounded.)
 __device__ __forceinline__ void ln_fold8(const Params& p, const Smem& s, int BNv, int r, int n0, float (&x)[8]) {
-  const float2 ms = ld_shared_v2(s.aux + (uint32_t)(8 * BNv * 8) + (uint32_t)(r * 8));
+  const float2 ms = ld_shared_v2(s.aux + (uint32_t)aux_rowst(BNv) + (uint32_t)(r * 8));
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const int n = min(n0 + e, p.cols_out - 1);

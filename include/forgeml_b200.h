@@ -104,7 +104,9 @@ FML_API int fml_gemm(const void* a, int64_t lda_m, int64_t lda_k,
  * the process exits).  Problems whose packing needs more than that return
  * FML_EWORKSPACE without launching.  The first call on a device looks up the
  * scratch address (cudaGetSymbolAddress) with that device current; make that
- * first call before any stream capture.  All calls share the one array:
+ * first call before any stream capture.  The address is kept for the life of
+ * the process: after cudaDeviceReset on a device, do not call this entry point
+ * on that device again in the same process.  All calls share the one array:
  * calls whose executions overlap on the GPU (different streams, or other
  * host threads) race on it, so serialise them.  Everything the kernels read
  * from the scratch is written earlier in the same call, so the contents left
