@@ -395,61 +395,110 @@ def _graph_time_us(fns, reps: int = 5) -> float:
     return best
 
 
-def kernel_rooflines(engine, dev, ctx_len: int, ms_per_step: float) -> dict:
-    """HBM rooflines of the decode step's two kernel families, each timed live
+def _step_lanes(dec, b: int) -> list[int]:
+    """Rows of each half-batch lane a decode step of ``b`` requests runs."""
+    return [b // 2, b - b // 2] if dec._split_ok(b, 1) else [b]
+
+
+def all_reduce_family_us(dec, dev, world: int) -> dict | None:
+    """Device time of one decode step's TP all-reduces (2 per layer and lane,
+    [rows, d] each, + residual) replayed from a CUDA graph on every rank at
+    once (max over ranks).  Collective: every rank calls it."""
+    import torch.distributed as dist
+
+    if world == 1 or dec._peer_ar is None:
+        return None
+    h = dec.config.hidden_size
+    calls = []
+    for rows in _step_lanes(dec, BATCH):
+        part = torch.randn(rows, h, device=dev).to(dec.dtype)
+        res = torch.randn(rows, h, device=dev).to(dec.dtype)
+        out = torch.empty_like(part)
+        calls += [lambda p=part, r=res, o=out: dec._peer_ar(p, r, o)] * (2 * len(dec.layers))
+    dist.barrier()
+    us = _graph_time_us(calls)
+    t = torch.tensor([us], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    us = float(t.item())
+    return {"kernel": "ar_ll_kernel / ar_ts_kernel (peer all-reduce + residual)", "us_per_step": us,
+            "launches_per_step": len(calls), "us_per_launch": us / len(calls),
+            "bytes_out_per_rank_per_launch": (world - 1) * (BATCH // len(_step_lanes(dec, BATCH))) * h * 2}
+
+
+def kernel_rooflines(engine, dev, ctx_len: int, ms_per_step: float, ar_family: dict | None = None) -> dict:
+    """HBM rooflines of the decode step's kernel families, each timed live
     with CUDA events as one step's launches of that family replayed from a
     CUDA graph on the engine's own weights and cache pools:
-      gemm       gemm_kernel (the 4 linears of every layer + lm_head);
-                 algorithmic bytes = weights + activations in + outputs (+ residual)
-      attention  neb_attn_bulk_kernel, one launch per layer at the step's context;
-                 algorithmic bytes = K + V rows + q + out
-    The family with the larger share of the step is reported as `roofline`."""
+      gemm       gemm_kernel as the step runs it: per layer the LayerNorm-
+                 folded QKV launch with the KV-append epilogue, o (+ residual
+                 at TP1), the LayerNorm-folded up launch with tanh GELU, down
+                 (+ residual at TP1); then lm_head.  Per half-batch lane when
+                 the step is split.  Algorithmic bytes = weights + activations
+                 in + outputs (K/V rows included) (+ residual)
+      attention  neb_attn_bulk_kernel, one launch per layer and lane at the
+                 step's context; algorithmic bytes = K + V rows + q + out
+    The family with the larger share of the step is reported as `roofline`;
+    `budget` splits the step's time among the families (they overlap when
+    the step runs two lanes, so the remainder can be negative)."""
     from forgeml_b200.nebula import ops
     from forgeml_b200 import _native
 
     dec = engine.decoder
     es = torch.empty((), dtype=dec.dtype).element_size()
-    b, h = BATCH, dec.config.hidden_size
+    h = dec.config.hidden_size
     hl_hd = dec.num_heads_local * dec.head_dim
+    tp1 = dec.context.tp_size == 1
     g = torch.Generator(device=dev).manual_seed(11)
+    lanes = _step_lanes(dec, BATCH)
 
     def rnd(*shape):
         return torch.randn(*shape, device=dev, generator=g).to(dec.dtype)
 
-    # ---- GEMM family: one decode step's linears
-    x = rnd(b, h)
-    attn = rnd(b, hl_hd)
+    # ---- GEMM family: one decode step's linears, as launched by the step
     fns, gbytes = [], 0
-    for L in dec.layers:
-        f_l = L.wup.shape[0]
-        qkv_out, o_out, up_out, dn_out = (torch.empty(b, n, device=dev, dtype=dec.dtype)
-                                          for n in (3 * hl_hd, h, f_l, h))
-        mid = rnd(b, f_l)
-        res = x if dec.context.tp_size == 1 else None
-        fns += [lambda L=L, o=qkv_out: L.qkv(x, o),
-                lambda L=L, o=o_out, r=res: L.o(attn, o, residual=r),
-                lambda L=L, o=up_out: L.up(x, o, act=_native.ACT_GELU_TANH),
-                lambda L=L, o=dn_out, m=mid, r=res: L.down(m, o, residual=r)]
-        for w, n_in, n_out, r in ((L.wqkv, h, 3 * hl_hd, 0), (L.wo, hl_hd, h, res is not None),
-                                  (L.wup, h, f_l, 0), (L.wdown, f_l, h, res is not None)):
-            gbytes += (w.numel() + b * n_in + b * n_out * (2 if r else 1)) * es
-    if dec.is_last:
-        head_out = torch.empty(b, dec.config.vocab_size, device=dev, dtype=dec.dtype)
-        fns.append(lambda: dec.head_gemm(x, head_out))
-        gbytes += (dec.head.numel() + b * h + b * dec.config.vocab_size) * es
+    scratch_pos = min(ctx_len, dec.config.max_seq_len - 1)  # KV rows written past the timed context
+    for b in lanes:
+        x, attn = rnd(b, h), rnd(b, hl_hd)
+        slots = torch.arange(b, dtype=torch.int32, device=dev)
+        starts = torch.full((b,), scratch_pos, dtype=torch.int32, device=dev)
+        for L, lid in zip(dec.layers, dec.owned_layer_ids):
+            f_l = L.wup.shape[0]
+            q_out, o_out, up_out, dn_out = (torch.empty(b, n, device=dev, dtype=dec.dtype)
+                                            for n in (hl_hd, h, f_l, h))
+            mid = rnd(b, f_l)
+            res = x if tp1 else None
+            kp, vp = dec.cache.k_pool[lid], dec.cache.v_pool[lid]
+            (qlin, qs, qb), (ulin, us_, ub) = L.qkv_ln, L.up_ln
+            fns += [lambda q=qlin, o=q_out, ws=qs, wb=qb, kp=kp, vp=vp, sl=slots, st=starts:
+                    q.fused(x, o, ln_fold=(ws, wb, 1e-5), kv=(kp, vp, sl, st, hl_hd, 1)),
+                    lambda L=L, o=o_out, r=res: L.o(attn, o, residual=r),
+                    lambda u=ulin, o=up_out, ws=us_, wb=ub: u.fused(x, o, act=_native.ACT_GELU_TANH,
+                                                                     ln_fold=(ws, wb, 1e-5)),
+                    lambda L=L, o=dn_out, m=mid, r=res: L.down(m, o, residual=r)]
+            for w, n_in, n_out, r in ((L.wqkv, h, 3 * hl_hd, 0), (L.wo, hl_hd, h, res is not None),
+                                      (L.wup, h, f_l, 0), (L.wdown, f_l, h, res is not None)):
+                gbytes += (w.numel() + b * n_in + b * n_out * (2 if r else 1)) * es
+        if dec.is_last:
+            head_out = torch.empty(b, dec.config.vocab_size, device=dev, dtype=dec.dtype)
+            fns.append(lambda x=x, o=head_out: dec.head_gemm(x, o))
+            gbytes += (dec.head.numel() + b * h + b * dec.config.vocab_size) * es
     g_us = _graph_time_us(fns)
     n_g = len(fns)
 
     # ---- attention family: one launch per layer at the step's context
     hl, hd = dec.num_heads_local, dec.head_dim
-    q = rnd(b, 1, hl, hd)
-    slots = torch.arange(b, dtype=torch.int32, device=dev)
-    starts = torch.full((b,), ctx_len - 1, dtype=torch.int32, device=dev)
-    aout = torch.empty(b, 1, hl * hd, device=dev, dtype=dec.dtype)
-    afns = [lambda lid=lid: ops.attention(q, dec.cache.k_pool[lid], dec.cache.v_pool[lid], slots, starts, aout)
-            for lid in dec.owned_layer_ids]
+    afns, abytes, row0 = [], 0, 0
+    for b in lanes:
+        q = rnd(b, 1, hl, hd)
+        slots = torch.arange(row0, row0 + b, dtype=torch.int32, device=dev)
+        starts = torch.full((b,), ctx_len - 1, dtype=torch.int32, device=dev)
+        aout = torch.empty(b, 1, hl * hd, device=dev, dtype=dec.dtype)
+        afns += [lambda lid=lid, q=q, sl=slots, st=starts, o=aout:
+                 ops.attention(q, dec.cache.k_pool[lid], dec.cache.v_pool[lid], sl, st, o)
+                 for lid in dec.owned_layer_ids]
+        abytes += len(dec.owned_layer_ids) * b * hl * (2 * ctx_len * hd + 2 * hd) * es
+        row0 += b
     a_us = _graph_time_us(afns)
-    abytes = len(afns) * b * hl * (2 * ctx_len * hd + 2 * hd) * es
 
     pk_ = _peaks()
     peak = pk_["hbm_gbs"]
@@ -467,10 +516,19 @@ def kernel_rooflines(engine, dev, ctx_len: int, ms_per_step: float) -> dict:
     att = entry("neb_attn_bulk_kernel (decode attention over the KV pool)", a_us, abytes, len(afns), "attention",
                 context=ctx_len)
     step_bytes = gbytes + abytes
+    fam_us = g_us + a_us + (ar_family["us_per_step"] if ar_family else 0.0)
+    budget = {"step_us": ms_per_step * 1e3, "gemm_us": g_us, "attention_us": a_us,
+              "all_reduce_us": ar_family["us_per_step"] if ar_family else 0.0,
+              "rest_us": ms_per_step * 1e3 - fam_us, "lanes": len(lanes),
+              "note": "families replayed one after another; a two-lane step overlaps them" if len(lanes) > 1
+              else "families replayed one after another"}
     step = {"bound": "hbm", "bytes_per_step": step_bytes, "achieved": step_bytes / (ms_per_step * 1e-3) / 1e9,
             "peak": peak, "unit": "GB/s", "frac": step_bytes / (ms_per_step * 1e-3) / 1e9 / peak}
     dominant, other = (gemm, att) if g_us >= a_us else (att, gemm)
-    return {"roofline": dominant, "roofline_other": other, "roofline_step": step}
+    out = {"roofline": dominant, "roofline_other": other, "roofline_step": step, "budget": budget}
+    if ar_family:
+        out["roofline_all_reduce"] = ar_family
+    return out
 
 
 def full_normal_weights(cfg, dev, dtype) -> dict:
@@ -652,6 +710,10 @@ def run_native(args) -> None:
         dec.cache.release(ids)
         torch.cuda.synchronize(dev)
 
+    # ---- TP all-reduce family, every rank at once (before the leader drives e2e)
+    with torch.inference_mode():
+        ar_family = all_reduce_family_us(dec, dev, world)
+
     # ---- end-to-end through the public Engine API (host tokens in, ids out) ----
     # Rank 0 drives the engine (it broadcasts the reference command protocol);
     # the other ranks serve until the leader's STOP at engine.close().
@@ -688,7 +750,7 @@ def run_native(args) -> None:
     extra = {}
     if rank == 0:
         with torch.inference_mode():
-            extra.update(kernel_rooflines(engine, dev, PROMPT + W + K, ms / K))
+            extra.update(kernel_rooflines(engine, dev, PROMPT + W + K, ms / K, ar_family))
         if world == 1 and not args.no_gemm:
             extra["gemm"] = gemm_headline(dev)
             extra["forgeml"] = forgeml_cases(dev)
@@ -807,6 +869,9 @@ def run_case(args) -> None:
                  engine's path): QKV 6144x2048, o 2048x2048 (+residual),
                  up 8192x2048 (+tanh GELU), down 2048x8192 (+residual),
                  lm_head 32000x2048; chains replayed from a CUDA graph
+    gemm-fused   the decode step's fused launches at batch 32 for the TP
+                 shard of --tp ranks: LayerNorm-folded QKV + KV append, o,
+                 folded up + tanh GELU, down (residuals at TP1)
     gemm         8192^3 bf16 + bias + GELU
     """
     from forgeml_b200.forgeml import kernels
@@ -846,6 +911,56 @@ def run_case(args) -> None:
             algo = (n * k + m * k + m * n * (2 if resid else 1)) * 2
             res[name] = {"us": us, "GB/s": algo / (us * 1e-6) / 1e9, "algo_bytes": algo}
             del ws
+    elif args.case == "gemm-fused":
+        # the decode step's fused launches at batch 32 for one TP shard
+        # (--tp): LayerNorm-folded QKV + KV append, o (+ residual), folded up
+        # + tanh GELU, down (+ residual); enough layers' weights that the
+        # replayed chain streams more than L2 from HBM
+        from forgeml_b200.linear import PackedLinear, ln_fold_vectors
+
+        tp = args.tp
+        m, hdim, hd = BATCH, C4["hidden_size"], 128
+        hl_hd, f_l = hdim // tp, C4["intermediate_size"] // tp
+        heads = hl_hd // hd
+        bf = torch.bfloat16
+        layer_bytes = (3 * hl_hd * hdim + hdim * hl_hd + 2 * f_l * hdim) * 2
+        n_layers = max(2, int(400e6 // layer_bytes) + 1)
+        ones, zeros = torch.ones(hdim, device=dev, dtype=bf), torch.zeros(hdim, device=dev, dtype=bf)
+        kp = torch.zeros(m, heads, 64, hd, device=dev, dtype=bf)
+        vp = torch.zeros_like(kp)
+        slots = torch.arange(m, dtype=torch.int32, device=dev)
+        starts = torch.full((m,), 7, dtype=torch.int32, device=dev)
+        x = torch.randn(m, hdim, device=dev, generator=g).to(bf)
+        attn = torch.randn(m, hl_hd, device=dev, generator=g).to(bf)
+        mid = torch.randn(m, f_l, device=dev, generator=g).to(bf)
+        q_out, o_out = torch.empty(m, hl_hd, device=dev, dtype=bf), torch.empty(m, hdim, device=dev, dtype=bf)
+        up_out, dn_out = torch.empty(m, f_l, device=dev, dtype=bf), torch.empty(m, hdim, device=dev, dtype=bf)
+        fns = {"qkv_ln_kv": [], "o": [], "up_ln_gelu": [], "down": []}
+        for _ in range(n_layers):
+            wq = (torch.randn(3 * hl_hd, hdim, device=dev, generator=g) * 0.02).to(bf)
+            wu = (torch.randn(f_l, hdim, device=dev, generator=g) * 0.02).to(bf)
+            wo = PackedLinear((torch.randn(hdim, hl_hd, device=dev, generator=g) * 0.02).to(bf))
+            wd = PackedLinear((torch.randn(hdim, f_l, device=dev, generator=g) * 0.02).to(bf))
+            (wqp, qs, qb), (wup, us_, ub) = ln_fold_vectors(wq, ones, zeros), ln_fold_vectors(wu, ones, zeros)
+            ql, ul = PackedLinear(wqp), PackedLinear(wup)
+            r = x if tp == 1 else None
+            fns["qkv_ln_kv"].append(lambda ql=ql, qs=qs, qb=qb: ql.fused(x, q_out, ln_fold=(qs, qb, 1e-5),
+                                                                          kv=(kp, vp, slots, starts, hl_hd, 1)))
+            fns["o"].append(lambda wo=wo, r=r: wo(attn, o_out, residual=r))
+            fns["up_ln_gelu"].append(lambda ul=ul, us_=us_, ub=ub: ul.fused(x, up_out, act=2,
+                                                                             ln_fold=(us_, ub, 1e-5)))
+            fns["down"].append(lambda wd=wd, r=r: wd(mid, dn_out, residual=r))
+        resid = 1 if tp == 1 else 0
+        algo = {"qkv_ln_kv": (3 * hl_hd * hdim + m * hdim + m * 3 * hl_hd) * 2,
+                "o": (hdim * hl_hd + m * hl_hd + m * hdim * (1 + resid)) * 2,
+                "up_ln_gelu": (f_l * hdim + m * hdim + m * f_l) * 2,
+                "down": (hdim * f_l + m * f_l + m * hdim * (1 + resid)) * 2}
+        chain = [f for i in range(n_layers) for k in fns for f in (fns[k][i],)]
+        us_chain = _graph_time_us(chain * max(1, reps // n_layers)) / (len(chain) * max(1, reps // n_layers))
+        for k, lst in fns.items():
+            us = _graph_time_us(lst * max(1, reps // n_layers)) / (len(lst) * max(1, reps // n_layers))
+            res[k] = {"us": us, "GB/s": algo[k] / (us * 1e-6) / 1e9, "algo_bytes": algo[k], "tp_shard": tp}
+        res["chain_avg_us"] = us_chain
     elif args.case == "gemm":
         res["gemm"] = gemm_headline(dev)
     print(json.dumps({"case": args.case, "results": res}), flush=True)
@@ -862,7 +977,8 @@ def main() -> None:
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the decode before timing")
     ap.add_argument("--cpu-steps", type=int, default=3)
     ap.add_argument("--cpu-layers", type=int, default=None, help="time this many layers of the CPU oracle")
-    ap.add_argument("--case", choices=("attention", "gemm-decode", "gemm"), default=None,
+    ap.add_argument("--tp", type=int, default=1, help="--case gemm-fused: TP shard shapes of this degree")
+    ap.add_argument("--case", choices=("attention", "gemm-decode", "gemm-fused", "gemm"), default=None,
                     help="run one kernel micro-benchmark instead of the decode bench")
     ap.add_argument("--workload", choices=("c4", "c5"), default="c4",
                     help="c5: serve config 5 through the AsyncBatcher over TP x PP (launch with torchrun)")
