@@ -1760,6 +1760,81 @@ static int validate_gemm(const void* a, const void* b, void* c, long long m, lon
   return FML_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Plan cache of fml_gemm.  A plan (tile shape, split, residency, packing) and
+// the two tensor maps depend only on the operands' addresses, layouts, the
+// problem shape, dtype, tile hint, device and workspace address -- all in
+// the key -- so a repeated call reuses them.  64 entries, replaced round
+// robin; a tensor map is a function of its key, so an entry never goes stale.
+// ---------------------------------------------------------------------------
+struct PlanKey {
+  const void* a;
+  const void* b;
+  const void* ws;
+  long long v[7];  // lda_m, lda_k, ldb_k, ldb_n, m, n, k
+  int dtype, dev;
+  int cfg[5];      // -1 when no tile hint
+  bool operator==(const PlanKey& o) const {
+    if (a != o.a || b != o.b || ws != o.ws || dtype != o.dtype || dev != o.dev) return false;
+    for (int i = 0; i < 7; ++i)
+      if (v[i] != o.v[i]) return false;
+    for (int i = 0; i < 5; ++i)
+      if (cfg[i] != o.cfg[i]) return false;
+    return true;
+  }
+};
+
+struct CachedPlan {
+  alignas(64) CUtensorMap mp;
+  alignas(64) CUtensorMap mq;
+  PlanKey key;
+  Plan pl;
+  bool used = false;
+};
+
+static PlanKey plan_key(const void* a, long long lda_m, long long lda_k, const void* b, long long ldb_k,
+                        long long ldb_n, long long m, long long n, long long k, int dtype, const fml_tile_cfg* cfg,
+                        int dev, const void* ws) {
+  PlanKey key;
+  key.a = a;
+  key.b = b;
+  key.ws = ws;
+  const long long v[7] = {lda_m, lda_k, ldb_k, ldb_n, m, n, k};
+  for (int i = 0; i < 7; ++i) key.v[i] = v[i];
+  key.dtype = dtype;
+  key.dev = dev;
+  const int c[5] = {cfg ? cfg->block_m : -1, cfg ? cfg->block_n : -1, cfg ? cfg->block_k : -1,
+                    cfg ? cfg->num_warps : -1, cfg ? cfg->num_stages : -1};
+  for (int i = 0; i < 5; ++i) key.cfg[i] = c[i];
+  return key;
+}
+
+constexpr int kPlanCacheSize = 64;
+static std::mutex g_plan_mu;
+static CachedPlan g_plans[kPlanCacheSize];
+static int g_plan_next = 0;
+
+static bool plan_cache_get(const PlanKey& key, CachedPlan& out) {
+  std::lock_guard<std::mutex> lock(g_plan_mu);
+  for (int i = 0; i < kPlanCacheSize; ++i)
+    if (g_plans[i].used && g_plans[i].key == key) {
+      out = g_plans[i];
+      return true;
+    }
+  return false;
+}
+
+static void plan_cache_put(const PlanKey& key, const Plan& pl, const CUtensorMap& mp, const CUtensorMap& mq) {
+  std::lock_guard<std::mutex> lock(g_plan_mu);
+  CachedPlan& e = g_plans[g_plan_next];
+  g_plan_next = (g_plan_next + 1) % kPlanCacheSize;
+  e.key = key;
+  e.pl = pl;
+  e.mp = mp;
+  e.mq = mq;
+  e.used = true;
+}
+
 extern "C" size_t fml_gemm_workspace_size(int64_t m, int64_t n, int64_t k, int dtype,
                                           int64_t lda_m, int64_t lda_k, int64_t ldb_k,
                                           int64_t ldb_n, const void* a, const void* b,
@@ -1789,7 +1864,20 @@ extern "C" int fml_gemm(const void* a, int64_t lda_m, int64_t lda_k, const void*
       return fail(FML_EINVAL, "gemm: tile config out of range");
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const int sms = num_sms(current_device());
+  const int dev = current_device();
+  const int sms = num_sms(dev);
+  const PlanKey key = plan_key(a, lda_m, lda_k, b, ldb_k, ldb_n, m, n, k, dtype, cfg, dev, workspace);
+  CachedPlan hit;
+  if (plan_cache_get(key, hit)) {
+    // A repeated call (same operands, layout and workspace): the plan and
+    // both tensor maps are the ones built before; only the packing kernels
+    // (operand contents may have changed) and the launch run again.
+    const bool tf32 = dtype == FML_F32;
+    if (hit.pl.P.pack && (rc = pack_operand(hit.pl.P, dtype, tf32 ? 1 : 0, workspace, st))) return rc;
+    if (hit.pl.Q.pack && (rc = pack_operand(hit.pl.Q, dtype, tf32 ? 2 : 0, workspace, st))) return rc;
+    return launch_plan(hit.pl, hit.mp, hit.mq, dtype, act, bias, bias_stride, residual, ldr, c, ldc, m, n, nullptr,
+                       sms, st);
+  }
   Plan pl;
   rc = make_plan(pl, a, lda_m, lda_k, b, ldb_k, ldb_n, m, n, k, dtype, cfg, sms);
   if (rc) return rc;
@@ -1824,6 +1912,7 @@ extern "C" int fml_gemm(const void* a, int64_t lda_m, int64_t lda_k, const void*
     }
     if (rc) return rc;
   }
+  plan_cache_put(key, pl, mp, mq);
   return launch_plan(pl, mp, mq, dtype, act, bias, bias_stride, residual, ldr, c, ldc, m, n, nullptr, sms, st);
 }
 

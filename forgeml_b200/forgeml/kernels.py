@@ -62,8 +62,15 @@ _GEMM_OPS = ("matmul", "linear", "fused_linear_gelu")
 _NATIVE_OPS = _GEMM_OPS + ("layer_norm", "sdpa")
 
 
+_SM100: dict = {}
+
+
 def _sm100(device: torch.device | int | None = None) -> bool:
-    return torch.cuda.get_device_capability(device) == (10, 0)
+    key = device.index if isinstance(device, torch.device) else device
+    hit = _SM100.get(key)
+    if hit is None:
+        hit = _SM100[key] = torch.cuda.get_device_capability(device) == (10, 0)
+    return hit
 
 
 def available() -> bool:
@@ -103,6 +110,17 @@ def _require_native(device: torch.device) -> None:
         raise GraphError(f"native library unavailable: {e}") from e
 
 
+class _NoContext:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+_NO_CONTEXT = _NoContext()
+
+
 def _workspace(nbytes: int, device: torch.device) -> tuple[torch.Tensor | None, int, int]:
     if nbytes <= 0:
         return None, 0, 0
@@ -110,6 +128,9 @@ def _workspace(nbytes: int, device: torch.device) -> tuple[torch.Tensor | None, 
     base = ws.data_ptr()
     aligned = (base + 255) // 256 * 256
     return ws, aligned, nbytes
+
+
+_FML_EWORKSPACE = 4
 
 
 def _launch_gemm(a, b, bias, out, act: int, config: KernelConfig, residual=None) -> None:
@@ -122,21 +143,24 @@ def _launch_gemm(a, b, bias, out, act: int, config: KernelConfig, residual=None)
         cfg = ctypes.byref(
             _native.fml_tile_cfg(config.block_m, config.block_n, config.block_k, config.num_warps, config.num_stages)
         )
+    args = (a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(), b.stride(0), b.stride(1),
+            bias.data_ptr() if bias is not None else None, bias.stride(0) if bias is not None else 0,
+            residual.data_ptr() if residual is not None else None, residual.stride(0) if residual is not None else 0,
+            out.data_ptr(), out.stride(0), m, n, k, code, act, cfg)
+    stream = torch.cuda.current_stream(a.device).cuda_stream
+    # 16-bit operands TMA can address need no workspace: try that first (one
+    # native call); fp32 (3xTF32 split) and unaddressable layouts ask for it.
+    if a.dtype != torch.float32:
+        rc = lib.fml_gemm(*args, None, 0, stream)
+        if rc == 0:
+            return
+        if rc != _FML_EWORKSPACE:
+            raise _native.NativeError("fml_gemm", int(rc), lib.fml_last_error().decode(errors="replace"))
     ws_bytes = lib.fml_gemm_workspace_size(
         m, n, k, code, a.stride(0), a.stride(1), b.stride(0), b.stride(1), a.data_ptr(), b.data_ptr(), cfg
     )
     ws, ws_ptr, ws_n = _workspace(int(ws_bytes), a.device)
-    _native.call(
-        "fml_gemm",
-        a.data_ptr(), a.stride(0), a.stride(1),
-        b.data_ptr(), b.stride(0), b.stride(1),
-        bias.data_ptr() if bias is not None else None, bias.stride(0) if bias is not None else 0,
-        residual.data_ptr() if residual is not None else None,
-        residual.stride(0) if residual is not None else 0,
-        out.data_ptr(), out.stride(0),
-        m, n, k, code, act, cfg,
-        ws_ptr or None, ws_n, _native.stream_ptr(a.device),
-    )
+    _native.call("fml_gemm", *args, ws_ptr or None, ws_n, stream)
     del ws  # the caching allocator keeps it alive until the stream is done with it
 
 
@@ -240,7 +264,8 @@ def matmul(
         or residual.stride(1) != 1
     ):
         raise GraphError("residual must be a row-major (M, N) tensor matching dtype/device")
-    _check_config(config)
+    if config is not DEFAULT_CONFIG:
+        _check_config(config)
     _require_native(a.device)
     if out is None:
         out = torch.empty((m, n), dtype=a.dtype, device=a.device)
@@ -260,7 +285,8 @@ def matmul(
     act = _native.ACT_NONE
     if activation == "gelu":
         act = _native.ACT_GELU_TANH if approximate == "tanh" else _native.ACT_GELU_ERF
-    with torch.cuda.device(a.device):
+    ctx = torch.cuda.device(a.device) if torch.cuda.current_device() != a.device.index else _NO_CONTEXT
+    with ctx:
         try:
             _launch_gemm(a, b, bias, out, act, config, residual)
         except _native.NativeError as e:
