@@ -310,7 +310,9 @@ def forgeml_cases(dev) -> dict:
             c = fml_compile(m, (x.to(dev),), backend="triton")
             xd = x.to(dev)
             ms = timed_ms(lambda: c(xd), 10)
-            out[name] = {"ms_per_call": ms, "gflop": 64.42, "tflops": 64.42e9 / (ms * 1e-3) / 1e12}
+            out[name] = {"ms_per_call": ms, "gflop": 64.42, "tflops": 64.42e9 / (ms * 1e-3) / 1e12,
+                         "node_ms": {k: round(v, 4) for k, v in c.node_times(xd).items()},
+                         "native_fusions": c.fusions}
         sweep = {}
         for dt, dn in ((torch.bfloat16, "bf16"), (torch.float32, "fp32")):
             for sz in (256, 1024, 4096, 8192):

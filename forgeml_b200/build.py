@@ -23,7 +23,7 @@ CSRC = PKG / "csrc"
 OUT_DIR = PKG / "_lib"
 OBJ_DIR = OUT_DIR / "obj"
 LIB_NAME = "libforgeml_b200.so"
-SOURCES = ["common.cu", "gemm.cu", "layernorm.cu", "attention.cu", "nebula_ops.cu", "allreduce.cu"]
+SOURCES = ["common.cu", "gemm.cu", "layernorm.cu", "attention.cu", "sdpa_tc.cu", "nebula_ops.cu", "allreduce.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -707,6 +707,13 @@ static int launch_sdpa(const SdpaParams& p, cudaStream_t st) {
 
 using namespace fml;
 
+namespace fml {
+int sdpa_tensor_core(const void* q, const int64_t qs[4], const void* k, const int64_t ks[4], const void* v,
+                     const int64_t vs[4], int mask_kind, int is_causal, float scale, void* out,
+                     const int64_t os[4], int64_t B, int64_t H, int64_t Sq, int64_t Sk, int64_t D, int dtype,
+                     cudaStream_t st);
+}
+
 extern "C" int neb_attention(const void* q, const int64_t q_strides[4], const void* k_pool,
                              const void* v_pool, const int32_t* slot_of, const int32_t* start_pos,
                              void* out, int64_t batch, int64_t t, int64_t heads, int64_t head_dim,
@@ -768,6 +775,11 @@ extern "C" int fml_sdpa(const void* q, const int64_t q_strides[4], const void* k
   p.B = (int)batch; p.H = (int)heads; p.Sq = (int)sq; p.Sk = (int)sk; p.D = (int)d;
   p.mask_kind = mask_kind; p.causal = is_causal ? 1 : 0; p.scale = scale;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // 16-bit attention without an explicit mask runs on the tensor cores
+  // (sdpa_tc.cu); fp32 keeps the exact CUDA-core recurrence below.
+  const int rc = sdpa_tensor_core(q, q_strides, k, k_strides, v, v_strides, mask_kind, is_causal, scale, out,
+                                  out_strides, batch, heads, sq, sk, d, dtype, st);
+  if (rc != FML_EUNSUPPORTED) return rc;
   if (dtype == FML_F32) return attn::launch_sdpa<float>(p, st);
   if (dtype == FML_BF16) return attn::launch_sdpa<__nv_bfloat16>(p, st);
   return attn::launch_sdpa<__half>(p, st);

@@ -253,6 +253,7 @@ class CompiledModel:
                                       if has_slot else None)
             drops = tuple(ids[i] for i in set(e.inputs) if last_reader.get(i) == k and i not in keep)
             instrs.append((_fail_wrap(node, fn), tuple(ids[i] for i in e.inputs), ids[e.name], drops))
+        self._instr_names = [f"{e.name} ({e.op})" for e in entries]
         produced = {e.name for e in entries}
         outputs = [(ids[o], o not in produced) for o in g.outputs]
         self._program = _Program(len(ids), [ids[n] for n in g.inputs],
@@ -375,6 +376,32 @@ class CompiledModel:
 
     def kernel_source(self) -> str:
         return kernels.kernel_source()
+
+    def node_times(self, *inputs: torch.Tensor, repeats: int = 5) -> dict[str, float]:
+        """Device milliseconds of each instruction of the program (median of
+        ``repeats`` runs; CUDA events between instructions on the current
+        stream).  A fused residual add reports under the add's name."""
+        self(*inputs)
+        prog = self._program
+        names = list(self._instr_names)
+        samples: dict[str, list[float]] = {n: [] for n in names}
+        stream = torch.cuda.current_stream()
+        with torch.inference_mode():
+            for _ in range(repeats):
+                vals: list = [None] * prog.n_values
+                for vid, t in zip(prog.inputs, inputs):
+                    vals[vid] = t
+                for vid, t in prog.constants:
+                    vals[vid] = t
+                events = [torch.cuda.Event(enable_timing=True) for _ in range(len(prog.instrs) + 1)]
+                events[0].record(stream)
+                for k, (fn, arg_ids, out_id, _) in enumerate(prog.instrs):
+                    vals[out_id] = fn(*[vals[i] for i in arg_ids])
+                    events[k + 1].record(stream)
+                events[-1].synchronize()
+                for k, n in enumerate(names):
+                    samples[n].append(events[k].elapsed_time(events[k + 1]))
+        return {n: sorted(v)[len(v) // 2] for n, v in samples.items()}
 
     def explain(self) -> dict:
         return {

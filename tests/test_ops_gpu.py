@@ -72,6 +72,25 @@ def test_sdpa(cuda, dtype, b, s, h, d, mode):
     close(got, want, dtype)
 
 
+@pytest.mark.parametrize("dtype,b,s,h,d,causal", [
+    (torch.bfloat16, 2, 512, 12, 64, False),   # config 2 shape (two batch elements)
+    (torch.bfloat16, 1, 512, 12, 64, True),
+    (torch.float16, 2, 300, 4, 128, True),     # Nebula prefill head size, partial key block
+    (torch.bfloat16, 1, 129, 2, 128, False),   # one position past a 128-block
+])
+def test_sdpa_tensor_core_path(cuda, dtype, b, s, h, d, causal):
+    """16-bit attention without an explicit mask runs on the tcgen05 kernel
+    (sdpa_tc.cu); checked against the oracle at the dtype's tolerance."""
+    (q, k, v), (qc, kc, vc) = _qkv_views(b, s, h, d, dtype, cuda, seed=3 * s + d)
+    got = kernels.sdpa(q, k, v, is_causal=causal)
+    want = sdpa_ref(qc, kc, vc, is_causal=causal)
+    close(got, want, dtype)
+    # written through strides into a [B, S, H, D] buffer (the compiled block's layout)
+    buf = torch.empty(b, s, h, d, dtype=dtype, device=cuda)
+    kernels.sdpa(q, k, v, is_causal=causal, out=buf.transpose(1, 2))
+    close(buf.transpose(1, 2), want, dtype)
+
+
 def test_sdpa_matches_torch_cpu_c2_slice(cuda):
     """c2 shapes (head_dim 64, 12 heads) on one batch element vs torch's own CPU SDPA."""
     (q, k, v), (qc, kc, vc) = _qkv_views(1, 512, 12, 64, torch.float32, cuda, seed=1)
