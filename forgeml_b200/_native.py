@@ -117,6 +117,7 @@ _SIGNATURES = {
     "neb_ar_open": (_I, [_P, _P]),
     "neb_ar_set_peers": (_I, [_P, ctypes.POINTER(ctypes.c_void_p)]),
     "neb_ar_buffer": (_P, [_P]),
+    "neb_ar_set_protocol": (_I, [_P, _I]),
     "neb_ar_all_reduce": (_I, [_P, _P, _P, _P, _I64, _I, _P]),
     "neb_ar_destroy": (_I, [_P]),
     "neb_linear_fused": (

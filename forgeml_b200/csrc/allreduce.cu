@@ -7,26 +7,22 @@
 // over the TP group) followed by the `x = x + part` of
 // src/nebula/runtime.py:146,154, each rounded to the model dtype.
 //
-// One-shot push design for the small messages of a decode step (B x T x d,
-// 128 KB at config 4): every rank owns a symmetric buffer, opened by its
-// peers through CUDA IPC.  CTA b of rank r writes chunk b of its partial into
-// slot r of every rank's buffer (NVLink stores), fences, and raises flag
-// [r][b] on every peer with the launch's epoch; then it waits until every
-// peer's flag [q][b] carries the same epoch, and sums the world slots of its
-// chunk in rank order, so all ranks produce bit-identical results.
+// Every rank owns a symmetric buffer (peer_layout.cuh), opened by its peers
+// through CUDA IPC.  Two low-latency (LL) protocols move the message: each
+// 4-byte word travels with the call's epoch in one 8-byte store, so a reader
+// polls the words themselves (no fence, no flag round trip):
+//   one-shot  every rank pushes its whole partial to every peer and sums all
+//             ranks' words locally (one NVLink hop, (W-1) copies out);
+//   two-shot  reduce-scatter to sub-shard owners, then all-gather of the
+//             finished words (two hops, 2 (W-1)/W of the message out).
+// Both sum the ranks in rank order in fp32, so all ranks hold bit-identical
+// results.  Epochs live in the buffer (one counter per CTA index, advanced by
+// the CTA itself), so a launch recorded in a CUDA graph stays correct on
+// replay.  Every wait is bounded (the context's timeout); on expiry the
+// kernel raises DEV_ERR_AR_TIMEOUT in the device error word and finishes.
 //
-// Epochs live in the buffer (one counter per CTA index, advanced by the CTA
-// itself), so a launch recorded in a CUDA graph stays correct on replay.  Two
-// buffer sets alternate by epoch parity: CTA b of rank r writes set e&1 of a
-// peer only after it has seen that peer's epoch e-1 flag for chunk b, which the
-// peer raised after it finished reading set e&1 in epoch e-2.  The grid size
-// is fixed, so CTA b always owns the same chunk of every message.
-//
-// Every wait is bounded (the context's timeout); on expiry the kernel raises
-// DEV_ERR_AR_TIMEOUT in the device error word and finishes without hanging.
-//
-// The same buffer carries a second region for the all-reduce fused into the
-// decode GEMM's epilogue (gemm.cu); its layout is in peer_layout.cuh.
+// The buffer also carries the exchange region of the all-reduce fused into
+// the decode GEMM's epilogue (gemm.cu).
 #include <cstdlib>
 #include <cstring>
 #include <string>
@@ -40,8 +36,6 @@ namespace ar {
 
 using peer::Ctx;
 using peer::kMaxWorld;
-using peer::ld_acquire_sys;
-using peer::st_release_sys;
 constexpr int kBlocks = peer::kArBlocks;  // fixed grid (one chunk per CTA index, every call)
 constexpr int kThreads = 256;
 using Args = peer::View;
@@ -51,79 +45,6 @@ __device__ __forceinline__ void add_vec(float (&acc)[16 / sizeof(T)], const uint
   const T* e = reinterpret_cast<const T*>(&raw);
 #pragma unroll
   for (int i = 0; i < (int)(16 / sizeof(T)); ++i) acc[i] += to_f32<T>(e[i]);
-}
-
-template <typename T>
-__global__ void __launch_bounds__(kThreads) ar_kernel(const Args a, const T* __restrict__ part,
-                                                      const T* __restrict__ residual, T* __restrict__ out,
-                                                      long long nvec) {
-  constexpr int VE = 16 / sizeof(T);
-  pdl_wait();
-  pdl_trigger();
-  const int blk = blockIdx.x, tid = threadIdx.x;
-  const int W = a.lay.world, r = a.rank;
-  uint32_t* epochs = reinterpret_cast<uint32_t*>(a.base[r] + a.lay.epoch_off(0, 0));
-  __shared__ uint32_t s_epoch;
-  __shared__ int s_ok;
-  if (tid == 0) {
-    s_epoch = epochs[blk] + 1u;
-    s_ok = 1;
-  }
-  __syncthreads();
-  const uint32_t e = s_epoch;
-  const int set = (int)(e & 1u);
-  const long long per = (nvec + kBlocks - 1) / kBlocks;
-  const long long v0 = (long long)blk * per, v1 = min(nvec, v0 + per);
-  const uint4* src = reinterpret_cast<const uint4*>(part);
-
-  // 1. push this chunk of the partial into slot r of every rank
-  for (long long i = v0 + tid; i < v1; i += kThreads) {
-    const uint4 v = src[i];
-    for (int q = 0; q < W; ++q)
-      reinterpret_cast<uint4*>(a.base[q] + a.lay.data_off(0, set, r))[i] = v;
-  }
-  __threadfence_system();
-  __syncthreads();
-  // 2. raise flag [r][blk] on every peer
-  if (tid < W && tid != r)
-    st_release_sys(reinterpret_cast<uint32_t*>(a.base[tid] + a.lay.flag_off(0, set, r, blk)), e);
-  // 3. wait for every peer's flag [q][blk] (bounded)
-  if (tid < W && tid != r) {
-    const uint32_t* f = reinterpret_cast<const uint32_t*>(a.base[r] + a.lay.flag_off(0, set, tid, blk));
-    const long long t0 = clock64();
-    while (ld_acquire_sys(f) != e) {
-      if (clock64() - t0 > a.timeout_cycles) {
-        raise_device_error(DEV_ERR_AR_TIMEOUT);
-        s_ok = 0;
-        break;
-      }
-    }
-  }
-  __syncthreads();
-  // 4. sum the world slots of this chunk in rank order, add the residual
-  for (long long i = v0 + tid; i < v1; i += kThreads) {
-    float acc[VE];
-#pragma unroll
-    for (int k = 0; k < VE; ++k) acc[k] = 0.f;
-    for (int q = 0; q < W; ++q) add_vec<T>(acc, reinterpret_cast<const uint4*>(a.base[r] + a.lay.data_off(0, set, q))[i]);
-    float res[VE];
-    if (residual != nullptr) {
-      const uint4 rv = reinterpret_cast<const uint4*>(residual)[i];
-      const T* re = reinterpret_cast<const T*>(&rv);
-#pragma unroll
-      for (int k = 0; k < VE; ++k) res[k] = to_f32<T>(re[k]);
-    }
-    uint4 o;
-    T* oe = reinterpret_cast<T*>(&o);
-#pragma unroll
-    for (int k = 0; k < VE; ++k) {
-      float x = to_f32<T>(from_f32<T>(acc[k]));      // the all-reduced partial in the model dtype
-      if (residual != nullptr) x = x + res[k];       // x + part, rounded once more below
-      oe[k] = from_f32<T>(x);
-    }
-    reinterpret_cast<uint4*>(out)[i] = o;
-  }
-  if (tid == 0) epochs[blk] = e;
 }
 
 // Low-latency (LL) variant.  Each 4-byte word of a rank's partial travels
@@ -339,14 +260,8 @@ __global__ void __launch_bounds__(kThreads) ar_ts_kernel(const __grid_constant__
   if (tid == 0) epochs[blk] = e;
 }
 
-// Protocol of neb_ar_all_reduce (FORGEML_AR_PROTO): "ll" one-shot LL
-// (default), "ll2" two-shot LL, "flag" stores + system fence + epoch flags.
-static int ar_proto() {
-  const char* v = getenv("FORGEML_AR_PROTO");
-  if (v && std::string(v) == "flag") return 0;
-  if (v && std::string(v) == "ll2") return 2;
-  return 1;
-}
+// Protocol of a call: the context's choice, else the one-shot.
+static int ar_proto(const Ctx* c) { return c->proto != 0 ? c->proto : 1; }
 
 }  // namespace ar
 }  // namespace fml
@@ -368,6 +283,7 @@ int neb_ar_create(int64_t max_bytes, int world, int rank, double timeout_ms, voi
   Ctx* c = new Ctx();
   c->v.lay.slot_bytes = max_bytes;
   c->v.lay.nsub = (int)((max_bytes + 1023) / 1024);
+  c->proto = 0;
   c->v.lay.world = world;
   c->v.rank = rank;
   int clk_khz = 0;
@@ -425,6 +341,14 @@ int neb_ar_set_peers(void* ctx, void* const* bases) {
 
 void* neb_ar_buffer(void* ctx) { return ctx ? static_cast<Ctx*>(ctx)->own : nullptr; }
 
+int neb_ar_set_protocol(void* ctx, int protocol) {
+  Ctx* c = static_cast<Ctx*>(ctx);
+  if (!c) return fail(FML_EINVAL, "neb_ar_set_protocol: null context");
+  if (protocol < 0 || protocol > 2) return fail(FML_EINVAL, "neb_ar_set_protocol: protocol must be 0, 1 or 2");
+  c->proto = protocol;
+  return FML_OK;
+}
+
 int neb_ar_all_reduce(void* ctx, const void* part, const void* residual, void* out, int64_t n, int dtype, void* stream) {
   Ctx* c = static_cast<Ctx*>(ctx);
   if (!c || !part || !out) return fail(FML_EINVAL, "neb_ar_all_reduce: null pointer");
@@ -440,22 +364,19 @@ int neb_ar_all_reduce(void* ctx, const void* part, const void* residual, void* o
   const long long nvec = bytes / 16;
   cudaError_t e;
   const dim3 grid(fml::ar::kBlocks), block(fml::ar::kThreads);
-  const int proto = fml::ar::ar_proto();
+  const bool two_shot = fml::ar::ar_proto(c) == 2;
   if (dtype == FML_F32)
-    e = fml::launch_pdl(proto == 2 ? fml::ar::ar_ts_kernel<float>
-                        : proto == 1 ? fml::ar::ar_ll_kernel<float> : fml::ar::ar_kernel<float>,
-                        grid, block, 0, st, 1, c->v, static_cast<const float*>(part),
-                        static_cast<const float*>(residual), static_cast<float*>(out), nvec);
+    e = fml::launch_pdl(two_shot ? fml::ar::ar_ts_kernel<float> : fml::ar::ar_ll_kernel<float>, grid, block, 0,
+                        st, 1, c->v, static_cast<const float*>(part), static_cast<const float*>(residual),
+                        static_cast<float*>(out), nvec);
   else if (dtype == FML_BF16)
-    e = fml::launch_pdl(proto == 2 ? fml::ar::ar_ts_kernel<__nv_bfloat16>
-                        : proto == 1 ? fml::ar::ar_ll_kernel<__nv_bfloat16> : fml::ar::ar_kernel<__nv_bfloat16>,
+    e = fml::launch_pdl(two_shot ? fml::ar::ar_ts_kernel<__nv_bfloat16> : fml::ar::ar_ll_kernel<__nv_bfloat16>,
                         grid, block, 0, st, 1, c->v, static_cast<const __nv_bfloat16*>(part),
                         static_cast<const __nv_bfloat16*>(residual), static_cast<__nv_bfloat16*>(out), nvec);
   else
-    e = fml::launch_pdl(proto == 2 ? fml::ar::ar_ts_kernel<__half>
-                        : proto == 1 ? fml::ar::ar_ll_kernel<__half> : fml::ar::ar_kernel<__half>,
-                        grid, block, 0, st, 1, c->v, static_cast<const __half*>(part),
-                        static_cast<const __half*>(residual), static_cast<__half*>(out), nvec);
+    e = fml::launch_pdl(two_shot ? fml::ar::ar_ts_kernel<__half> : fml::ar::ar_ll_kernel<__half>, grid, block,
+                        0, st, 1, c->v, static_cast<const __half*>(part), static_cast<const __half*>(residual),
+                        static_cast<__half*>(out), nvec);
   fml::count_launch();
   return fml::check_cuda(e, "neb_ar_all_reduce launch");
 }

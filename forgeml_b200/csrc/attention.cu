@@ -734,9 +734,7 @@ extern "C" int neb_attention(const void* q, const int64_t q_strides[4], const vo
   // launch shape (not on the device-side positions), so a captured decode
   // step keeps a valid split.
   const long long nq = batch * t * heads;
-  const char* tune = getenv("FORGEML_NEB_ATTN_CTAS_PER_SM");  // tuning override
-  const long long target_per_sm = (tune && atoll(tune) > 0) ? atoll(tune) : 2LL;
-  const long long target = target_per_sm * num_sms(current_device());
+  const long long target = 2LL * num_sms(current_device());
   int nsplit = (int)std::min<long long>(8, std::max<long long>(1, target / nq));
   nsplit = (int)std::min<long long>(nsplit, std::max<long long>(1, max_seq / 64));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);

@@ -49,10 +49,7 @@ int num_sms(int device) {
   return cache[device];
 }
 
-bool pdl_enabled() {
-  const char* e = getenv("FORGEML_PDL");
-  return !(e && e[0] == '0');
-}
+bool pdl_enabled() { return true; }
 
 }  // namespace fml
 

@@ -63,8 +63,8 @@ __device__ __forceinline__ void raise_device_error(int code) {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-// Programmatic dependent launch is on unless FORGEML_PDL=0 (a diagnostic
-// switch: every kernel stays correct either way).
+// Programmatic dependent launch is always requested (every kernel is also
+// correct without it).
 bool pdl_enabled();
 
 // Host: launch with programmatic stream serialization (and an optional

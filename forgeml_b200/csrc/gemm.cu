@@ -676,7 +676,7 @@ __device__ bool ar_exchange(const Params& p, const Smem& s, int ti, int r0, int 
   constexpr int kChunks = kSubBytes / 16;
   const uint32_t ep = s.aux + aux_ep(BN);
   const uint32_t stg = s.aux + aux_stage(BN);
-  uint32_t* epochs = reinterpret_cast<uint32_t*>(a.base[rank] + a.lay.epoch_off(1, 0));
+  uint32_t* epochs = reinterpret_cast<uint32_t*>(a.base[rank] + a.lay.ex_epoch_off(0));
   if (tid < nsb) st_shared_u32(ep + 4 * tid, c0 + tid < nsub_valid ? epochs[c0 + tid] + 1u : 0u);
   epi_bar_sync();  // staging block and epochs visible to all epilogue threads
   for (int u = tid; u < nsb * W * kChunks; u += 128) {
@@ -685,7 +685,7 @@ __device__ bool ar_exchange(const Params& p, const Smem& s, int ti, int r0, int 
     if (c0 + sb >= nsub_valid) continue;
     const uint32_t e = ld_shared_u32(ep + 4 * sb);
     const uint4 v = ld_shared_u4(stg + (uint32_t)(sb * kSubBytes + ch * 16));
-    *reinterpret_cast<uint4*>(a.base[q] + a.lay.data_off(1, (int)(e & 1u), rank) + (long long)(c0 + sb) * kSubBytes +
+    *reinterpret_cast<uint4*>(a.base[q] + a.lay.ex_data_off((int)(e & 1u), rank) + (long long)(c0 + sb) * kSubBytes +
                               ch * 16) = v;
   }
   __threadfence_system();
@@ -694,14 +694,14 @@ __device__ bool ar_exchange(const Params& p, const Smem& s, int ti, int r0, int 
     const int sb = u / W, q = u - sb * W;
     if (q == rank || c0 + sb >= nsub_valid) continue;
     const uint32_t e = ld_shared_u32(ep + 4 * sb);
-    peer::st_release_sys(reinterpret_cast<uint32_t*>(a.base[q] + a.lay.flag_off(1, (int)(e & 1u), rank, c0 + sb)), e);
+    peer::st_release_sys(reinterpret_cast<uint32_t*>(a.base[q] + a.lay.ex_flag_off((int)(e & 1u), rank, c0 + sb)), e);
   }
   bool got = true;
   for (int u = tid; u < nsb * W; u += 128) {
     const int sb = u / W, q = u - sb * W;
     if (q == rank || c0 + sb >= nsub_valid) continue;
     const uint32_t e = ld_shared_u32(ep + 4 * sb);
-    const uint32_t* f = reinterpret_cast<const uint32_t*>(a.base[rank] + a.lay.flag_off(1, (int)(e & 1u), q, c0 + sb));
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(a.base[rank] + a.lay.ex_flag_off((int)(e & 1u), q, c0 + sb));
     const long long t0 = clock64();
     while (peer::ld_acquire_sys(f) != e) {
       if (clock64() - t0 > a.timeout_cycles) {
@@ -723,7 +723,7 @@ __device__ bool ar_exchange(const Params& p, const Smem& s, int ti, int r0, int 
     const long long off = (long long)(c0 + sb) * kSubBytes + ((f % peer::kSubFeatures) * peer::kSubTokens + m) * 2;
     float acc = 0.f;
     for (int q = 0; q < W; ++q)
-      acc += h2f(*reinterpret_cast<const uint16_t*>(a.base[rank] + a.lay.data_off(1, (int)(e & 1u), q) + off), bf);
+      acc += h2f(*reinterpret_cast<const uint16_t*>(a.base[rank] + a.lay.ex_data_off((int)(e & 1u), q) + off), bf);
     float x = h2f(f2h(acc, bf), bf);  // the all-reduced partial in the model dtype
     if (res != nullptr) x = x + h2f(res[(long long)m * p.ldr + n], bf);
     out[(long long)m * p.ldo + n] = (uint16_t)f2h(x, bf);
@@ -1507,11 +1507,6 @@ static void choose_split(Plan& pl, long long tiles, long long num_kb, const fml_
     const double cost = rounds * per_cta + (ks > 1 ? 4.0 : 0.0);
     if (cost < best_cost - 1e-9) { best_cost = cost; best_ks = ks; }
   }
-  const char* tune = getenv("FORGEML_GEMM_KSPLIT");  // tuning override: 1, 2, 4 or 8
-  if (tune) {
-    const int ks = atoi(tune);
-    if ((ks == 1 || ks == 2 || ks == 4 || ks == 8) && (ks == 1 || (pl.bn <= 128 && num_kb >= 2LL * ks))) best_ks = ks;
-  }
   pl.ksplit = best_ks;
   pl.stages = stages_for(pl.bn, best_ks, cfg, pl.slabs, pl.packed);
 }
@@ -1577,10 +1572,8 @@ static int make_plan(Plan& pl, const void* a, long long lda_m, long long lda_k, 
   // Large 16-bit tiles run as CTA pairs (256 x 256 per pair, each CTA
   // loading half of Q) when there are enough pair tiles to fill the GPU.
   {
-    const char* e = getenv("FORGEML_GEMM_PAIR");  // diagnostic switch, default on
-    const bool allow = !(e && e[0] == '0');
     const long long pair_tiles = ((I + 2 * kBM - 1) / (2 * kBM)) * ((J + 255) / 256);
-    pl.pair = allow && !pl.swap && !pl.promote && dtype != FML_F32 && pl.bn == 256 && I >= 2 * kBM &&
+    pl.pair = !pl.swap && !pl.promote && dtype != FML_F32 && pl.bn == 256 && I >= 2 * kBM &&
               pair_tiles * 2 >= sms && pl.slabs == 1;
   }
   if (pl.pair) {
@@ -1647,10 +1640,6 @@ static int launch_plan(const Plan& pl, const CUtensorMap& mp, const CUtensorMap&
   // Tile raster: groups of group_i tile rows advance along N together
   // (measured on B200: 8 for CTA pairs, 16 for single CTAs).
   prm.group_i = std::min(prm.tiles_i, pl.pair ? 8 : 16);
-  if (const char* g = getenv("FORGEML_GEMM_GROUP")) {  // tuning override: tile-raster group height
-    const int v = atoi(g);
-    if (v > 0) prm.group_i = std::min(prm.tiles_i, v);
-  }
   prm.ksplit = pl.ksplit;
   prm.fmt = dtype == FML_F32 ? 2 : dtype == FML_BF16 ? 1 : 0;
   prm.p_mn = (pl.P.pack || pl.packed) ? 0 : (pl.P.mn ? 1 : 0);
@@ -1688,11 +1677,6 @@ static int launch_plan(const Plan& pl, const CUtensorMap& mp, const CUtensorMap&
     int res = resident_ctas(pl.bn, pl.promote, pl.ksplit, smem, sms);
     if (res <= 0) res = sms;
     grid = (int)std::min<long long>(want, res);
-  }
-  if (getenv("FORGEML_GEMM_DEBUG")) {  // diagnostic: the chosen plan
-    const int res = resident_ctas(pl.bn, pl.promote, pl.ksplit, smem, sms);
-    fprintf(stderr, "[fml_gemm] I=%d J=%d num_kb=%d bn=%d swap=%d packed=%d ksplit=%d slabs=%d stages=%d smem=%d grid=%d resident=%d\n",
-            prm.I, prm.J, prm.num_kb, pl.bn, prm.swap, pl.packed ? 1 : 0, pl.ksplit, pl.slabs, pl.stages, smem, grid, res);
   }
   if (pl.fused) {
     // one tile per cluster: the LayerNorm prologue and the exchange run once per CTA

@@ -1,23 +1,20 @@
 // Symmetric NVLink peer buffer of the tensor-parallel SUM all-reduce: one per
 // TP rank, opened by every peer through CUDA IPC (allreduce.cu), and read and
-// written by three kinds of kernel:
+// written by three kinds of kernel, each in a region of its own:
 //
-//   * the standalone all-reduce (allreduce.cu), which splits a message into
-//     kArBlocks fixed chunks, one per CTA index;
-//   * the GEMM epilogue of the fused decode linear (gemm.cu), which exchanges
-//     16-feature sub-blocks of a [features x 32 tokens] partial;
-//   * the low-latency (LL) all-reduce (allreduce.cu), whose data words carry
-//     their epoch: [2 sets][world slots][2 * slot_bytes] of 8-byte
+//   * exchange: the all-reduce fused into the decode GEMM's epilogue
+//     (gemm.cu), which exchanges 16-feature sub-blocks of a [features x 32
+//     tokens] partial: data [2 sets][world slots][slot_bytes], flags
+//     [2 sets][world sources][nsub] (u32 epochs raised by the source rank),
+//     epochs [nsub] (this rank's count of completed exchanges per sub-block);
+//   * ll: the one-shot low-latency all-reduce (allreduce.cu), whose data words
+//     carry their epoch: [2 sets][world slots][2 * slot_bytes] of 8-byte
 //     (4 data bytes, 4 epoch bytes) pairs, plus kArBlocks epochs;
-//   * the two-shot LL all-reduce (allreduce.cu): a reduce-scatter area like
-//     the LL one, an all-gather area [2 sets][2 * slot_bytes] (each position
-//     has one writer, its owner rank), plus kArBlocks epochs.
+//   * ts: the two-shot LL all-reduce (allreduce.cu): a reduce-scatter area
+//     like the LL one, an all-gather area [2 sets][2 * slot_bytes] (each
+//     position has one writer, its owner rank), plus kArBlocks epochs.
 //
-// Each kind owns its own data slots, flags and epochs, so they never
-// share a buffer region or an epoch counter.  Per flag region, data is
-// [2 sets][world slots][slot_bytes], flags [2 sets][world sources][units]
-// (u32 epochs raised by the source rank), epochs [units] (this rank's count
-// of completed exchanges per unit).
+// No two kinds share a byte or an epoch counter.
 #pragma once
 
 #include <stdint.h>
@@ -33,32 +30,30 @@ constexpr int kSubTokens = 32;     // token capacity of a sub-block (the decode 
 struct Layout {
   long long slot_bytes;  // one rank's message, per region
   int world;
-  int nsub;              // sub-blocks of the fused region (slot_bytes / 1024)
+  int nsub;              // sub-blocks of the exchange region (slot_bytes / 1 KB)
 
-  __host__ __device__ long long region_bytes(int units) const {
-    return 2LL * world * slot_bytes + 2LL * world * units * 4 + (long long)units * 4;
+  // exchange region, at offset 0
+  __host__ __device__ long long ex_data_off(int set, int slot) const {
+    return ((long long)set * world + slot) * slot_bytes;
   }
-  // region 0: standalone all-reduce; region 1: fused GEMM exchange
-  __host__ __device__ long long base(int region) const { return region == 0 ? 0 : region_bytes(kArBlocks); }
-  __host__ __device__ int units(int region) const { return region == 0 ? kArBlocks : nsub; }
-  __host__ __device__ long long data_off(int region, int set, int slot) const {
-    return base(region) + ((long long)set * world + slot) * slot_bytes;
+  __host__ __device__ long long ex_flag_off(int set, int src, int unit) const {
+    return 2LL * world * slot_bytes + (((long long)set * world + src) * nsub + unit) * 4;
   }
-  __host__ __device__ long long flag_off(int region, int set, int src, int unit) const {
-    return base(region) + 2LL * world * slot_bytes + (((long long)set * world + src) * units(region) + unit) * 4;
+  __host__ __device__ long long ex_epoch_off(int unit) const {
+    return 2LL * world * slot_bytes + 2LL * world * nsub * 4 + (long long)unit * 4;
   }
-  __host__ __device__ long long epoch_off(int region, int unit) const {
-    return base(region) + 2LL * world * slot_bytes + 2LL * world * units(region) * 4 + (long long)unit * 4;
+  __host__ __device__ long long ex_bytes() const {
+    return 2LL * world * slot_bytes + 2LL * world * nsub * 4 + (long long)nsub * 4;
   }
-  // region 2: LL all-reduce
-  __host__ __device__ long long ll_base() const { return region_bytes(kArBlocks) + region_bytes(nsub); }
+  // ll region
+  __host__ __device__ long long ll_base() const { return (ex_bytes() + 15) / 16 * 16; }
   __host__ __device__ long long ll_data_off(int set, int slot) const {
     return ll_base() + ((long long)set * world + slot) * 2 * slot_bytes;
   }
   __host__ __device__ long long ll_epoch_off(int unit) const {
     return ll_base() + 2LL * world * 2 * slot_bytes + (long long)unit * 4;
   }
-  // region 3: two-shot LL all-reduce
+  // ts region
   __host__ __device__ long long ts_base() const { return ll_base() + 4LL * world * slot_bytes + kArBlocks * 4; }
   __host__ __device__ long long ts_rs_off(int set, int slot) const {
     return ts_base() + ((long long)set * world + slot) * 2 * slot_bytes;
@@ -88,6 +83,7 @@ struct Ctx {
   uint8_t* own = nullptr;
   bool opened[kMaxWorld] = {};
   int device = 0;
+  int proto = 0;  // standalone all-reduce: 0 by group size, 1 one-shot LL, 2 two-shot LL
 };
 
 #ifdef __CUDACC__

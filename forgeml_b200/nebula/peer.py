@@ -14,7 +14,6 @@ up to ``max_bytes``; larger messages (prefill) go through NCCL.
 from __future__ import annotations
 
 import ctypes
-import os
 
 import torch
 import torch.distributed as dist
@@ -25,7 +24,11 @@ _DTYPES = (torch.float32, torch.float16, torch.bfloat16)
 
 
 class PeerAllReduce:
-    def __init__(self, context, max_bytes: int = 1 << 20, timeout_ms: float = 5000.0):
+    PROTOCOLS = {"auto": 0, "one_shot": 1, "two_shot": 2}
+
+    def __init__(self, context, max_bytes: int = 1 << 20, timeout_ms: float = 5000.0, protocol: str = "auto"):
+        if protocol not in self.PROTOCOLS:
+            raise ValueError(f"protocol must be one of {sorted(self.PROTOCOLS)}")
         if context.tp_size < 2 or context.device.type != "cuda":
             raise ValueError("PeerAllReduce needs a CUDA tensor-parallel group of 2 or more ranks")
         lib = _native.load()
@@ -36,6 +39,7 @@ class PeerAllReduce:
                      ctypes.byref(ptr), handle)
         self._ctx = ptr
         self.max_bytes = int(max_bytes)
+        _native.call("neb_ar_set_protocol", self._ctx, self.PROTOCOLS[protocol])
         gathered: list = [None] * context.tp_size
         dist.all_gather_object(gathered, bytes(handle), group=context.tp_group)
         self._blob = ctypes.create_string_buffer(b"".join(gathered), hb * context.tp_size)
@@ -67,8 +71,3 @@ class PeerAllReduce:
             _native.call("neb_ar_destroy", self._ctx)
             self._ctx = None
 
-
-def enabled() -> bool:
-    """The peer all-reduce is on unless FORGEML_PEER_ALLREDUCE=0 (NCCL then
-    carries every TP reduction)."""
-    return os.environ.get("FORGEML_PEER_ALLREDUCE", "1") != "0"

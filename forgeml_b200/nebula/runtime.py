@@ -17,7 +17,7 @@ attention kernel:
 with the K/V columns written into the pools by the GEMM epilogue and the TP
 partials summed over NVLink by the standalone peer all-reduce kernel (or, opt
 in, exchanged from the GEMM epilogue itself).  The two LayerNorms
-are folded into the QKV / up products (decode_ln_mode): gamma is folded into
+are folded into the QKV / up products (decode_ln): gamma is folded into
 the packed weight and the GEMM corrects its accumulator with the row
 statistics it computes while streaming the weight.  Larger steps (prefill) run the unfused chain:
 
@@ -39,7 +39,6 @@ cache slots are device inputs, so one graph serves every step).
 from __future__ import annotations
 
 import ctypes
-import os
 
 import torch
 import torch.distributed as dist
@@ -223,7 +222,7 @@ class ShardedDecoder(nn.Module):
         # peer all-reduce fused with the residual add; collective over the TP
         # group, so every rank builds it here in the same order.
         self._peer_ar = None
-        if context.tp_size > 1 and dev.type == "cuda" and peer.enabled():
+        if context.tp_size > 1 and dev.type == "cuda":
             es = torch.empty((), dtype=dtype).element_size()
             slot = max(16, (max(max_requests, 32) * h * es + 15) // 16 * 16)
             self._peer_ar = peer.PeerAllReduce(context, max_bytes=slot)
@@ -234,22 +233,36 @@ class ShardedDecoder(nn.Module):
         self._side_stream = None
         if self._peer_ar is not None and context.pp_size == 1:
             self._peer_ar2 = peer.PeerAllReduce(context, max_bytes=self._peer_ar.max_bytes)
-        self._fused_cache: dict[int, bool] = {}
+        self._fused_cache: dict[tuple, bool] = {}
+        # Decode-step layout choices (the defaults are the measured best; the
+        # alternatives compute the same step and are kept for tests):
+        #   fused_decode        layers of <= 32 tokens as fused GEMM launches
+        #   decode_ln           "fold": LayerNorms folded into the QKV / up
+        #                       products; "prologue": normalised by the GEMM's
+        #                       epilogue warps; "kernel": a LayerNorm launch
+        #   all_reduce_in_gemm  TP exchange inside the o / down GEMM epilogue
+        #                       instead of the standalone peer all-reduce
+        #                       (measured slower: the exchange then waits on
+        #                       the GEMM's critical path)
+        self.fused_decode = True
+        self.decode_ln = "fold"
+        self.all_reduce_in_gemm = False
 
     # ------------------------------------------------------------------ math
     def _fused_ok(self, bt: int) -> bool:
         """Whether a layer of ``bt`` tokens runs as the fused launches
         (LN+QKV+KV append, o+all-reduce, LN+up+GELU, down+all-reduce)."""
-        ok = self._fused_cache.get(bt)
+        key = (bt, self.fused_decode)
+        ok = self._fused_cache.get(key)
         if ok is None:
             ctx = self.context
             L = self.layers[0] if self.layers else None
-            ok = (L is not None and fused_enabled() and bt <= 32 and self.dtype in (torch.bfloat16, torch.float16)
+            ok = (L is not None and self.fused_decode and bt <= 32 and self.dtype in (torch.bfloat16, torch.float16)
                   and self.config.hidden_size % 64 == 0
                   and all(isinstance(g, PackedLinear) and g.fused_ok(bt) for g in (L.qkv, L.o, L.up, L.down))
                   and (ctx.tp_size == 1 or (self._peer_ar is not None and self.config.hidden_size % 16 == 0
                                             and self.config.hidden_size * 64 <= self._peer_ar.max_bytes)))
-            self._fused_cache[bt] = ok
+            self._fused_cache[key] = ok
         return ok
 
     def _layer_fused(self, L: _Layer, lid: int, x: torch.Tensor, b: int, t: int, slots: torch.Tensor,
@@ -259,7 +272,7 @@ class ShardedDecoder(nn.Module):
         hl, hd, hl_hd = self.num_heads_local, self.head_dim, self._hl_hd
         dev = x.device
         kp, vp = self.cache.k_pool[lid], self.cache.v_pool[lid]
-        ln_mode = decode_ln_mode()
+        ln_mode = self.decode_ln
         if ln_mode == "fold":
             lin, wsum, wbias = L.qkv_ln
             q = lin.fused(x, torch.empty((bt, hl_hd), dtype=self.dtype, device=dev), ln_fold=(wsum, wbias, 1e-5),
@@ -275,7 +288,7 @@ class ShardedDecoder(nn.Module):
         tp = self.context.tp_size
         if tp == 1:  # residual add in the plain epilogue
             x = L.o(attn, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x)
-        elif fused_ar_enabled(tp):
+        elif self.all_reduce_in_gemm:
             x = L.o.fused(attn, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x,
                           ar_ctx=ar.handle)
         else:
@@ -292,7 +305,7 @@ class ShardedDecoder(nn.Module):
             mid = L.up(h2, torch.empty((bt, L.wup.shape[0]), dtype=self.dtype, device=dev), act=_native.ACT_GELU_TANH)
         if tp == 1:
             return L.down(mid, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x)
-        if fused_ar_enabled(tp):
+        if self.all_reduce_in_gemm:
             return L.down.fused(mid, torch.empty((bt, h), dtype=self.dtype, device=dev), residual=x,
                                 ar_ctx=ar.handle)
         return self._tp_sum_add(L.down(mid, torch.empty((bt, h), dtype=self.dtype, device=dev)), x, ar)
@@ -505,36 +518,6 @@ class ShardedDecoder(nn.Module):
             if ar is not None:
                 ar.close()
                 setattr(self, name, None)
-
-
-def fused_enabled() -> bool:
-    """Decode layers run as fused launches unless FORGEML_FUSED_DECODE=0 (a
-    diagnostic switch: the unfused chain computes the same step)."""
-    return os.environ.get("FORGEML_FUSED_DECODE", "1") != "0"
-
-
-def fused_ar_enabled(tp: int) -> bool:
-    """TP all-reduce inside the o / down GEMM epilogue (FORGEML_FUSED_AR=1),
-    or the standalone peer all-reduce kernel after the GEMM (default).
-    Measured on B200 at config 4 with the current GEMM epilogue: TP2 1.006 ms
-    per step standalone vs 1.046 ms in the epilogue, TP8 1.13 vs 1.38 ms: the
-    exchange waits inside the GEMM's critical path, while the standalone
-    kernel's prologue overlaps the GEMM's tail."""
-    return os.environ.get("FORGEML_FUSED_AR", "0") == "1"
-
-
-def decode_ln_mode() -> str:
-    """How the decode step's pre-QKV / pre-up LayerNorms run
-    (FORGEML_DECODE_LN):
-      "fold"     folded into the QKV / up products (gamma in the packed
-                 weight, statistics computed by the GEMM while its main loop
-                 runs, correction in the epilogue): no LayerNorm launch;
-      "prologue" normalised by the GEMM's epilogue warps into the operand
-                 stages before the main loop (slower on B200: it lengthens
-                 the GEMM's critical path);
-      "kernel"   a separate LayerNorm launch before the GEMM."""
-    v = os.environ.get("FORGEML_DECODE_LN", "fold")
-    return v if v in ("fold", "prologue", "kernel") else "fold"
 
 
 # The serving engine lives in engine.py; the reference exposes it from this module.

@@ -238,8 +238,9 @@ FML_API int neb_add(const void* a, const void* b, void* y, int64_t n, int dtype,
  * (stream-ordered, CUDA-graph capturable).  A wait that exceeds timeout_ms
  * raises bit 32 of fml_device_status() instead of hanging.  Protocol: each
  * 4-byte word travels with the call's epoch in one 8-byte store and readers
- * poll the words (low latency; FORGEML_AR_PROTO=flag selects data stores,
- * a system fence and per-chunk epoch flags instead).
+ * poll the words (low latency), either one-shot (every rank pushes its whole
+ * partial to every peer) or two-shot (reduce-scatter to sub-shard owners,
+ * then all-gather of the sums); see neb_ar_set_protocol.
  * ------------------------------------------------------------------------- */
 /* Bytes of one IPC handle (cudaIpcMemHandle_t). */
 FML_API int64_t neb_ar_handle_bytes(void);
@@ -251,6 +252,11 @@ FML_API int neb_ar_open(void* ctx, const void* handles);
  * buffer (neb_ar_buffer of the other contexts); this rank's entry ignored. */
 FML_API int neb_ar_set_peers(void* ctx, void* const* bases);
 FML_API void* neb_ar_buffer(void* ctx);
+/* Protocol of this context's standalone all-reduce: 0 = the library's
+ * choice (one-shot), 1 = one-shot LL, 2 = two-shot LL.  Every rank of a
+ * group must use the same protocol.  No reference counterpart (NCCL chose
+ * its own algorithm there). */
+FML_API int neb_ar_set_protocol(void* ctx, int protocol);
 /* n elements of dtype; residual may be NULL (then out = round(sum)); 16-byte
  * aligned pointers, n * sizeof(dtype) a multiple of 16 and <= max_bytes. */
 FML_API int neb_ar_all_reduce(void* ctx, const void* part, const void* residual, void* out, int64_t n,

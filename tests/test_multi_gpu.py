@@ -113,13 +113,12 @@ def test_tp8_bf16():
     _run(8, 8, 1, "bfloat16")
 
 
-def _ar_worker(rank, world, store, dtype_name, proto="ll"):
+def _ar_worker(rank, world, store, dtype_name, proto="auto"):
     import os
 
     from forgeml_b200.nebula import ParallelContext
     from forgeml_b200.nebula.peer import PeerAllReduce
 
-    os.environ["FORGEML_AR_PROTO"] = proto
     os.environ["LOCAL_RANK"] = str(rank)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     torch.cuda.set_device(rank)
@@ -128,7 +127,7 @@ def _ar_worker(rank, world, store, dtype_name, proto="ll"):
     ctx = ParallelContext.from_env(tp_size=world, pp_size=1, device="cuda", timeout_s=60)
     dtype = getattr(torch, dtype_name)
     dev = ctx.device
-    ar = PeerAllReduce(ctx, max_bytes=1 << 20)
+    ar = PeerAllReduce(ctx, max_bytes=1 << 20, protocol=proto)
     try:
         for it, n in enumerate((2048 * 32, 8, 4096, 2048 * 32)):
             g = torch.Generator().manual_seed(1000 * it + rank)
@@ -175,7 +174,7 @@ def _ar_worker(rank, world, store, dtype_name, proto="ll"):
             dist.destroy_process_group()
 
 
-def _run_ar(world, dtype_name, proto="ll"):
+def _run_ar(world, dtype_name, proto="auto"):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     with tempfile.TemporaryDirectory() as d:
@@ -196,20 +195,20 @@ def test_peer_all_reduce_2_bf16():
     _run_ar(2, "bfloat16")
 
 
-def test_peer_all_reduce_2_bf16_flag_protocol():
-    _run_ar(2, "bfloat16", "flag")
-
-
 def test_peer_all_reduce_2_bf16_two_shot():
-    _run_ar(2, "bfloat16", "ll2")
+    _run_ar(2, "bfloat16", "two_shot")
 
 
 def test_peer_all_reduce_4_bf16_two_shot():
-    _run_ar(4, "bfloat16", "ll2")
+    _run_ar(4, "bfloat16", "two_shot")
 
 
 def test_peer_all_reduce_8_bf16_two_shot():
-    _run_ar(8, "bfloat16", "ll2")
+    _run_ar(8, "bfloat16", "two_shot")
+
+
+def test_peer_all_reduce_8_bf16_one_shot():
+    _run_ar(8, "bfloat16", "one_shot")
 
 
 def test_peer_all_reduce_2_fp32():

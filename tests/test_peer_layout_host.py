@@ -1,9 +1,9 @@
 """Layout of the NVLink peer buffer (forgeml_b200/csrc/peer_layout.cuh), checked
 on the CPU: the header is compiled with g++ into a small program that prints
-every region's byte ranges, and the test asserts that the flag-protocol
-all-reduce, the GEMM-epilogue exchange, the LL and the two-shot LL
-all-reduce regions (data sets, flags, epochs) are pairwise disjoint, aligned as their kernels access
-them, and inside the allocation neb_ar_create makes (Layout::total)."""
+every region's byte ranges, and the test asserts that the GEMM-epilogue
+exchange, the LL and the two-shot LL all-reduce regions (data sets, flags,
+epochs) are pairwise disjoint, aligned as their kernels access them, and
+inside the allocation neb_ar_create makes (Layout::total)."""
 
 import shutil
 import subprocess
@@ -26,16 +26,11 @@ int main(int argc, char** argv) {
   l.world = atoi(argv[2]);
   l.nsub = (int)((l.slot_bytes + 1023) / 1024);
   printf("total %lld\n", l.total());
-  for (int region = 0; region < 2; ++region) {
-    const int units = l.units(region);
-    for (int set = 0; set < 2; ++set)
-      for (int s = 0; s < l.world; ++s)
-        printf("data%d %lld %lld\n", region, l.data_off(region, set, s), l.slot_bytes);
-    for (int set = 0; set < 2; ++set)
-      for (int s = 0; s < l.world; ++s)
-        printf("flags%d %lld %lld\n", region, l.flag_off(region, set, s, 0), (long long)units * 4);
-    printf("epochs%d %lld %lld\n", region, l.epoch_off(region, 0), (long long)units * 4);
-  }
+  for (int set = 0; set < 2; ++set)
+    for (int s = 0; s < l.world; ++s) printf("data %lld %lld\n", l.ex_data_off(set, s), l.slot_bytes);
+  for (int set = 0; set < 2; ++set)
+    for (int s = 0; s < l.world; ++s) printf("flags %lld %lld\n", l.ex_flag_off(set, s, 0), (long long)l.nsub * 4);
+  printf("epochs %lld %lld\n", l.ex_epoch_off(0), (long long)l.nsub * 4);
   for (int set = 0; set < 2; ++set)
     for (int s = 0; s < l.world; ++s) printf("lldata %lld %lld\n", l.ll_data_off(set, s), 2 * l.slot_bytes);
   printf("llepochs %lld %lld\n", l.ll_epoch_off(0), (long long)fml::peer::kArBlocks * 4);
