@@ -825,7 +825,10 @@ def run_c5(args) -> None:
     gaps = [rng.expovariate(64.0) for _ in range(n_req)]
 
     async def drive():
-        b = AsyncBatcher(engine, max_batch_size=64, max_queue_size=n_req + 1, batch_window_ms=2.0)
+        # prompts of different lengths share decode batches (Engine.generate_mixed);
+        # --c5-cohorts keeps the reference's equal-length cohorts instead
+        b = AsyncBatcher(engine, max_batch_size=64, max_queue_size=n_req + 1, batch_window_ms=args.c5_window_ms,
+                         mix_prompt_lengths=not args.c5_cohorts)
         lat = []
 
         async def one(i, delay):
@@ -853,7 +856,8 @@ def run_c5(args) -> None:
             "config": {"workload": "nebula_c5_async_batcher", "model": "32L d4096 h32x128 ffn16384 v32000",
                        "parallelism": f"tp{tp}xpp{pp}", "requests": n_req, "new_tokens": n_new,
                        "arrivals": "poisson 64 req/s (seeded)", "prompt_len": "uniform [128, 2048]",
-                       "batch_cap": 64},
+                       "batch_cap": 64, "batching": "equal-length cohorts" if args.c5_cohorts
+                       else "mixed prompt lengths (generate_mixed)", "window_ms": args.c5_window_ms},
             "wall_s": wall, "generated_tokens": total,
             "latency_s": {"p50": lat[len(lat) // 2], "p90": lat[int(len(lat) * 0.9)], "max": lat[-1]}}
     print(json.dumps(line), flush=True)
@@ -986,6 +990,8 @@ def main() -> None:
                     help="c5: serve config 5 through the AsyncBatcher over TP x PP (launch with torchrun)")
     ap.add_argument("--c5-requests", type=int, default=32)
     ap.add_argument("--c5-new", type=int, default=64)
+    ap.add_argument("--c5-window-ms", type=float, default=50.0, help="batching window of the c5 batcher")
+    ap.add_argument("--c5-cohorts", action="store_true", help="c5: equal-length cohorts (the reference's batching)")
     args = ap.parse_args()
     if args.case:
         run_case(args)

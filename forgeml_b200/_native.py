@@ -107,7 +107,7 @@ _SIGNATURES = {
         _I,
         [_P, _S4, _P, _S4, _P, _S4, _P, _S4, _I, _I, _F, _P, _S4, _I64, _I64, _I64, _I64, _I64, _I, _P],
     ),
-    "neb_attention": (_I, [_P, _S4, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _I, _P]),
+    "neb_attention": (_I, [_P, _S4, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _F, _I, _P]),
     "neb_kv_append": (_I, [_P, _S4, _P, _S4, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I, _P]),
     "neb_embed": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I, _P]),
     "neb_argmax": (_I, [_P, _I64, _I64, _I64, _P, _I, _P]),

@@ -708,6 +708,10 @@ static int launch_sdpa(const SdpaParams& p, cudaStream_t st) {
 using namespace fml;
 
 namespace fml {
+int neb_prefill_tensor_core(const void* q, const int64_t qs[4], const void* k_pool, const void* v_pool,
+                            const int32_t* slot_of, const int32_t* start_pos, void* out, int64_t B, int64_t T,
+                            int64_t H, int64_t D, int64_t max_seq, int64_t slots, float scale, int dtype,
+                            cudaStream_t st);
 int sdpa_tensor_core(const void* q, const int64_t qs[4], const void* k, const int64_t ks[4], const void* v,
                      const int64_t vs[4], int mask_kind, int is_causal, float scale, void* out,
                      const int64_t os[4], int64_t B, int64_t H, int64_t Sq, int64_t Sk, int64_t D, int dtype,
@@ -717,11 +721,11 @@ int sdpa_tensor_core(const void* q, const int64_t qs[4], const void* k, const in
 extern "C" int neb_attention(const void* q, const int64_t q_strides[4], const void* k_pool,
                              const void* v_pool, const int32_t* slot_of, const int32_t* start_pos,
                              void* out, int64_t batch, int64_t t, int64_t heads, int64_t head_dim,
-                             int64_t max_seq, float scale, int dtype, void* stream) {
+                             int64_t max_seq, int64_t pool_slots, float scale, int dtype, void* stream) {
   if (!valid_dtype(dtype)) return fail(FML_EINVAL, "neb_attention: bad dtype");
   if (!q || !q_strides || !k_pool || !v_pool || !slot_of || !start_pos || !out)
     return fail(FML_EINVAL, "neb_attention: null pointer");
-  if (batch <= 0 || t <= 0 || heads <= 0 || head_dim <= 0 || max_seq <= 0)
+  if (batch <= 0 || t <= 0 || heads <= 0 || head_dim <= 0 || max_seq <= 0 || pool_slots <= 0)
     return fail(FML_EINVAL, "neb_attention: sizes must be positive");
   if (head_dim > attn::kMaxD) return fail(FML_EUNSUPPORTED, "neb_attention: head_dim > 256");
   if (q_strides[3] != 1) return fail(FML_EUNSUPPORTED, "neb_attention: q innermost stride must be 1");
@@ -733,6 +737,15 @@ extern "C" int neb_attention(const void* q, const int64_t q_strides[4], const vo
   // and shorter CTAs lose to their per-CTA start-up.  Depends only on the
   // launch shape (not on the device-side positions), so a captured decode
   // step keeps a valid split.
+  // Steps of several tokens per request (prefill) run on the tensor cores
+  // when the layout allows (sdpa_tc.cu); single-token decode steps stream
+  // the keys with the bulk-copy kernel below.
+  if (t > 1) {
+    const int rc = neb_prefill_tensor_core(q, q_strides, k_pool, v_pool, slot_of, start_pos, out, batch, t, heads,
+                                           head_dim, max_seq, pool_slots, scale, dtype,
+                                           reinterpret_cast<cudaStream_t>(stream));
+    if (rc != FML_EUNSUPPORTED) return rc;
+  }
   const long long nq = batch * t * heads;
   const long long target = 2LL * num_sms(current_device());
   int nsplit = (int)std::min<long long>(8, std::max<long long>(1, target / nq));

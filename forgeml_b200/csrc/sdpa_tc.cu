@@ -46,6 +46,13 @@ struct Args {
   float scale_log2;  // softmax scale * log2(e)
   void* out;
   long long os[4];   // output strides (elements) of [B, H, Sq, D]
+  // Nebula prefill over the KV pool (null for plain SDPA): request b's keys
+  // are rows 0 .. start_pos[b] + Sq - 1 of pool slot slot_of[b], and its
+  // query i sits at absolute position start_pos[b] + i (causal over
+  // absolute positions, src/nebula/runtime.py:139-143).
+  const int32_t* slot_of;
+  const int32_t* start_pos;
+  int max_seq;
 };
 
 // Coordinates of a tile in a 4-D tensor map whose outer dimensions are S, H
@@ -100,8 +107,21 @@ __global__ void __launch_bounds__(kThreads, D <= 64 ? 2 : 1)
   const int q0 = qblk * kBQ;
   auto bar = [&](int i) { return base + L::bars + 8u * (uint32_t)i; };
   const uint32_t tmem_holder = base + L::bars + 8u * kNumBars;
+  // Keys of this request and the absolute position of its first query.
+  // Pool slots and start positions are step inputs (no kernel of this
+  // library writes them), so they are read before the dependency wait.
+  int kv_b = b, q_off = 0, sk = a.Sk;
+  if (a.slot_of != nullptr) {
+    kv_b = a.slot_of[b];
+    q_off = a.start_pos[b];
+    sk = q_off + a.Sq;
+    if (kv_b < 0 || q_off < 0 || sk > a.max_seq) {  // uniform over the CTA: no TMEM or barrier touched yet
+      if (threadIdx.x == 0 && qblk == 0 && h == 0) raise_device_error(DEV_ERR_ATTN_RANGE);
+      return;
+    }
+  }
   // keys this block of queries attends to
-  const int kend = a.causal ? min(a.Sk, q0 + kBQ) : a.Sk;
+  const int kend = a.causal ? min(sk, q0 + kBQ + q_off) : sk;
   const int nkb = (kend + kBK - 1) / kBK;
   __shared__ int s_abort;
 
@@ -151,8 +171,8 @@ __global__ void __launch_bounds__(kThreads, D <= 64 ? 2 : 1)
         const uint32_t kdst = base + L::kv + st * 2 * L::kTile, vdst = kdst + L::kTile;
         mbar_arrive_expect_tx(bar(kKvFull0 + st), 2 * L::kTile);
         for (int sl = 0; sl < L::kSlabs; ++sl) {
-          load_tile(&tmK, ord_k, bar(kKvFull0 + st), kdst + sl * kBK * 128, sl * 64, j * kBK, h, b);
-          load_tile(&tmV, ord_v, bar(kKvFull0 + st), vdst + sl * kBK * 128, sl * 64, j * kBK, h, b);
+          load_tile(&tmK, ord_k, bar(kKvFull0 + st), kdst + sl * kBK * 128, sl * 64, j * kBK, h, kv_b);
+          load_tile(&tmV, ord_v, bar(kKvFull0 + st), vdst + sl * kBK * 128, sl * 64, j * kBK, h, kv_b);
         }
         ++issued;
       }
@@ -233,8 +253,8 @@ __global__ void __launch_bounds__(kThreads, D <= 64 ? 2 : 1)
       tc_fence_after();
       const int key0 = j * kBK;
       // keys of this block this row may see
-      int lim = min(kBK, a.Sk - key0);
-      if (a.causal) lim = min(lim, qi - key0 + 1);
+      int lim = min(kBK, sk - key0);
+      if (a.causal) lim = min(lim, qi + q_off - key0 + 1);
       // pass 1: row maximum of the scaled scores
       float mx = -INFINITY;
 #pragma unroll
@@ -406,6 +426,46 @@ static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMa
 }
 
 }  // namespace sdpa_tc
+
+// Nebula prefill attention over the KV pool on the tensor cores: queries
+// q [B, T, H, D] (strided), keys / values rows of pool [slots, H, max_seq, D]
+// (contiguous), out [B, T, H*D] contiguous.  FML_EUNSUPPORTED when not
+// covered (fp32, head dim other than 64 / 128, unaddressable strides).
+int neb_prefill_tensor_core(const void* q, const int64_t qs[4], const void* k_pool, const void* v_pool,
+                            const int32_t* slot_of, const int32_t* start_pos, void* out, int64_t B, int64_t T,
+                            int64_t H, int64_t D, int64_t max_seq, int64_t slots, float scale, int dtype,
+                            cudaStream_t st) {
+  using namespace sdpa_tc;
+  if ((dtype != FML_BF16 && dtype != FML_F16) || (D != 64 && D != 128)) return FML_EUNSUPPORTED;
+  if (B * H > 65535 || max_seq > (1 << 30)) return FML_EUNSUPPORTED;
+  const bool bf = dtype == FML_BF16;
+  // q as [B, H, T, D]; the pools as [slots, H, max_seq, D]
+  const int64_t q4[4] = {qs[0], qs[2], qs[1], qs[3]};
+  const int64_t p4[4] = {H * max_seq * D, max_seq * D, D, 1};
+  CUtensorMap mq, mk, mv;
+  MapOrder oq{}, okk{}, ov{};
+  if (!encode_operand(&mq, &oq, q, q4, B, H, T, D, bf) ||
+      !encode_operand(&mk, &okk, k_pool, p4, slots, H, max_seq, D, bf) ||
+      !encode_operand(&mv, &ov, v_pool, p4, slots, H, max_seq, D, bf))
+    return FML_EUNSUPPORTED;
+  Args a = {};
+  a.Sq = (int)T;
+  a.Sk = (int)max_seq;
+  a.H = (int)H;
+  a.causal = 1;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.out = out;
+  const int64_t o4[4] = {T * H * D, D, H * D, 1};  // [B, T, H, D] seen as [B, H, T, D]
+  for (int i = 0; i < 4; ++i) a.os[i] = o4[i];
+  a.slot_of = slot_of;
+  a.start_pos = start_pos;
+  a.max_seq = (int)max_seq;
+  if (bf)
+    return D == 64 ? launch<__nv_bfloat16, 64>(mq, mk, mv, oq, okk, ov, a, B, H, st)
+                   : launch<__nv_bfloat16, 128>(mq, mk, mv, oq, okk, ov, a, B, H, st);
+  return D == 64 ? launch<__half, 64>(mq, mk, mv, oq, okk, ov, a, B, H, st)
+                 : launch<__half, 128>(mq, mk, mv, oq, okk, ov, a, B, H, st);
+}
 
 // Runs the tensor-core kernel when it covers the call: 16-bit q/k/v/out,
 // head dim 64 or 128, no explicit mask (causal allowed), unit head-dim

@@ -37,7 +37,7 @@ def attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, slot_
         out = torch.empty((b, t, h * d), dtype=q.dtype, device=q.device)
     _native.call(
         "neb_attention", q.data_ptr(), _native.strides4(q), k_pool.data_ptr(), v_pool.data_ptr(),
-        slot_of.data_ptr(), start_pos.data_ptr(), out.data_ptr(), b, t, h, d, k_pool.shape[2],
+        slot_of.data_ptr(), start_pos.data_ptr(), out.data_ptr(), b, t, h, d, k_pool.shape[2], k_pool.shape[0],
         1.0 / math.sqrt(d), _native.dtype_code(q.dtype), _stream(q),
     )
     return out

@@ -180,13 +180,17 @@ FML_API int fml_sdpa(const void* q, const int64_t q_strides[4],
  * slot slot_of[b] (int32, device).  Query b,t sits at absolute position
  * start_pos[b] + t (int32, device) and attends keys 0..start_pos[b]+t.
  * q is [B,T,H,D] with element strides q_strides (innermost 1); out is
- * [B,T,H,D] contiguous rows of H*D.  Scores and softmax in fp32.
+ * [B,T,H,D] contiguous rows of H*D.  Scores and softmax in fp32.  The pools
+ * hold pool_slots slots.  Steps of more than one token per request (prefill)
+ * with 16-bit data and head dim 64 or 128 run on the tensor cores (scores
+ * and P V by tcgen05, P rounded to the model dtype as in the reference's
+ * attn.to(x.dtype)); single-token steps stream the keys on CUDA cores.
  * ------------------------------------------------------------------------- */
 FML_API int neb_attention(const void* q, const int64_t q_strides[4],
                   const void* k_pool, const void* v_pool,
                   const int32_t* slot_of, const int32_t* start_pos,
                   void* out, int64_t batch, int64_t t, int64_t heads,
-                  int64_t head_dim, int64_t max_seq, float scale,
+                  int64_t head_dim, int64_t max_seq, int64_t pool_slots, float scale,
                   int dtype, void* stream);
 
 /* ---------------------------------------------------------------------------
