@@ -480,10 +480,11 @@ def kernel_rooflines(engine, dev, ctx_len: int, ms_per_step: float, ar_family: d
             for w, n_in, n_out, r in ((L.wqkv, h, 3 * hl_hd, 0), (L.wo, hl_hd, h, res is not None),
                                       (L.wup, h, f_l, 0), (L.wdown, f_l, h, res is not None)):
                 gbytes += (w.numel() + b * n_in + b * n_out * (2 if r else 1)) * es
-        if dec.is_last:
-            head_out = torch.empty(b, dec.config.vocab_size, device=dev, dtype=dec.dtype)
-            fns.append(lambda x=x, o=head_out: dec.head_gemm(x, o))
-            gbytes += (dec.head.numel() + b * h + b * dec.config.vocab_size) * es
+    if dec.is_last:  # once per step for the whole batch
+        xh = rnd(BATCH, h)
+        head_out = torch.empty(BATCH, dec.config.vocab_size, device=dev, dtype=dec.dtype)
+        fns.append(lambda: dec.head_gemm(xh, head_out))
+        gbytes += (dec.head.numel() + BATCH * h + BATCH * dec.config.vocab_size) * es
     g_us = _graph_time_us(fns)
     n_g = len(fns)
 

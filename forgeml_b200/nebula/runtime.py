@@ -368,23 +368,25 @@ class ShardedDecoder(nn.Module):
             return self._core_rows(tokens, slots, starts, b, t, last_only, self._peer_ar)
         dev = self.context.device
         h0 = b // 2
-        logits = torch.empty((b, self.config.vocab_size), dtype=self.dtype, device=dev)
         main = torch.cuda.current_stream(dev)
         if self._side_stream is None:
             self._side_stream = torch.cuda.Stream(device=dev)
         side = self._side_stream
         side.wait_stream(main)
-        self._core_rows(tokens[:h0], slots[:h0], starts[:h0], h0, 1, last_only, self._peer_ar, out=logits[:h0])
+        # the layers per half; the final LayerNorm and lm_head once for the
+        # whole batch (the head's weights are streamed once per step)
+        xa = self._core_rows(tokens[:h0], slots[:h0], starts[:h0], h0, 1, last_only, self._peer_ar, head=False)
         with torch.cuda.stream(side):
-            self._core_rows(tokens[h0:], slots[h0:], starts[h0:], b - h0, 1, last_only, self._peer_ar2,
-                            out=logits[h0:])
+            xb = self._core_rows(tokens[h0:], slots[h0:], starts[h0:], b - h0, 1, last_only, self._peer_ar2,
+                                 head=False)
         main.wait_stream(side)
-        return logits
+        return self._head(torch.cat([xa, xb]), b, 1, last_only)
 
     def _core_rows(self, tokens: torch.Tensor, slots: torch.Tensor, starts: torch.Tensor, b: int, t: int,
-                   last_only: bool, ar, out: torch.Tensor | None = None) -> torch.Tensor:
-        """Forward of these rows on this stage (all-reduce context ``ar``);
-        logits on the last stage (into ``out`` when given), else None."""
+                   last_only: bool, ar, head: bool = True) -> torch.Tensor:
+        """Forward of these rows on this stage (all-reduce context ``ar``):
+        logits on the last stage (the hidden rows when ``head`` is False),
+        else None."""
         ctx = self.context
         h = self.config.hidden_size
         dev = ctx.device
@@ -401,13 +403,17 @@ class ShardedDecoder(nn.Module):
             with record_function("nebula::pp_send"):
                 dist.send(x, dst=ctx.rank + ctx.tp_size)
             return None
+        return self._head(x, b, t, last_only) if head else x
+
+    def _head(self, x: torch.Tensor, b: int, t: int, last_only: bool) -> torch.Tensor:
+        """Final LayerNorm and lm_head of hidden rows x [b*t, h]."""
+        h = self.config.hidden_size
+        dev = x.device
         rows = b if last_only else b * t
         stride = t * h if last_only else h
         src = x[(t - 1):] if last_only else x  # row (t-1) of each request, stride t*h
         hf = _ln(src, self.lnf_w, self.lnf_b, torch.empty((rows, h), dtype=self.dtype, device=dev), rows, x_stride=stride)
-        if out is None:
-            out = torch.empty((rows, self.config.vocab_size), dtype=self.dtype, device=dev)
-        return self.head_gemm(hf, out)
+        return self.head_gemm(hf, torch.empty((rows, self.config.vocab_size), dtype=self.dtype, device=dev))
 
     # ------------------------------------------------------------------ API
     def forward(self, tokens: torch.Tensor, request_ids: tuple[int, ...], start_pos,
