@@ -379,12 +379,16 @@ def reference_forgeml_cpu() -> dict | None:
         sys.path.remove(str(ref_root))
 
 
-# DRAM traffic per launch over the algorithmic bytes, from one ncu capture of
-# each kernel family (dram__bytes_read.sum + dram__bytes_write.sum):
-#   attention: ncu --set full --clock-control none -k regex:neb_attn -s 3 -c 1 ... bench.py --case attention --steps 20
-#   gemm:      ncu --set full --clock-control none -k regex:gemm_kernel ... bench.py --case gemm-decode --steps 20 (down projection)
+# DRAM traffic per launch over the algorithmic bytes, from the ncu captures
+# summarised under profiles/ (dram__bytes_read.sum + dram__bytes_write.sum of
+# each captured launch / its algorithmic bytes):
+#   attention: neb_attn_bulk_kernel_b32_ctx1024.md
+#              (ncu --set full --clock-control none -k regex:neb_attn ... bench.py --case attention)
+#   gemm:      gemm_kernel_decode_fused_m32_tp1_tp8.md, the four TP1 launches
+#              (ncu --set full --clock-control none -k regex:gemm_kernel ... bench.py --case gemm-fused --tp 1)
 # Traffic in the JSON line is this ratio times the launch's algorithmic bytes.
-TRAFFIC_RATIO = {"attention": (268.618240e6 + 4.372736e6) / 268697600, "gemm": (34.288384e6 + 1.28e3) / 34340864}
+TRAFFIC_RATIO = {"attention": (268.618240e6 + 4.372736e6) / 268697600,
+                 "gemm": (33.801216 + 34.293248 + 25.405184 + 8.734208) / (34.209792 + 34.340864 + 25.690112 + 8.781824)}
 
 
 def _graph_time_us(fns, reps: int = 5) -> float:

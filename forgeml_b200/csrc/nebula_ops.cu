@@ -102,7 +102,9 @@ __device__ __forceinline__ bool better(float v, long long i, float bv, long long
   return i < bi;
 }
 
-template <typename T>
+// One CTA per row.  VEC: 16-byte loads, a thread's vectors all issued before
+// any is compared (one memory latency per row instead of one per element).
+template <typename T, bool VEC>
 __global__ void __launch_bounds__(1024)
     argmax_kernel(const T* __restrict__ logits, long long rs, long long cols, int64_t* __restrict__ out) {
   pdl_wait();
@@ -110,9 +112,40 @@ __global__ void __launch_bounds__(1024)
   const T* row = logits + (long long)blockIdx.x * rs;
   float bv = -INFINITY;
   long long bi = cols;  // sentinel (worse than any real index once a value is seen)
-  for (long long c = threadIdx.x; c < cols; c += blockDim.x) {
-    const float v = to_f32<T>(row[c]);
-    if (bi == cols || better(v, c, bv, bi)) { bv = v; bi = c; }
+  if (VEC) {
+    constexpr int E = 16 / sizeof(T);
+    constexpr int kBatch = 4;  // vectors in flight per thread
+    const long long nvec = cols / E;
+    const uint4* rv = reinterpret_cast<const uint4*>(row);
+    for (long long v0 = threadIdx.x; v0 < nvec; v0 += (long long)kBatch * blockDim.x) {
+      uint4 w[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const long long vi = v0 + (long long)u * blockDim.x;
+        if (vi < nvec) w[u] = rv[vi];
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const long long vi = v0 + (long long)u * blockDim.x;
+        if (vi >= nvec) continue;
+        const T* e = reinterpret_cast<const T*>(&w[u]);
+#pragma unroll
+        for (int k = 0; k < E; ++k) {
+          const float v = to_f32<T>(e[k]);
+          const long long c = vi * E + k;
+          if (bi == cols || better(v, c, bv, bi)) { bv = v; bi = c; }
+        }
+      }
+    }
+    for (long long c = nvec * E + threadIdx.x; c < cols; c += blockDim.x) {  // tail
+      const float v = to_f32<T>(row[c]);
+      if (bi == cols || better(v, c, bv, bi)) { bv = v; bi = c; }
+    }
+  } else {
+    for (long long c = threadIdx.x; c < cols; c += blockDim.x) {
+      const float v = to_f32<T>(row[c]);
+      if (bi == cols || better(v, c, bv, bi)) { bv = v; bi = c; }
+    }
   }
   __shared__ float sv[32];
   __shared__ long long si[32];
@@ -228,13 +261,17 @@ extern "C" int neb_argmax(const void* logits, int64_t row_stride, int64_t rows, 
   if (rows <= 0 || cols <= 0 || rows > (1ll << 31) - 1) return fail(FML_EINVAL, "neb_argmax: bad sizes");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int threads = cols >= 1024 ? 1024 : 256;
-  if (dtype == FML_F32)
-    launch_pdl(neb::argmax_kernel<float>, dim3((unsigned)rows), dim3(threads), 0, st, 1, static_cast<const float*>(logits), row_stride, cols, out);
-  else if (dtype == FML_BF16)
-    launch_pdl(neb::argmax_kernel<__nv_bfloat16>, dim3((unsigned)rows), dim3(threads), 0, st, 1, 
-        static_cast<const __nv_bfloat16*>(logits), row_stride, cols, out);
-  else
-    launch_pdl(neb::argmax_kernel<__half>, dim3((unsigned)rows), dim3(threads), 0, st, 1, static_cast<const __half*>(logits), row_stride, cols, out);
+  const long long es = (long long)dtype_size(dtype);
+  const bool vec = reinterpret_cast<uintptr_t>(logits) % 16 == 0 && (row_stride * es) % 16 == 0;
+#define ARGMAX_LAUNCH(TT)                                                                                       \
+  (vec ? launch_pdl(neb::argmax_kernel<TT, true>, dim3((unsigned)rows), dim3(threads), 0, st, 1,              \
+                    static_cast<const TT*>(logits), (long long)row_stride, (long long)cols, out)                 \
+       : launch_pdl(neb::argmax_kernel<TT, false>, dim3((unsigned)rows), dim3(threads), 0, st, 1,             \
+                    static_cast<const TT*>(logits), (long long)row_stride, (long long)cols, out))
+  if (dtype == FML_F32) ARGMAX_LAUNCH(float);
+  else if (dtype == FML_BF16) ARGMAX_LAUNCH(__nv_bfloat16);
+  else ARGMAX_LAUNCH(__half);
+#undef ARGMAX_LAUNCH
   count_launch();
   return check_cuda(cudaGetLastError(), "neb_argmax launch");
 }
