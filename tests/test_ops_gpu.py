@@ -182,6 +182,15 @@ def test_argmax_exact_with_ties(cuda, dtype, rows, cols):
     assert torch.equal(got.cpu(), x.argmax(-1))
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_argmax_nan_wins_first(cuda, dtype):
+    x = torch.randn(4, 32000, generator=torch.Generator().manual_seed(6)).to(dtype)
+    x[1, 777] = float("nan")
+    x[1, 20000] = float("nan")
+    x[2, 31999] = float("inf")
+    assert torch.equal(nops.argmax(x.to(cuda)).cpu(), x.argmax(-1))
+
+
 def test_add_rounding(cuda):
     g = torch.Generator().manual_seed(4)
     a = torch.randn(1000, generator=g).to(torch.bfloat16)
