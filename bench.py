@@ -18,7 +18,13 @@ JSON line keys (one line on rank 0):
   roofline     the decode step's dominant kernel family (HBM): algorithmic bytes /
                CUDA-event time of that family's launches replayed from a graph;
                roofline_other the other family, roofline_step the whole step
-  gemm         fused linear+GELU GEMM TFLOP/s at 8192^3 bf16 (N=1)
+  parity       16 greedy steps of the full model checked before timing against
+               the reference's TinyDecoder (fp32 CPU, bf16-rounded weights):
+               max relative logit error, greedy agreement; failing exits 1
+  budget       the step's time split among the GEMM, attention and (all ranks
+               at once) TP all-reduce families
+  gemm         fused linear+GELU GEMM TFLOP/s at 8192^3 bf16 (N=1), output
+               rows checked against torch fp32
   forgeml      configs 1-3 on the native kernels: compiled MLP and encoder
                block, GEMM sweep (N=1)
   cpu_baseline the reference's own CPU implementation of the decode step (its
@@ -829,10 +835,23 @@ def run_c5(args) -> None:
 
     from forgeml_b200.nebula import AsyncBatcher, DecoderConfig, Engine, ParallelContext
 
+    from forgeml_b200.nebula.runtime import ShardedDecoder
+
     world = int(os.environ.get("WORLD_SIZE", "1"))
     pp = 2 if world % 2 == 0 and world >= 2 else 1
     tp = world // pp
     ctx = ParallelContext.from_env(tp_size=tp, pp_size=pp, device="cuda", timeout_s=300.0)
+    # parity first, on a 2-layer slice of the config-5 geometry over the same
+    # TP x PP layout (the full 32-layer model is too large for the CPU check)
+    parity = None
+    if not args.no_parity:
+        slice_cfg = DecoderConfig(**{**C5, "num_layers": 2 * pp})
+        dec = ShardedDecoder(slice_cfg, ctx, dtype=torch.bfloat16, max_requests=8, init="normal")
+        parity = decode_parity(dec, ctx.device, batch=8, prompt_len=16, steps=8, checker=ctx.rank == 0)
+        dec.close()
+        del dec
+        torch.cuda.synchronize()
+        dist.barrier()
     cfg = DecoderConfig(**C5)
     engine = Engine(cfg, context=ctx, dtype=torch.bfloat16, max_requests=64, init="normal")
     if ctx.rank != 0:
@@ -881,7 +900,7 @@ def run_c5(args) -> None:
                        "arrivals": "poisson 64 req/s (seeded)", "prompt_len": "uniform [128, 2048]",
                        "batch_cap": 64, "batching": "equal-length cohorts" if args.c5_cohorts
                        else "mixed prompt lengths (generate_mixed)", "window_ms": args.c5_window_ms},
-            "wall_s": wall, "generated_tokens": total,
+            "wall_s": wall, "generated_tokens": total, "parity": parity,
             "latency_s": {"p50": lat[len(lat) // 2], "p90": lat[int(len(lat) * 0.9)], "max": lat[-1]}}
     print(json.dumps(line), flush=True)
     torch.cuda.synchronize()
