@@ -15,6 +15,8 @@ JSON line keys (one line on rank 0):
   value        decode tokens/s, device-timed (CUDA events, max over ranks)
   e2e          the same metric through Engine.forward with the step's tokens
                copied from pinned host memory and the argmax ids read back
+  generate     the workload's whole 128-token generation through
+               Engine.generate (prefill + contexts 513..640), wall clock
   roofline     the decode step's dominant kernel family (HBM): algorithmic bytes /
                CUDA-event time of that family's launches replayed from a graph;
                roofline_other the other family, roofline_step the whole step
@@ -771,14 +773,26 @@ def run_native(args) -> None:
             torch.cuda.synchronize(dev)
             e2e_s = time.perf_counter() - t0
             engine.release(ids)
+            # the workload's whole generation: prefill of every prompt, then
+            # NEW_TOKENS greedy steps over contexts PROMPT+1 .. PROMPT+NEW_TOKENS
+            host_prompts = prompts.tolist()
+            torch.cuda.synchronize(dev)
+            t0 = time.perf_counter()
+            outs = engine.generate(host_prompts, NEW_TOKENS)
+            gen_s = time.perf_counter() - t0
         e2e = {"value": BATCH * K / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": BATCH * 8,
                "d2h_bytes_per_step": BATCH * 8,
                "path": "Engine.forward(host int64 tokens) + native argmax + D2H ids, per step"
                        + ("" if world == 1 else "; leader drives workers through the command protocol")}
+        generate = {"tokens_per_s": sum(len(o) for o in outs) / gen_s, "wall_s": gen_s, "new_tokens": NEW_TOKENS,
+                    "batch": BATCH, "context": [PROMPT + 1, PROMPT + NEW_TOKENS],
+                    "path": "Engine.generate(host prompts): prefill of every prompt + greedy decode, wall clock"}
     else:
         engine.serve()
 
     extra = {}
+    if rank == 0:
+        extra["generate"] = generate
     if rank == 0:
         with torch.inference_mode():
             extra.update(kernel_rooflines(engine, dev, PROMPT + W + K, ms / K, ar_family))

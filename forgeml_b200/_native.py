@@ -92,6 +92,16 @@ _SIGNATURES = {
         [_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I, _I,
          ctypes.POINTER(fml_tile_cfg), _P, ctypes.c_size_t, _P],
     ),
+    "fml_gemm_packed_b_bytes": (ctypes.c_size_t, [_I64, _I64, _I]),
+    "fml_gemm_pack_b": (_I, [_P, _I64, _I64, _I64, _I64, _I, _P, ctypes.c_size_t, _P]),
+    "fml_gemm_packed_b_workspace_size": (
+        ctypes.c_size_t, [_I64, _I64, _I64, _I, _I64, _I64, _P, ctypes.POINTER(fml_tile_cfg)]
+    ),
+    "fml_gemm_packed_b": (
+        _I,
+        [_P, _I64, _I64, _P, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I, _I,
+         ctypes.POINTER(fml_tile_cfg), _P, ctypes.c_size_t, _P],
+    ),
     "fml_gemm_noalloc": (
         _I,
         [_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I, _I,

@@ -1293,7 +1293,14 @@ struct Operand {
   bool pack;     // needs a packed copy in workspace
   size_t ws_off; // workspace offset of the packed copy
   long long kp;  // padded row length of the packed copy (elements)
+  const void* pre = nullptr;  // caller-packed 3xTF32 image (fml_gemm_packed_b), read directly
 };
+
+// 3xTF32 split layout of one operand (pack_kernel modes): the A operand is
+// stored [lo | hi | hi] and the B operand [hi | lo | hi] along K, so the
+// product over the tripled K is A_lo B_hi + A_hi B_lo + A_hi B_hi whichever
+// operand the plan puts in the 128-row (P) position.
+static inline int split_mode(bool is_b, int dtype) { return dtype == FML_F32 ? (is_b ? 2 : 1) : 0; }
 
 static inline long long round_up(long long v, long long m) { return (v + m - 1) / m * m; }
 
@@ -1540,7 +1547,7 @@ static int pick_bn(const Plan& pl, long long I, long long J, const fml_tile_cfg*
 
 static int make_plan(Plan& pl, const void* a, long long lda_m, long long lda_k, const void* b,
                      long long ldb_k, long long ldb_n, long long M, long long N, long long K,
-                     int dtype, const fml_tile_cfg* cfg, int sms) {
+                     int dtype, const fml_tile_cfg* cfg, int sms, const void* b_pre = nullptr) {
   pl.packed = false;
   pl.swap = (M <= 128 && N > M);
   if (pl.swap) {
@@ -1558,6 +1565,13 @@ static int make_plan(Plan& pl, const void* a, long long lda_m, long long lda_k, 
   const long long es = (long long)dtype_size(dtype);
   const long long kp = round_up(K, 16 / es);
   pl.keff = dtype == FML_F32 ? 3 * kp : K;
+  if (b_pre) {  // fp32 B already split by fml_gemm_pack_b
+    Operand& bo = pl.swap ? pl.P : pl.Q;
+    bo.pack = false;
+    bo.mn = false;
+    bo.pre = b_pre;
+    bo.kp = kp;
+  }
   size_t ws = 0;
   for (Operand* o : {&pl.P, &pl.Q}) {
     if (!o->pack) continue;
@@ -1758,8 +1772,9 @@ struct PlanKey {
   long long v[7];  // lda_m, lda_k, ldb_k, ldb_n, m, n, k
   int dtype, dev;
   int cfg[5];      // -1 when no tile hint
+  bool b_pre = false;  // b is a caller-packed 3xTF32 image
   bool operator==(const PlanKey& o) const {
-    if (a != o.a || b != o.b || ws != o.ws || dtype != o.dtype || dev != o.dev) return false;
+    if (a != o.a || b != o.b || ws != o.ws || dtype != o.dtype || dev != o.dev || b_pre != o.b_pre) return false;
     for (int i = 0; i < 7; ++i)
       if (v[i] != o.v[i]) return false;
     for (int i = 0; i < 5; ++i)
@@ -1833,11 +1848,12 @@ extern "C" size_t fml_gemm_workspace_size(int64_t m, int64_t n, int64_t k, int d
   return pl.ws_bytes;
 }
 
-extern "C" int fml_gemm(const void* a, int64_t lda_m, int64_t lda_k, const void* b,
-                        int64_t ldb_k, int64_t ldb_n, const void* bias, int64_t bias_stride,
-                        const void* residual, int64_t ldr, void* c, int64_t ldc, int64_t m,
-                        int64_t n, int64_t k, int dtype, int act, const fml_tile_cfg* cfg,
-                        void* workspace, size_t workspace_bytes, void* stream) {
+// Shared body of fml_gemm and fml_gemm_packed_b (b_pre: B's caller-packed
+// 3xTF32 image, or null).
+static int gemm_entry(const void* a, int64_t lda_m, int64_t lda_k, const void* b, int64_t ldb_k, int64_t ldb_n,
+                      const void* b_pre, const void* bias, int64_t bias_stride, const void* residual, int64_t ldr,
+                      void* c, int64_t ldc, int64_t m, int64_t n, int64_t k, int dtype, int act,
+                      const fml_tile_cfg* cfg, void* workspace, size_t workspace_bytes, void* stream) {
   int rc = validate_gemm(a, b, c, m, n, k, dtype);
   if (rc) return rc;
   if (act < 0 || act > 2) return fail(FML_EINVAL, "gemm: act must be 0 (none), 1 (erf) or 2 (tanh)");
@@ -1850,20 +1866,22 @@ extern "C" int fml_gemm(const void* a, int64_t lda_m, int64_t lda_k, const void*
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int dev = current_device();
   const int sms = num_sms(dev);
-  const PlanKey key = plan_key(a, lda_m, lda_k, b, ldb_k, ldb_n, m, n, k, dtype, cfg, dev, workspace);
+  PlanKey key = plan_key(a, lda_m, lda_k, b, ldb_k, ldb_n, m, n, k, dtype, cfg, dev, workspace);
+  key.b_pre = b_pre != nullptr;
   CachedPlan hit;
   if (plan_cache_get(key, hit)) {
     // A repeated call (same operands, layout and workspace): the plan and
     // both tensor maps are the ones built before; only the packing kernels
     // (operand contents may have changed) and the launch run again.
-    const bool tf32 = dtype == FML_F32;
-    if (hit.pl.P.pack && (rc = pack_operand(hit.pl.P, dtype, tf32 ? 1 : 0, workspace, st))) return rc;
-    if (hit.pl.Q.pack && (rc = pack_operand(hit.pl.Q, dtype, tf32 ? 2 : 0, workspace, st))) return rc;
+    if (hit.pl.P.pack && (rc = pack_operand(hit.pl.P, dtype, split_mode(hit.pl.swap, dtype), workspace, st)))
+      return rc;
+    if (hit.pl.Q.pack && (rc = pack_operand(hit.pl.Q, dtype, split_mode(!hit.pl.swap, dtype), workspace, st)))
+      return rc;
     return launch_plan(hit.pl, hit.mp, hit.mq, dtype, act, bias, bias_stride, residual, ldr, c, ldc, m, n, nullptr,
                        sms, st);
   }
   Plan pl;
-  rc = make_plan(pl, a, lda_m, lda_k, b, ldb_k, ldb_n, m, n, k, dtype, cfg, sms);
+  rc = make_plan(pl, a, lda_m, lda_k, b, ldb_k, ldb_n, m, n, k, dtype, cfg, sms, b_pre);
   if (rc) return rc;
   if (pl.ws_bytes > 0 && (workspace == nullptr || workspace_bytes < pl.ws_bytes))
     return fail(FML_EWORKSPACE, "gemm: workspace of " + std::to_string(pl.ws_bytes) +
@@ -1873,11 +1891,11 @@ extern "C" int fml_gemm(const void* a, int64_t lda_m, int64_t lda_k, const void*
   const bool tf32 = dtype == FML_F32;
   // Pack operands that TMA cannot read directly.
   if (pl.P.pack) {
-    rc = pack_operand(pl.P, dtype, tf32 ? 1 : 0, workspace, st);
+    rc = pack_operand(pl.P, dtype, split_mode(pl.swap, dtype), workspace, st);
     if (rc) return rc;
   }
   if (pl.Q.pack) {
-    rc = pack_operand(pl.Q, dtype, tf32 ? 2 : 0, workspace, st);
+    rc = pack_operand(pl.Q, dtype, split_mode(!pl.swap, dtype), workspace, st);
     if (rc) return rc;
   }
   CUtensorMap mp, mq;
@@ -1885,7 +1903,9 @@ extern "C" int fml_gemm(const void* a, int64_t lda_m, int64_t lda_k, const void*
     Operand& o = w == 0 ? pl.P : pl.Q;
     CUtensorMap* map = w == 0 ? &mp : &mq;
     const int box_rows = w == 0 ? kBM : (pl.pair ? pl.bn / 2 : pl.bn);
-    if (o.pack) {
+    if (o.pre) {
+      rc = encode(map, o.pre, dtype, tf32, false, o.rows, pl.keff, 3 * o.kp, box_rows);
+    } else if (o.pack) {
       const void* ptr = static_cast<uint8_t*>(workspace) + o.ws_off;
       rc = encode(map, ptr, dtype, tf32, false, o.rows, pl.keff, tf32 ? 3 * o.kp : o.kp,
                   box_rows);
@@ -1898,6 +1918,60 @@ extern "C" int fml_gemm(const void* a, int64_t lda_m, int64_t lda_k, const void*
   }
   plan_cache_put(key, pl, mp, mq);
   return launch_plan(pl, mp, mq, dtype, act, bias, bias_stride, residual, ldr, c, ldc, m, n, nullptr, sms, st);
+}
+
+extern "C" int fml_gemm(const void* a, int64_t lda_m, int64_t lda_k, const void* b,
+                        int64_t ldb_k, int64_t ldb_n, const void* bias, int64_t bias_stride,
+                        const void* residual, int64_t ldr, void* c, int64_t ldc, int64_t m,
+                        int64_t n, int64_t k, int dtype, int act, const fml_tile_cfg* cfg,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  return gemm_entry(a, lda_m, lda_k, b, ldb_k, ldb_n, nullptr, bias, bias_stride, residual, ldr, c, ldc, m, n, k,
+                    dtype, act, cfg, workspace, workspace_bytes, stream);
+}
+
+// ---------------------------------------------------------------------------
+// fp32 constant B operands split once (3xTF32 image [N, 3*Kp], hi|lo|hi).
+// ---------------------------------------------------------------------------
+static long long f32_kp(long long k) { return round_up(k, 4); }
+
+extern "C" size_t fml_gemm_packed_b_bytes(int64_t n, int64_t k, int dtype) {
+  if (dtype != FML_F32 || n <= 0 || k <= 0) return 0;
+  return (size_t)round_up(n * 3 * f32_kp(k) * 4, 256);
+}
+
+extern "C" int fml_gemm_pack_b(const void* b, int64_t ldb_k, int64_t ldb_n, int64_t k, int64_t n, int dtype,
+                               void* dst, size_t dst_bytes, void* stream) {
+  if (dtype != FML_F32) return fail(FML_EUNSUPPORTED, "gemm_pack_b: fp32 only (16-bit B needs no split)");
+  if (!b || !dst) return fail(FML_EINVAL, "gemm_pack_b: null pointer");
+  if (n <= 0 || k <= 0) return fail(FML_EINVAL, "gemm_pack_b: N and K must be positive");
+  if (n > (1ll << 31) - 1 || k > (1ll << 31) - 1) return fail(FML_EUNSUPPORTED, "gemm_pack_b: dimension exceeds int32");
+  if (reinterpret_cast<uintptr_t>(dst) % 256 != 0) return fail(FML_EINVAL, "gemm_pack_b: dst must be 256-byte aligned");
+  if (dst_bytes < fml_gemm_packed_b_bytes(n, k, dtype))
+    return fail(FML_EINVAL, "gemm_pack_b: dst smaller than fml_gemm_packed_b_bytes");
+  Operand o{b, ldb_n, ldb_k, n, k, false, true, 0, f32_kp(k)};
+  return pack_operand(o, dtype, split_mode(true, dtype), dst, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t fml_gemm_packed_b_workspace_size(int64_t m, int64_t n, int64_t k, int dtype, int64_t lda_m,
+                                                   int64_t lda_k, const void* a, const fml_tile_cfg* cfg) {
+  if (dtype != FML_F32 || m <= 0 || n <= 0 || k <= 0) return 0;
+  Plan pl;
+  const void* ap = a ? a : reinterpret_cast<const void*>(uintptr_t(256));
+  const void* bp = reinterpret_cast<const void*>(uintptr_t(256));
+  if (make_plan(pl, ap, lda_m, lda_k, bp, 0, 0, m, n, k, dtype, cfg, num_sms(current_device()), bp) != FML_OK)
+    return 0;
+  return pl.ws_bytes;
+}
+
+extern "C" int fml_gemm_packed_b(const void* a, int64_t lda_m, int64_t lda_k, const void* b_packed,
+                                 const void* bias, int64_t bias_stride, const void* residual, int64_t ldr, void* c,
+                                 int64_t ldc, int64_t m, int64_t n, int64_t k, int dtype, int act,
+                                 const fml_tile_cfg* cfg, void* workspace, size_t workspace_bytes, void* stream) {
+  if (dtype != FML_F32) return fail(FML_EUNSUPPORTED, "gemm_packed_b: fp32 only");
+  if (b_packed && reinterpret_cast<uintptr_t>(b_packed) % 256 != 0)
+    return fail(FML_EINVAL, "gemm_packed_b: packed B must be 256-byte aligned");
+  return gemm_entry(a, lda_m, lda_k, b_packed, 0, 0, b_packed, bias, bias_stride, residual, ldr, c, ldc, m, n, k,
+                    dtype, act, cfg, workspace, workspace_bytes, stream);
 }
 
 static long long packed_kb(long long k, int dtype) { return (k * (long long)dtype_size(dtype) + kSlab - 1) / kSlab; }

@@ -292,7 +292,13 @@ class CompiledModel:
     def _gemm_launch(self, node) -> kernels.PreparedGemm:
         act = "gelu" if node.op == "fused_linear_gelu" else "none"
         approx = node.attrs.get("approximate", "none") if act == "gelu" else "none"
-        return kernels.PreparedGemm(node.spec.dtype, act, approx, self.kernel_configs.get(node.name, DEFAULT_CONFIG))
+        launch = kernels.PreparedGemm(node.spec.dtype, act, approx,
+                                      self.kernel_configs.get(node.name, DEFAULT_CONFIG))
+        w = self.graph.constants.get(node.inputs[1])
+        if w is not None and w.dtype == torch.float32 and w.is_cuda:
+            launch.pack_constant_b(w)  # a compiled fp32 weight is split into its 3xTF32 image once
+            torch.cuda.current_stream(w.device).synchronize()  # ready for calls on any stream
+        return launch
 
     def _native_step(self, node, arena_view, bshd: bool) -> Callable:
         op, attrs, spec = node.op, node.attrs, node.spec

@@ -164,6 +164,10 @@ def _launch_gemm(a, b, bias, out, act: int, config: KernelConfig, residual=None)
     del ws  # the caching allocator keeps it alive until the stream is done with it
 
 
+def _aligned(buf: torch.Tensor, align: int) -> int:
+    return (buf.data_ptr() + align - 1) // align * align
+
+
 class PreparedGemm:
     """A GEMM launch whose validation was done once (by the compiler, from the
     graph's specs): each call passes the current pointers straight to
@@ -185,10 +189,57 @@ class PreparedGemm:
             self.cfg = ctypes.byref(self._cfg_obj)
         self.lib = _native.load()
         self.ws: torch.Tensor | None = None
+        self._b_const: torch.Tensor | None = None  # fp32 constant B and its 3xTF32 image
+        self._b_image: torch.Tensor | None = None
+        self._b_version = -1
+
+    def pack_constant_b(self, b: torch.Tensor) -> None:
+        """Split a constant fp32 B [K, N] into its 3xTF32 image once
+        (fml_gemm_pack_b); calls with this tensor then split only A.  Other
+        dtypes read B directly and keep no image."""
+        if self.code != _native.dtype_code(torch.float32) or b.dtype != torch.float32 or not b.is_cuda:
+            return
+        k, n = b.shape
+        nbytes = int(self.lib.fml_gemm_packed_b_bytes(n, k, self.code))
+        img = torch.empty(nbytes + 256, dtype=torch.uint8, device=b.device)
+        with torch.cuda.device(b.device):
+            _native.call("fml_gemm_pack_b", b.data_ptr(), b.stride(0), b.stride(1), k, n, self.code,
+                         _aligned(img, 256), nbytes, torch.cuda.current_stream(b.device).cuda_stream)
+        self._b_const, self._b_image, self._b_version = b, img, b._version
+
+    def _packed_call(self, a, b, bias, out, residual) -> bool:
+        """Run on B's image when b is the packed constant (re-split first if
+        it was written in place since); False when b is another tensor."""
+        if b is not self._b_const:
+            return False
+        if b._version != self._b_version:
+            self.pack_constant_b(b)
+        m, k = a.shape
+        n = b.shape[1]
+        lib = self.lib
+        need = int(lib.fml_gemm_packed_b_workspace_size(m, n, k, self.code, a.stride(0), a.stride(1),
+                                                        a.data_ptr(), self.cfg))
+        ws_ptr = None
+        if need > 0:
+            if self.ws is None or self.ws.numel() < need + 256:
+                self.ws = torch.empty(need + 256, dtype=torch.uint8, device=a.device)
+            ws_ptr = _aligned(self.ws, 256)
+        rc = lib.fml_gemm_packed_b(a.data_ptr(), a.stride(0), a.stride(1), _aligned(self._b_image, 256),
+                                   bias.data_ptr() if bias is not None else None,
+                                   bias.stride(0) if bias is not None else 0,
+                                   residual.data_ptr() if residual is not None else None,
+                                   residual.stride(0) if residual is not None else 0,
+                                   out.data_ptr(), out.stride(0), m, n, k, self.code, self.act, self.cfg,
+                                   ws_ptr, need, torch.cuda.current_stream(a.device).cuda_stream)
+        if rc != 0:
+            raise GraphError(f"fml_gemm_packed_b failed ({rc}): {lib.fml_last_error().decode(errors='replace')}")
+        return True
 
     def __call__(self, a, b, bias, out, residual=None):
         if not (a.is_cuda and b.is_cuda and out.is_cuda):
             raise GraphError("native GEMM operands must be CUDA tensors")
+        if self._b_const is not None and self._packed_call(a, b, bias, out, residual):
+            return out
         m, k = a.shape
         n = b.shape[1]
         lib = self.lib
@@ -198,7 +249,7 @@ class PreparedGemm:
         if need > 0:
             if self.ws is None or self.ws.numel() < need + 256:
                 self.ws = torch.empty(need + 256, dtype=torch.uint8, device=a.device)
-            ws_ptr = (self.ws.data_ptr() + 255) // 256 * 256
+            ws_ptr = _aligned(self.ws, 256)
         rc = lib.fml_gemm(a.data_ptr(), a.stride(0), a.stride(1), b.data_ptr(), b.stride(0), b.stride(1),
                           bias.data_ptr() if bias is not None else None, bias.stride(0) if bias is not None else 0,
                           residual.data_ptr() if residual is not None else None,

@@ -91,6 +91,29 @@ FML_API int fml_gemm(const void* a, int64_t lda_m, int64_t lda_k,
              void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * fp32 GEMM with a constant B split once.  fml_gemm splits both fp32
+ * operands into their 3xTF32 images on every call; a compiled graph's
+ * weights never change, so fml_gemm_pack_b writes B's image once
+ * (fml_gemm_packed_b_bytes bytes at a 256-byte aligned dst; B[k,n] at
+ * b[k*ldb_k + n*ldb_n] as in fml_gemm) and fml_gemm_packed_b then runs the
+ * same product as fml_gemm on it, splitting only A (its workspace:
+ * fml_gemm_packed_b_workspace_size).  Same results as fml_gemm.  fp32 only
+ * (FML_EUNSUPPORTED otherwise).  An extension of the fml_gemm entry point
+ * (the reference's launch, src/forgeml/_triton.py:65-93) for the compiled
+ * dispatch of src/forgeml/compiler.py:93-126.
+ * ------------------------------------------------------------------------- */
+FML_API size_t fml_gemm_packed_b_bytes(int64_t n, int64_t k, int dtype);
+FML_API int fml_gemm_pack_b(const void* b, int64_t ldb_k, int64_t ldb_n, int64_t k, int64_t n, int dtype,
+                    void* dst, size_t dst_bytes, void* stream);
+FML_API size_t fml_gemm_packed_b_workspace_size(int64_t m, int64_t n, int64_t k, int dtype, int64_t lda_m,
+                                        int64_t lda_k, const void* a, const fml_tile_cfg* cfg);
+FML_API int fml_gemm_packed_b(const void* a, int64_t lda_m, int64_t lda_k, const void* b_packed,
+                      const void* bias, int64_t bias_stride, const void* residual, int64_t ldr,
+                      void* c, int64_t ldc, int64_t m, int64_t n, int64_t k,
+                      int dtype, int act, const fml_tile_cfg* cfg,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Allocation-free GEMM.  This entry point has no counterpart in the
  * reference; it exists for callers that cannot allocate device memory at the
  * call site -- for example a host runtime that reserves the GPU's memory up

@@ -167,3 +167,32 @@ def test_packed_linear(cuda, dtype, m, n, k, epi):
     want = matmul_epilogue(x, w.t(), bias, activation="gelu" if act else "none",
                            approximate="tanh" if act else "none", residual=r)
     close(out, want, dtype)
+
+
+@pytest.mark.parametrize("m,n,k", [(64, 2048, 512), (64, 512, 2048), (300, 700, 513), (4096, 768, 768),
+                                   (1, 1000, 33)])
+@pytest.mark.parametrize("epi", ["plain", "bias_gelu", "residual"])
+@pytest.mark.parametrize("layout", ["linear_t", "row_major"])
+def test_packed_b_fp32(cuda, m, n, k, epi, layout):
+    """fp32 B split once (fml_gemm_pack_b) then used by fml_gemm_packed_b:
+    same product as fml_gemm, checked against the oracle at the fp32 bar;
+    a B written in place is split again before the next call."""
+    g = torch.Generator().manual_seed(m + 3 * n + 11 * k)
+    a_cpu = torch.rand(m, k, generator=g) * 2 - 1
+    w_cpu = torch.rand(n, k, generator=g) * 2 - 1
+    b_cpu = w_cpu.t() if layout == "linear_t" else w_cpu.t().contiguous()
+    bias_cpu = torch.randn(n, generator=g) if epi != "plain" else None
+    res_cpu = torch.randn(m, n, generator=g) if epi == "residual" else None
+    act = "gelu" if epi == "bias_gelu" else "none"
+    b = w_cpu.to(cuda).t() if layout == "linear_t" else b_cpu.to(cuda)
+    launch = kernels.PreparedGemm(torch.float32, act)
+    launch.pack_constant_b(b)
+    out = torch.empty(m, n, device=cuda)
+    args = (a_cpu.to(cuda), b, None if bias_cpu is None else bias_cpu.to(cuda), out)
+    launch(*args, residual=None if res_cpu is None else res_cpu.to(cuda))
+    want = matmul_epilogue(a_cpu, b_cpu, bias_cpu, activation=act, residual=res_cpu)
+    close(out, want, torch.float32)
+    b.mul_(0.5)  # in place: the image must follow
+    launch(*args, residual=None if res_cpu is None else res_cpu.to(cuda))
+    want = matmul_epilogue(a_cpu, b_cpu * 0.5, bias_cpu, activation=act, residual=res_cpu)
+    close(out, want, torch.float32)
