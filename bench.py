@@ -935,6 +935,8 @@ def run_case(args) -> None:
                  shard of --tp ranks: LayerNorm-folded QKV + KV append, o,
                  folded up + tanh GELU, down (residuals at TP1)
     gemm         8192^3 bf16 + bias + GELU
+    c2           the compiled config-2 encoder block (bf16, then fp32): every
+                 instruction's device time alone and the whole call
     """
     from forgeml_b200.forgeml import kernels
     from forgeml_b200.nebula import ops
@@ -1025,6 +1027,20 @@ def run_case(args) -> None:
         res["chain_avg_us"] = us_chain
     elif args.case == "gemm":
         res["gemm"] = gemm_headline(dev)
+    elif args.case == "c2":
+        # the compiled config-2 encoder block: each instruction's device time
+        # alone (CompiledModel.node_times) and the whole call from a graph
+        from forgeml_b200.forgeml import compile as fml_compile
+        from forgeml_b200.workloads import make_c2_block
+
+        for dt, name in ((torch.bfloat16, "c2_block_bf16"), (torch.float32, "c2_block_fp32")):
+            m, x = make_c2_block(dtype=dt)
+            c = fml_compile(m.to(dev, dt), (x.to(dev),), backend="triton")
+            xd = x.to(dev)
+            with torch.inference_mode():
+                us = _graph_time_us([lambda: c(xd)] * max(1, reps)) / max(1, reps)
+                nodes = {k: round(v * 1e3, 2) for k, v in c.node_times(xd, repeats=max(1, reps)).items()}
+            res[name] = {"us": us, "tflops": 64.42e9 / (us * 1e-6) / 1e12, "node_us": nodes}
     print(json.dumps({"case": args.case, "results": res}), flush=True)
 
 
@@ -1040,7 +1056,7 @@ def main() -> None:
     ap.add_argument("--cpu-steps", type=int, default=3)
     ap.add_argument("--cpu-layers", type=int, default=None, help="time this many layers of the CPU oracle")
     ap.add_argument("--tp", type=int, default=1, help="--case gemm-fused: TP shard shapes of this degree")
-    ap.add_argument("--case", choices=("attention", "gemm-decode", "gemm-fused", "gemm"), default=None,
+    ap.add_argument("--case", choices=("attention", "gemm-decode", "gemm-fused", "gemm", "c2"), default=None,
                     help="run one kernel micro-benchmark instead of the decode bench")
     ap.add_argument("--workload", choices=("c4", "c5"), default="c4",
                     help="c5: serve config 5 through the AsyncBatcher over TP x PP (launch with torchrun)")

@@ -145,6 +145,22 @@ __device__ __forceinline__ uint32_t bar_ln(const Smem& s) {
 constexpr int kNumBars = 2 * kMaxStages + 8;
 constexpr int kBarBytes = 8 * kNumBars + 16;  // + tmem holder
 
+// Wide tiles (BN >= 128, 16-bit, not fused) add four epilogue helper warps
+// (warps 9-12, TMEM lane quadrant = warp % 4): without a split-K reduction
+// a tile's columns are shared between the four epilogue warps (first half)
+// and the helpers (second half).  One warp per quadrant and SM sub-partition
+// leaves the epilogue latency-bound; at short K (a few dozen slabs) that
+// epilogue, not the main loop, sets the tile rate.
+constexpr int kHelperWarp0 = 9;
+template <int BN, bool PROMOTE, bool FUSED>
+struct EpiHelp {
+  static constexpr bool on = BN >= 128 && !PROMOTE && !FUSED;
+};
+template <int BN, bool PROMOTE, bool FUSED>
+constexpr int threads_of() {
+  return EpiHelp<BN, PROMOTE, FUSED>::on ? kThreads + 128 : kThreads;
+}
+
 __device__ __forceinline__ void tile_coords(const Params& p, int t, int& ti, int& tj) {
   int per_group = p.group_i * p.tiles_j;
   int g = t / per_group;
@@ -238,6 +254,28 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int i, int j, fl
   else reinterpret_cast<__half*>(p.out)[off] = __float2half_rn(x);
 }
 
+// Eight consecutive 16-bit bias values bias[n0 .. n0+7] as floats: one
+// 16-byte load when the bias is contiguous and aligned there.
+__device__ __forceinline__ void load_bias8(const Params& p, int n0, float (&bv)[8]) {
+  const bool bf = p.out_dtype == FML_BF16;
+  const uint16_t* bb = reinterpret_cast<const uint16_t*>(p.bias);
+  auto cvt = [&](uint32_t h) {
+    return bf ? __uint_as_float(h << 16) : __half2float(__ushort_as_half((unsigned short)h));
+  };
+  if (p.bias_stride == 1 && (reinterpret_cast<uintptr_t>(bb + n0) & 15) == 0) {
+    const uint4 r = *reinterpret_cast<const uint4*>(bb + n0);
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      bv[2 * i] = cvt(w[i] & 0xffffu);
+      bv[2 * i + 1] = cvt(w[i] >> 16);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) bv[e] = cvt(bb[(long long)(n0 + e) * p.bias_stride]);
+  }
+}
+
 // Fast path: 32 consecutive output columns of one row (non-swap), 16-bit
 // output, no residual, aligned.  Applies the same per-element contract.
 __device__ __forceinline__ bool epilogue_row32_fast(const Params& p, int m, int n0,
@@ -248,22 +286,14 @@ __device__ __forceinline__ bool epilogue_row32_fast(const Params& p, int m, int 
   if ((off & 7) != 0 || (reinterpret_cast<uintptr_t>(p.out) & 15) != 0) return false;
   const int od = p.out_dtype;
   uint32_t packed[16];
+  float bv[8];
 #pragma unroll
   for (int e = 0; e < 32; e += 2) {
+    if (p.bias != nullptr && (e & 7) == 0) load_bias8(p, n0 + e, bv);
     float x0 = round_to(v[e], od), x1 = round_to(v[e + 1], od);
     if (p.bias != nullptr) {
-      float b0, b1;
-      if (od == FML_BF16) {
-        const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(p.bias);
-        b0 = __bfloat162float(bb[(n0 + e) * p.bias_stride]);
-        b1 = __bfloat162float(bb[(n0 + e + 1) * p.bias_stride]);
-      } else {
-        const __half* bb = reinterpret_cast<const __half*>(p.bias);
-        b0 = __half2float(bb[(n0 + e) * p.bias_stride]);
-        b1 = __half2float(bb[(n0 + e + 1) * p.bias_stride]);
-      }
-      x0 = round_to(x0 + b0, od);
-      x1 = round_to(x1 + b1, od);
+      x0 = round_to(x0 + bv[e & 7], od);
+      x1 = round_to(x1 + bv[(e & 7) + 1], od);
     }
     if (p.act == FML_ACT_GELU_ERF) { x0 = gelu_erf(x0); x1 = gelu_erf(x1); }
     else if (p.act == FML_ACT_GELU_TANH) { x0 = gelu_tanh(x0); x1 = gelu_tanh(x1); }
@@ -359,10 +389,11 @@ __device__ __forceinline__ uint4 pack8_16(const float (&x)[8], bool bf) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// Eight consecutive outputs (m, n0..n0+7) from the split-K buffer with the
-// epilogue contract of epilogue_store.  16-bit outputs with 16-byte aligned
-// rows take a straight-line path: round, bias, GELU, residual (one 16-byte
-// load) and one 16-byte store; GELU runs in a rolled loop that rotates the
+// Eight consecutive outputs (m, n0..n0+7) with the epilogue contract of
+// epilogue_store (from the split-K buffer, or from TMEM for tiles whose
+// epilogue has a residual or an fp32 output).  Outputs with 16-byte aligned
+// rows take a straight-line path: round, bias, GELU, residual (16-byte
+// loads) and 16-byte stores; GELU runs in a rolled loop that rotates the
 // eight registers (one copy of its code, nothing indexed dynamically, so
 // nothing goes to local memory).  Other cases store element by element.
 __device__ __forceinline__ void epilogue_store8(const Params& p, int m, int n0, float (&x)[8]) {
@@ -370,9 +401,10 @@ __device__ __forceinline__ void epilogue_store8(const Params& p, int m, int n0, 
   const int od = p.out_dtype;
   const long long off = (long long)m * p.ldo + n0;
   const long long roff = (long long)m * p.ldr + n0;
-  const bool vec = od != FML_F32 && n0 + 8 <= p.cols_out && (off & 7) == 0 &&
-                   (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 &&
-                   (p.residual == nullptr || ((roff & 7) == 0 && (reinterpret_cast<uintptr_t>(p.residual) & 15) == 0));
+  const long long ve = od == FML_F32 ? 4 : 8;  // elements per 16 bytes
+  const bool vec = n0 + 8 <= p.cols_out && (off % ve) == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 &&
+                   (p.residual == nullptr ||
+                    ((roff % ve) == 0 && (reinterpret_cast<uintptr_t>(p.residual) & 15) == 0));
   if (!vec) {
 #pragma unroll 1
     for (int e = 0; e < 8; ++e) {
@@ -392,9 +424,15 @@ __device__ __forceinline__ void epilogue_store8(const Params& p, int m, int n0, 
 #pragma unroll
   for (int e = 0; e < 8; ++e) x[e] = round_to(x[e], od);
   if (p.bias != nullptr) {
-    const uint16_t* bb = reinterpret_cast<const uint16_t*>(p.bias);
+    if (od == FML_F32) {
+      const float* bb = reinterpret_cast<const float*>(p.bias);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) x[e] = round_to(x[e] + h2f(bb[(long long)(n0 + e) * p.bias_stride], bf), od);
+      for (int e = 0; e < 8; ++e) x[e] = x[e] + bb[(long long)(n0 + e) * p.bias_stride];
+    } else {
+      const uint16_t* bb = reinterpret_cast<const uint16_t*>(p.bias);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = round_to(x[e] + h2f(bb[(long long)(n0 + e) * p.bias_stride], bf), od);
+    }
   }
   if (p.act != FML_ACT_NONE) {
     const bool erf_act = p.act == FML_ACT_GELU_ERF;
@@ -405,6 +443,18 @@ __device__ __forceinline__ void epilogue_store8(const Params& p, int m, int n0, 
       for (int i = 0; i < 7; ++i) x[i] = x[i + 1];
       x[7] = g;
     }
+  }
+  if (od == FML_F32) {
+    if (p.residual != nullptr) {
+      const float4* rp = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.residual) + roff);
+      const float4 r0 = rp[0], r1 = rp[1];
+      x[0] += r0.x; x[1] += r0.y; x[2] += r0.z; x[3] += r0.w;
+      x[4] += r1.x; x[5] += r1.y; x[6] += r1.z; x[7] += r1.w;
+    }
+    float4* op = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + off);
+    op[0] = make_float4(x[0], x[1], x[2], x[3]);
+    op[1] = make_float4(x[4], x[5], x[6], x[7]);
+    return;
   }
   if (p.residual != nullptr) {
     const uint4 rv = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.residual) + roff);
@@ -742,7 +792,7 @@ __device__ bool ar_exchange(const Params& p, const Smem& s, int ti, int r0, int 
 // all-reduce epilogues (pre-packed 16-bit P, swapped, one tile per cluster,
 // always through the split-K reduction buffer).
 template <int BN, bool PROMOTE, bool PAIR = false, bool FUSED = false>
-__global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
+__global__ void __launch_bounds__(threads_of<BN, PROMOTE, FUSED>(), (BN <= 64 && !PROMOTE) ? 2 : 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
                 const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -773,6 +823,8 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
   const int kb_begin = PAIR ? 0 : (int)((long long)crank * p.num_kb / ksplit);
   const int kb_end = PAIR ? p.num_kb : (int)((long long)(crank + 1) * p.num_kb / ksplit);
   (void)kClusterLaunch;
+  constexpr bool kHelp = EpiHelp<BN, PROMOTE, FUSED>::on;
+  const bool help_on = kHelp && ksplit == 1;  // split-K tiles reduce through the 4-warp path
 
   constexpr int kAccStride = BN < 32 ? 32 : BN;
   constexpr int kTmemCols = (2 * kAccStride <= 32) ? 32
@@ -787,7 +839,8 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(bar_tfull(s, a), 1);
-      mbar_init(bar_tempty(s, a), PAIR ? 8 : 4);  // a pair's leader hears both CTAs' epilogues
+      // a pair's leader hears both CTAs' epilogues (and helpers)
+      mbar_init(bar_tempty(s, a), (PAIR ? 8 : 4) * (help_on ? 2 : 1));
     }
     mbar_init(bar_recv(s), 1);
     mbar_init(bar_ln(s), 1);
@@ -817,7 +870,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
   const int mn_box = kSlab / p.esize;         // MN elements per MN-major box
   const uint32_t slab_box_bytes = (uint32_t)bke * kSlab;  // bytes of one MN-major box
 
-  if (warp >= kProducerWarp0) {
+  if (warp >= kProducerWarp0 && warp < kHelperWarp0) {
     // ------------------------------------------------------------ producers
     // Four warps: P or Q operand x even or odd pipeline steps.  A warp's
     // bulk/TMA copies are processed one after another (about a memory
@@ -991,13 +1044,17 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
     // ------------------------------------------------------------ epilogue
     pdl_wait();  // bias / residual / output may belong to the previous grid
     pdl_trigger();
-    const int quad = warp;                  // TMEM lane quadrant of this warp
+    const bool helper = kHelp && warp >= kHelperWarp0;
+    const bool idle = helper && !help_on;
+    const int quad = warp & 3;              // TMEM lane quadrant of this warp
     const int row = quad * 32 + lane;       // MMA row within the tile
-    const int ep_tid = threadIdx.x;         // 0..127
+    const int ep_tid = threadIdx.x;         // 0..127 (helpers: 288..415, no shared-buffer work)
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
     constexpr int kChunks = (BN + 31) / 32;
+    const int c_begin = helper ? kChunks / 2 : 0;               // this warp's 32-column chunks
+    const int c_end = (help_on && !helper) ? kChunks / 2 : kChunks;
     float* red = reinterpret_cast<float*>(smem_raw + (s.red - smem_u32(smem_raw)));
     // Split-K (one tile per cluster): rows [crank*rows_per, +rows_per) of the
     // tile are owned by this CTA.  Every CTA pushes its partial of each row
@@ -1026,7 +1083,7 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
       if (p.ln_mode == 2 && cluster_id < p.num_tiles)
         ok = epi_bar_and(ln_stats<BN>(p, s, ksplit, crank, kb_begin, kb_end, ep_tid));
     }
-    for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
+    for (int t = cluster_id; t < p.num_tiles && ok && !idle; t += num_clusters) {
       int ti, tj;
       tile_coords(p, t, ti, tj);
       const int i = ti * kTileM + prank * kBM + row;
@@ -1057,10 +1114,10 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
           }
         } else {
 #pragma unroll 1
-          for (int c = 0; c < kChunks; ++c) {
+          for (int c = c_begin; c < c_end; ++c) {
             float v[32];
             tmem_ld32(tbase + c * 32, v);
-            if (c == kChunks - 1) {
+            if (c == c_end - 1) {
               tc_fence_before();
               __syncwarp();
               if (lane == 0) {
@@ -1072,8 +1129,28 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
             if (!use_red) {
               const int j0 = tj * BN + c * 32;
               if (nvalid == 32 && epilogue_row32_fast(p, i, j0, v)) continue;
+              if (!p.swap) {
+                // residual or fp32 output: 16-byte vectors of eight columns
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  if (8 * q < nvalid) {
+                    float x[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) x[e] = v[8 * q + e];
+                    epilogue_store8(p, i, j0 + 8 * q, x);
+                  }
+                }
+              } else {
+                // swapped: MMA row i is an output column, the 32 values are
+                // 32 output rows; a rolled loop that rotates the registers
 #pragma unroll 1
-              for (int e = 0; e < nvalid; ++e) epilogue_store(p, i, j0 + e, v[e]);
+                for (int e = 0; e < nvalid; ++e) {
+                  const float v0 = v[0];
+#pragma unroll
+                  for (int k = 0; k < 31; ++k) v[k] = v[k + 1];
+                  epilogue_store(p, i, j0 + e, v0);
+                }
+              }
             } else {
 #pragma unroll
               for (int q = 0; q < 8; ++q)
@@ -1085,9 +1162,25 @@ __global__ void __launch_bounds__(kThreads, (BN <= 64 && !PROMOTE) ? 2 : 1)
       }
       if (!ok) break;
       if (PROMOTE) {
-        if (!use_red) {
+        if (!use_red && !p.swap) {
+          // a row of BN consecutive output columns: 16-byte vectors of eight
+#pragma unroll
+          for (int q = 0; q < BN / 8; ++q) {
+            float x[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[e] = racc[8 * q + e];
+            epilogue_store8(p, i, tj * BN + 8 * q, x);
+          }
+        } else if (!use_red) {
+          // swapped: one output column, BN rows; a rolled loop that rotates
+          // the registers (nothing indexed dynamically, no local memory)
 #pragma unroll 1
-          for (int e = 0; e < BN; ++e) epilogue_store(p, i, tj * BN + e, racc[e]);
+          for (int e = 0; e < BN; ++e) {
+            const float v0 = racc[0];
+#pragma unroll
+            for (int k = 0; k < BN - 1; ++k) racc[k] = racc[k + 1];
+            epilogue_store(p, i, tj * BN + e, v0);
+          }
         } else {
 #pragma unroll
           for (int q = 0; q < BN / 4; ++q)
@@ -1404,13 +1497,14 @@ static int per_sm_ctas(int smem) {
   int dev = current_device(), smem_sm = 0;
   if (cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess || smem_sm <= 0)
     smem_sm = 233472;
-  const int warps = kThreads / 32;
+  constexpr int threads = threads_of<BN, PROMOTE, false>();
+  const int warps = threads / 32;
   const int regs_block = warps * ((fa.numRegs * 32 + 255) / 256) * 256;
   constexpr int acc = BN < 32 ? 32 : BN;
   constexpr int tmem_cols = (2 * acc <= 32) ? 32 : (2 * acc <= 64) ? 64 : (2 * acc <= 128) ? 128 : (2 * acc <= 256) ? 256 : 512;
   int n = smem_sm / (smem + (int)fa.sharedSizeBytes + 1024);
   n = std::min(n, 65536 / std::max(regs_block, 1));
-  n = std::min(n, 2048 / kThreads);
+  n = std::min(n, 2048 / threads);
   n = std::min(n, 512 / tmem_cols);
   return std::max(n, 1);
 }
@@ -1424,7 +1518,7 @@ static int resident_ctas_t(int ksplit, int smem, int sms) {
   // inside a GPC) scaled by the CTAs an SM really holds.
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(ksplit);
-  lc.blockDim = dim3(kThreads);
+  lc.blockDim = dim3(threads_of<BN, PROMOTE, false>());
   lc.dynamicSmemBytes = smem;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1614,7 +1708,7 @@ static int launch_bn(const CUtensorMap& mp, const CUtensorMap& mq, const Params&
   if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(gemm)");
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(grid);
-  lc.blockDim = dim3(kThreads);
+  lc.blockDim = dim3(threads_of<BN, PROMOTE, FUSED>());
   lc.dynamicSmemBytes = smem;
   lc.stream = st;
   cudaLaunchAttribute attr[2];

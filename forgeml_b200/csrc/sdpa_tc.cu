@@ -323,21 +323,6 @@ __global__ void __launch_bounds__(kThreads, D <= 64 ? 2 : 1)
                            : "memory");
         }
       }
-      // Pool rows past this request's keys hold stale data (possibly not
-      // finite) that P V would multiply by zero: clear them in the V tile.
-      // (Outside the tensor map, as in plain SDPA, TMA fills zeros itself.)
-      if (a.slot_of != nullptr && key0 + kBK > sk) {
-        live = live && mbar_wait(bar(kKvFull0 + (j & 1)), (j >> 1) & 1, DEV_ERR_ATTN_TIMEOUT);
-        if (key0 + r >= sk) {
-          const uint32_t vrow = base + L::kv + (j & 1) * 2 * L::kTile + L::kTile + (uint32_t)r * 128u;
-#pragma unroll
-          for (int sl = 0; sl < L::kSlabs; ++sl)
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-              asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(vrow + sl * kBK * 128 + c * 16), "r"(0u)
-                           : "memory");
-        }
-      }
       fence_async_smem();
       tc_fence_before();
       __syncwarp();

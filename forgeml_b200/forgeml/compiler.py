@@ -37,6 +37,7 @@ each output element is computed by the same kernel arithmetic.
 from __future__ import annotations
 
 import math
+import warnings
 from dataclasses import asdict
 from typing import Callable
 
@@ -383,31 +384,52 @@ class CompiledModel:
     def kernel_source(self) -> str:
         return kernels.kernel_source()
 
-    def node_times(self, *inputs: torch.Tensor, repeats: int = 5) -> dict[str, float]:
-        """Device milliseconds of each instruction of the program (median of
-        ``repeats`` runs; CUDA events between instructions on the current
-        stream).  A fused residual add reports under the add's name."""
-        self(*inputs)
+    def node_times(self, *inputs: torch.Tensor, repeats: int = 20) -> dict[str, float]:
+        """Device milliseconds of each instruction of the program: the
+        instruction alone, ``repeats`` times back to back from one CUDA graph
+        (operands from a preceding full run), best of three replays -- no
+        host gaps, no overlap with other instructions.  View-only
+        instructions launch nothing and report ~0.  A fused residual add
+        reports under the add's name."""
         prog = self._program
-        names = list(self._instr_names)
-        samples: dict[str, list[float]] = {n: [] for n in names}
-        stream = torch.cuda.current_stream()
+        dev = next(t.device for t in inputs)
+        vals: list = [None] * prog.n_values
         with torch.inference_mode():
-            for _ in range(repeats):
-                vals: list = [None] * prog.n_values
-                for vid, t in zip(prog.inputs, inputs):
-                    vals[vid] = t
-                for vid, t in prog.constants:
-                    vals[vid] = t
-                events = [torch.cuda.Event(enable_timing=True) for _ in range(len(prog.instrs) + 1)]
-                events[0].record(stream)
-                for k, (fn, arg_ids, out_id, _) in enumerate(prog.instrs):
-                    vals[out_id] = fn(*[vals[i] for i in arg_ids])
-                    events[k + 1].record(stream)
-                events[-1].synchronize()
-                for k, n in enumerate(names):
-                    samples[n].append(events[k].elapsed_time(events[k + 1]))
-        return {n: sorted(v)[len(v) // 2] for n, v in samples.items()}
+            for vid, t in zip(prog.inputs, inputs):
+                vals[vid] = t
+            for vid, t in prog.constants:
+                vals[vid] = t
+            for fn, arg_ids, out_id, _ in prog.instrs:  # keep every value: each instruction is replayed alone
+                vals[out_id] = fn(*[vals[i] for i in arg_ids])
+            torch.cuda.synchronize(dev)
+            times: dict[str, float] = {}
+            for name, (fn, arg_ids, _, _) in zip(self._instr_names, prog.instrs):
+                args = [vals[i] for i in arg_ids]
+                side = torch.cuda.Stream(dev)
+                side.wait_stream(torch.cuda.current_stream(dev))
+                with torch.cuda.stream(side):
+                    fn(*args)
+                torch.cuda.current_stream(dev).wait_stream(side)
+                torch.cuda.synchronize(dev)
+                graph = torch.cuda.CUDAGraph()
+                with warnings.catch_warnings():  # view-only instructions capture an empty graph
+                    warnings.simplefilter("ignore", UserWarning)
+                    with torch.cuda.graph(graph):
+                        for _ in range(repeats):
+                            fn(*args)
+                graph.replay()
+                torch.cuda.synchronize(dev)
+                best = float("inf")
+                for _ in range(3):
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    graph.replay()
+                    e1.record()
+                    e1.synchronize()
+                    best = min(best, e0.elapsed_time(e1) / repeats)
+                times[name] = best
+                del graph
+        return times
 
     def explain(self) -> dict:
         return {
