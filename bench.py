@@ -428,8 +428,8 @@ def _graph_time_us(fns, reps: int = 5) -> float:
 
 
 def _step_lanes(dec, b: int) -> list[int]:
-    """Rows of each half-batch lane a decode step of ``b`` requests runs."""
-    return [b // 2, b - b // 2] if dec._split_ok(b, 1) else [b]
+    """Rows of each batch lane a decode step of ``b`` requests runs."""
+    return dec._lanes(b, 1)
 
 
 def all_reduce_family_us(dec, dev, world: int) -> dict | None:
@@ -464,7 +464,7 @@ def kernel_rooflines(engine, dev, ctx_len: int, ms_per_step: float, ar_family: d
       gemm       gemm_kernel as the step runs it: per layer the LayerNorm-
                  folded QKV launch with the KV-append epilogue, o (+ residual
                  at TP1), the LayerNorm-folded up launch with tanh GELU, down
-                 (+ residual at TP1); then lm_head.  Per half-batch lane when
+                 (+ residual at TP1); then lm_head.  Per batch lane when
                  the step is split.  Algorithmic bytes = weights + activations
                  in + outputs (K/V rows included) (+ residual)
       attention  neb_attn_bulk_kernel, one launch per layer and lane at the

@@ -20,6 +20,9 @@
 //               accumulator, apply the reference's rounding contract (round
 //               to output dtype, + bias, round, GELU in fp32), optional
 //               residual add, store.
+//   warps 9..12 (wide 16-bit tiles only) epilogue helpers: the second half
+//               of each tile's columns, so that two warps per TMEM lane
+//               quadrant share a tile's epilogue.
 //
 // The kernel works in "MMA space": D[i][j] = sum_k P[i][k] * Q[j][k] where P
 // supplies the 128 TMEM lanes and Q the BN columns.  For ordinary shapes
@@ -50,7 +53,7 @@ namespace gemm {
 constexpr int kBM = 128;        // UMMA M
 constexpr int kSlab = 128;      // bytes of K per smem row (one swizzle row)
 // Warp roles: 0-3 epilogue (TMEM lane quadrant = warp), 4 UMMA issuer,
-// 5-8 TMA producers.
+// 5-8 TMA producers, 9-12 epilogue helpers (wide tiles, threads_of()).
 constexpr int kMmaWarp = 4;
 constexpr int kProducerWarp0 = 5;
 constexpr int kThreads = 288;   // 9 warps
@@ -152,6 +155,8 @@ constexpr int kBarBytes = 8 * kNumBars + 16;  // + tmem holder
 // leaves the epilogue latency-bound; at short K (a few dozen slabs) that
 // epilogue, not the main loop, sets the tile rate.
 constexpr int kHelperWarp0 = 9;
+// Per epilogue warp (8 on wide tiles): a 32-row x 64-byte staging block.
+constexpr int kEpiStageBytes = 8 * 32 * 64;
 template <int BN, bool PROMOTE, bool FUSED>
 struct EpiHelp {
   static constexpr bool on = BN >= 128 && !PROMOTE && !FUSED;
@@ -791,6 +796,77 @@ __device__ bool ar_exchange(const Params& p, const Smem& s, int ti, int r0, int 
 // FUSED: the decode linear with the LayerNorm prologue, KV-append and
 // all-reduce epilogues (pre-packed 16-bit P, swapped, one tile per cluster,
 // always through the split-K reduction buffer).
+// One warp's 32 rows x 32 columns of a wide 16-bit tile (thread = row, v =
+// its 32 accumulators, output columns n0..n0+31 of rows m0..m0+31), stored
+// coalesced: the rows are staged in this warp's 2 KB block of shared memory
+// (16-byte chunk q of row r at r*64 + (q ^ ((r >> 1) & 3))*16, conflict-free
+// both ways) and written back by the warp 8 rows x 64 bytes per instruction,
+// so the L2 sees whole sectors instead of 16-byte pieces of 32 rows.  The
+// residual block comes in the same way.  Epilogue contract of
+// epilogue_store.  False (nothing done) when the block is not whole or not
+// 16-byte aligned; the caller then stores element-wise.  Warp-uniform.
+__device__ __forceinline__ bool stage_store32(const Params& p, uint32_t stg, int m0, int n0, int lane,
+                                              const float (&v)[32]) {
+  if (m0 + 32 > p.rows_out || n0 + 32 > p.cols_out || (p.ldo & 7) != 0 ||
+      (reinterpret_cast<uintptr_t>(p.out) & 15) != 0)
+    return false;
+  if (p.residual != nullptr && ((p.ldr & 7) != 0 || (reinterpret_cast<uintptr_t>(p.residual) & 15) != 0))
+    return false;
+  const int od = p.out_dtype;
+  const bool bf = od == FML_BF16;
+  const int cr = lane >> 2, cq = lane & 3;  // coalesced pass: row within 8, 16-byte chunk
+  auto slot = [&](int r, int q) { return stg + (uint32_t)(r * 64 + ((q ^ ((r >> 1) & 3)) * 16)); };
+  if (p.residual != nullptr) {
+    const uint16_t* rb = reinterpret_cast<const uint16_t*>(p.residual);
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int r = cr + 8 * it;
+      const uint4 t = *reinterpret_cast<const uint4*>(rb + (long long)(m0 + r) * p.ldr + n0 + cq * 8);
+      st_shared_u4(slot(r, cq), t.x, t.y, t.z, t.w);
+    }
+    __syncwarp();
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float x[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] = round_to(v[8 * q + e], od);
+    if (p.bias != nullptr) {
+      float bv[8];
+      load_bias8(p, n0 + 8 * q, bv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = round_to(x[e] + bv[e], od);
+    }
+    if (p.act != FML_ACT_NONE) {
+      const bool erf_act = p.act == FML_ACT_GELU_ERF;
+#pragma unroll 1
+      for (int e = 0; e < 8; ++e) {  // one copy of the GELU code, registers rotated
+        const float g = erf_act ? gelu_erf(x[0]) : gelu_tanh(x[0]);
+#pragma unroll
+        for (int k = 0; k < 7; ++k) x[k] = x[k + 1];
+        x[7] = g;
+      }
+    }
+    if (p.residual != nullptr) {
+      float r[8];
+      unpack8(ld_shared_u4(slot(lane, q)), bf, r);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = round_to(x[e], od) + r[e];
+    }
+    const uint4 o = pack8_16(x, bf);
+    st_shared_u4(slot(lane, q), o.x, o.y, o.z, o.w);
+  }
+  __syncwarp();
+  uint16_t* ob = reinterpret_cast<uint16_t*>(p.out);
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int r = cr + 8 * it;
+    *reinterpret_cast<uint4*>(ob + (long long)(m0 + r) * p.ldo + n0 + cq * 8) = ld_shared_u4(slot(r, cq));
+  }
+  __syncwarp();  // the block is refilled by the next chunk
+  return true;
+}
+
 template <int BN, bool PROMOTE, bool PAIR = false, bool FUSED = false>
 __global__ void __launch_bounds__(threads_of<BN, PROMOTE, FUSED>(), (BN <= 64 && !PROMOTE) ? 2 : 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
@@ -1128,6 +1204,13 @@ __global__ void __launch_bounds__(threads_of<BN, PROMOTE, FUSED>(), (BN <= 64 &&
             const int nvalid = min(32, BN - c * 32);
             if (!use_red) {
               const int j0 = tj * BN + c * 32;
+              if constexpr (kHelp) {
+                // wide tiles: this warp's 32 x 32 block through its staging slot
+                const uint32_t stg = s.red + (uint32_t)((helper ? warp - kHelperWarp0 + 4 : warp) * 2048);
+                if (help_on && !p.swap && p.out_dtype != FML_F32 && nvalid == 32 &&
+                    stage_store32(p, stg, i - lane, j0, lane, v))
+                  continue;
+              }
               if (nvalid == 32 && epilogue_row32_fast(p, i, j0, v)) continue;
               if (!p.swap) {
                 // residual or fp32 output: 16-byte vectors of eight columns
@@ -1483,6 +1566,9 @@ static int smem_bytes_for(int bn, int stages, int ksplit, int* red_stride, int s
   int rs = bn + 4;
   if (red_stride) *red_stride = rs;
   int red = (ksplit > 1 || fused || bn <= 32) ? kBM * rs * 4 + 16 : 0;  // narrow swapped tiles store through it
+  // wide tiles without split-K stage their output rows for coalesced stores
+  // (in the place of the unused split-K buffer)
+  if (red == 0 && bn >= 128 && !fused) red = kEpiStageBytes;
   return 1024 + stages * stage_bytes + kBarBytes + 16 + red + (fused ? aux_bytes(bn) : 0);
 }
 

@@ -55,15 +55,23 @@ __global__ void __launch_bounds__(kWarps * 32)
   constexpr int W = Vec<T>::N;
   const int lane = threadIdx.x & 31;
   const int nvec = cols / W;
-  // gamma / beta are constant weights: bring them into L2 while the
-  // previous grid finishes (they are read only after the statistics).
+  // gamma / beta are constant weights: this lane's vectors are loaded into
+  // registers while the previous grid finishes, off the row's dependency
+  // chain (rows up to 8 vectors per lane; wider rows prefetch them to L2).
+  constexpr bool kPreload = VPL_MAX <= 8;
+  uint4 graw[kPreload ? VPL_MAX : 1], braw[kPreload ? VPL_MAX : 1];
   if (g != nullptr) {
 #pragma unroll
     for (int i = 0; i < VPL_MAX; ++i) {
       const int vi = lane + 32 * i;
-      if (vi < nvec && (vi & 7) == 0) {
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(g + vi * W));
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(b + vi * W));
+      if (vi < nvec) {
+        if constexpr (kPreload) {
+          graw[i] = *reinterpret_cast<const uint4*>(g + vi * W);
+          braw[i] = *reinterpret_cast<const uint4*>(b + vi * W);
+        } else if ((vi & 7) == 0) {
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(g + vi * W));
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(b + vi * W));
+        }
       }
     }
   }
@@ -106,8 +114,18 @@ __global__ void __launch_bounds__(kWarps * 32)
       float o[W];
       float gv[W], bv[W];
       if (g != nullptr) {
-        load_vec<T>(g + vi * W, gv);
-        load_vec<T>(b + vi * W, bv);
+        if constexpr (kPreload) {
+          const T* ge = reinterpret_cast<const T*>(&graw[i]);
+          const T* be = reinterpret_cast<const T*>(&braw[i]);
+#pragma unroll
+          for (int e = 0; e < W; ++e) {
+            gv[e] = to_f32<T>(ge[e]);
+            bv[e] = to_f32<T>(be[e]);
+          }
+        } else {
+          load_vec<T>(g + vi * W, gv);
+          load_vec<T>(b + vi * W, bv);
+        }
       }
 #pragma unroll
       for (int e = 0; e < W; ++e) {

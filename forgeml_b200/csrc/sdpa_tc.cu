@@ -18,9 +18,13 @@
 //   warps 0-3  softmax and epilogue, one query row per thread (its TMEM
 //              lane): running max and sum in fp32, P = exp(S - max) written
 //              as 16-bit values into shared memory in the swizzled UMMA
-//              operand layout, the block's P V read back from TMEM and
-//              accumulated in fp32 registers with the usual rescaling, the
-//              normalised row stored once at the end.
+//              operand layout.  P V accumulates over the key blocks in TMEM;
+//              when a row's maximum moves its TMEM output is scaled in place
+//              (a warp whose rows all kept their maximum skips that), and the
+//              normalised row is read out and stored once at the end.
+//              Key blocks every row of a warp sees whole take an unmasked
+//              path (MUFU exp2, packed 16-bit conversion, four independent
+//              partial sums).
 //
 // Every wait is bounded (DEV_ERR_ATTN_TIMEOUT); a CTA that gives up lets its
 // copies land and frees its TMEM before it exits.
@@ -38,7 +42,11 @@ constexpr int kBQ = 128;           // queries per CTA (UMMA M, TMEM lanes)
 constexpr int kBK = 128;           // keys per block (UMMA N of S, K of P V)
 constexpr int kProducerWarp = 4;
 constexpr int kMmaWarp = 5;
-constexpr uint32_t kTmemCols = 256;  // S: 128 columns, O block: head-dim columns
+// Dynamic shared memory beyond the layout: alignment of its base to 1024
+// bytes.  Dynamic shared memory starts at least 512-byte aligned here (the
+// kernel checks); 512 bytes keep two head-dim-64 CTAs within one SM.
+constexpr uint32_t kAlignSlack = 512;
+constexpr uint32_t kTmemCols = 256;  // S: 128 columns, the running O: head-dim columns
 
 struct Args {
   int Sq, Sk, H;
@@ -94,6 +102,34 @@ __device__ __forceinline__ void load_tile(const CUtensorMap* map, const MapOrder
   tma_load_4d(map, bar, dst, x, at(1), at(2), at(3));
 }
 
+// 2^x by the MUFU instruction (PTX ex2.approx.ftz.f32: a few ulp; the
+// probabilities are rounded to 16 bits right after).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// Two probabilities as one packed 16-bit pair (first in the low half), and
+// back to floats: the values the tensor core multiplies.
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  } else {
+    return __half22float2(*reinterpret_cast<__half2*>(&w));
+  }
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, D <= 64 ? 2 : 1)
     sdpa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -101,6 +137,12 @@ __global__ void __launch_bounds__(kThreads, D <= 64 ? 2 : 1)
                    const MapOrder ord_v, const Args a) {
   using L = Smem<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // The swizzled tiles want a 1024-byte aligned base; the launch adds
+  // kAlignSlack bytes for that, enough for any 512-byte aligned start.
+  if ((smem_u32(smem_raw) & 511u) != 0) {  // uniform: nothing touched yet
+    if (threadIdx.x == 0) raise_device_error(DEV_ERR_ATTN_RANGE);
+    return;
+  }
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int qblk = blockIdx.x, h = blockIdx.y % a.H, b = blockIdx.y / a.H;
@@ -123,7 +165,6 @@ __global__ void __launch_bounds__(kThreads, D <= 64 ? 2 : 1)
   // keys this block of queries attends to
   const int kend = a.causal ? min(sk, q0 + kBQ + q_off) : sk;
   const int nkb = (kend + kBK - 1) / kBK;
-  __shared__ int s_abort;
 
   if (threadIdx.x == 0) {
     mbar_init(bar(kQFull), 1);
@@ -135,7 +176,6 @@ __global__ void __launch_bounds__(kThreads, D <= 64 ? 2 : 1)
     mbar_init(bar(kPFull), 4);  // one arrive per softmax warp
     mbar_init(bar(kOFull), 1);
     fence_mbar_init();
-    s_abort = 0;
   }
   if (warp == kMmaWarp) {
     tmem_alloc(tmem_holder, kTmemCols);
@@ -177,7 +217,6 @@ __global__ void __launch_bounds__(kThreads, D <= 64 ? 2 : 1)
         ++issued;
       }
       if (!ok) {
-        s_abort = 1;
         // let the loads already issued land before the CTA may exit
         mbar_wait(bar(kQFull), 0, DEV_ERR_ATTN_TIMEOUT);
         for (int j = max(0, issued - 2); j < issued; ++j)
@@ -215,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, D <= 64 ? 2 : 1)
           }
         umma_commit(bar(kSFull));
         s_issued = j + 1;
-        // O = P V once the softmax warps wrote P (and read the last O block)
+        // O += P V once the softmax warps wrote P (and rescaled O where needed)
         if (!mbar_wait(bar(kPFull), j & 1, DEV_ERR_ATTN_TIMEOUT)) { okk = false; break; }
         tc_fence_after();
 #pragma unroll
@@ -223,13 +262,12 @@ __global__ void __launch_bounds__(kThreads, D <= 64 ? 2 : 1)
           // P: 16 keys = 32 bytes within a 64-key slab; V: 16 key rows of 128 bytes
           const uint32_t poff = (uint32_t)((k / 4) * kBQ * 128 + (k % 4) * 32) >> 4;
           const uint32_t voff = (uint32_t)(k * 16 * 128) >> 4;
-          umma_f16(tmem + kBK, dp + poff, dv + voff, id_o, k != 0);
+          umma_f16(tmem + kBK, dp + poff, dv + voff, id_o, (j | k) != 0);  // O accumulates over the blocks
         }
         umma_commit(bar(kOFull));
         umma_commit(bar(kKvEmpty0 + st));
         done = j + 1;
       }
-      if (!okk) s_abort = 1;
       // every UMMA issued above completes before TMEM is released: the last
       // Q K^T commit and the last P V commit
       if (s_issued > 0) mbar_wait(bar(kSFull), (s_issued - 1) & 1, DEV_ERR_ATTN_TIMEOUT);
@@ -243,9 +281,6 @@ __global__ void __launch_bounds__(kThreads, D <= 64 ? 2 : 1)
     const int r = threadIdx.x;  // query row in the block = TMEM lane
     const int qi = q0 + r;
     const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-    float o[D];
-#pragma unroll
-    for (int d = 0; d < D; ++d) o[d] = 0.f;
     float m = -INFINITY, l = 0.f;
     bool live = true;
     for (int j = 0; j < nkb; ++j) {
@@ -255,48 +290,75 @@ __global__ void __launch_bounds__(kThreads, D <= 64 ? 2 : 1)
       // keys of this block this row may see
       int lim = min(kBK, sk - key0);
       if (a.causal) lim = min(lim, qi + q_off - key0 + 1);
+      // every row of the warp sees the whole block: no per-key masking
+      const bool full = __all_sync(0xffffffffu, lim >= kBK);
       // pass 1: row maximum of the scaled scores
       float mx = -INFINITY;
+      if (full) {
 #pragma unroll
-      for (int c = 0; c < kBK / 32; ++c) {
-        float v[32];
-        tmem_ld32(trow + c * 32, v);
+        for (int c = 0; c < kBK / 32; ++c) {
+          float v[32];
+          tmem_ld32(trow + c * 32, v);
+          float m2[4] = {v[0], v[1], v[2], v[3]};
 #pragma unroll
-        for (int e = 0; e < 32; ++e)
-          if (c * 32 + e < lim) mx = fmaxf(mx, v[e]);
+          for (int e = 4; e < 32; ++e) m2[e & 3] = fmaxf(m2[e & 3], v[e]);
+          mx = fmaxf(mx, fmaxf(fmaxf(m2[0], m2[1]), fmaxf(m2[2], m2[3])));
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < kBK / 32; ++c) {
+          float v[32];
+          tmem_ld32(trow + c * 32, v);
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (c * 32 + e < lim) mx = fmaxf(mx, v[e]);
+        }
       }
       const float m_new = fmaxf(m, mx * a.scale_log2);
-      // the previous block's P V: add it to the running output, then rescale
+      // The running output lives in TMEM (P V accumulates into it).  Once
+      // the previous block's P V has landed, rows whose maximum moved scale
+      // their output in place; a warp whose rows all kept theirs skips it.
+      const float alpha = (m == -INFINITY) ? 0.f : exp2f(m - m_new);
       if (j > 0) {
         live = live && mbar_wait(bar(kOFull), (j - 1) & 1, DEV_ERR_ATTN_TIMEOUT);
         tc_fence_after();
+        if (!__all_sync(0xffffffffu, alpha == 1.f)) {
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          float v[32];
-          tmem_ld32(trow + kBK + c * 32, v);
+          for (int c = 0; c < D / 32; ++c) {
+            float v[32];
+            tmem_ld32(trow + kBK + c * 32, v);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[c * 32 + e] += v[e];
+            for (int e = 0; e < 32; ++e) v[e] *= alpha;
+            tmem_st32(trow + kBK + c * 32, v);
+          }
         }
       }
-      const float alpha = (m == -INFINITY) ? 0.f : exp2f(m - m_new);
       l *= alpha;
-#pragma unroll
-      for (int d = 0; d < D; ++d) o[d] *= alpha;
       m = m_new;
       // pass 2: probabilities, their sum, and P into the swizzled operand tile
       const uint32_t prow = base + L::p + (uint32_t)r * 128u;
+      float lp[4] = {0.f, 0.f, 0.f, 0.f};  // partial sums (independent add chains)
 #pragma unroll
       for (int c = 0; c < kBK / 32; ++c) {
         float v[32];
         tmem_ld32(trow + c * 32, v);
         uint32_t w[16];
+        if (full) {
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float p0 = (c * 32 + e < lim && m != -INFINITY) ? exp2f(v[e] * a.scale_log2 - m) : 0.f;
-          const float p1 = (c * 32 + e + 1 < lim && m != -INFINITY) ? exp2f(v[e + 1] * a.scale_log2 - m) : 0.f;
-          T t0 = from_f32<T>(p0), t1 = from_f32<T>(p1);
-          l += to_f32<T>(t0) + to_f32<T>(t1);  // the sum of what the tensor core multiplies
-          w[e / 2] = (uint32_t)(*reinterpret_cast<uint16_t*>(&t0)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&t1)) << 16);
+          for (int e = 0; e < 32; e += 2) {
+            w[e / 2] = pack2<T>(ex2_approx(fmaf(v[e], a.scale_log2, -m)), ex2_approx(fmaf(v[e + 1], a.scale_log2, -m)));
+            const float2 f = unpack2<T>(w[e / 2]);  // the sum of what the tensor core multiplies
+            lp[(e / 2) & 3] += f.x + f.y;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float p0 = (c * 32 + e < lim && m != -INFINITY) ? exp2f(v[e] * a.scale_log2 - m) : 0.f;
+            const float p1 = (c * 32 + e + 1 < lim && m != -INFINITY) ? exp2f(v[e + 1] * a.scale_log2 - m) : 0.f;
+            T t0 = from_f32<T>(p0), t1 = from_f32<T>(p1);
+            lp[0] += to_f32<T>(t0) + to_f32<T>(t1);
+            w[e / 2] = (uint32_t)(*reinterpret_cast<uint16_t*>(&t0)) | ((uint32_t)(*reinterpret_cast<uint16_t*>(&t1)) << 16);
+          }
         }
         // 32 keys = 4 chunks of 16 bytes, in slab (c / 2), chunks 4 * (c % 2) ..
 #pragma unroll
@@ -308,6 +370,7 @@ __global__ void __launch_bounds__(kThreads, D <= 64 ? 2 : 1)
                        : "memory");
         }
       }
+      l += (lp[0] + lp[1]) + (lp[2] + lp[3]);
       // Pool rows past this request's keys hold stale data (possibly not
       // finite) that P V would multiply by zero: clear them in the V tile.
       // (Outside the tensor map, as in plain SDPA, TMA fills zeros itself.)
@@ -328,35 +391,32 @@ __global__ void __launch_bounds__(kThreads, D <= 64 ? 2 : 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kPFull));
     }
+    // the output row: the accumulated P V from TMEM, normalised by the sum
     if (nkb > 0) {
       live = live && mbar_wait(bar(kOFull), (nkb - 1) & 1, DEV_ERR_ATTN_TIMEOUT);
       tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        float v[32];
-        tmem_ld32(trow + kBK + c * 32, v);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) o[c * 32 + e] += v[e];
-      }
     }
-    if (live && qi < a.Sq) {
-      // l == 0 (every key masked) gives NaN, as torch
-      const float inv = 1.0f / l;
-      T* out = static_cast<T*>(a.out) + b * a.os[0] + h * a.os[1] + (long long)qi * a.os[2];
-      if (a.os[3] == 1 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+    const float inv = 1.0f / l;  // l == 0 (every key masked) gives NaN, as torch
+    T* out = static_cast<T*>(a.out) + b * a.os[0] + h * a.os[1] + (long long)qi * a.os[2];
+    const bool vec = a.os[3] == 1 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
 #pragma unroll
-        for (int d = 0; d < D; d += 8) {
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 8; e += 2) {
-            T t0 = from_f32<T>(o[d + e] * inv), t1 = from_f32<T>(o[d + e + 1] * inv);
-            w[e / 2] = (uint32_t)(*reinterpret_cast<uint16_t*>(&t0)) |
-                       ((uint32_t)(*reinterpret_cast<uint16_t*>(&t1)) << 16);
-          }
-          *reinterpret_cast<uint4*>(out + d) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
+    for (int c = 0; c < D / 32; ++c) {
+      float v[32];
+      if (nkb > 0) {
+        tmem_ld32(trow + kBK + c * 32, v);
       } else {
-        for (int d = 0; d < D; ++d) out[(long long)d * a.os[3]] = from_f32<T>(o[d] * inv);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = 0.f;
+      }
+      if (!(live && qi < a.Sq)) continue;
+      if (vec) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          reinterpret_cast<uint4*>(out + c * 32)[q] =
+              make_uint4(pack2<T>(v[8 * q] * inv, v[8 * q + 1] * inv), pack2<T>(v[8 * q + 2] * inv, v[8 * q + 3] * inv),
+                         pack2<T>(v[8 * q + 4] * inv, v[8 * q + 5] * inv), pack2<T>(v[8 * q + 6] * inv, v[8 * q + 7] * inv));
+      } else {
+        for (int e = 0; e < 32; ++e) out[(long long)(c * 32 + e) * a.os[3]] = from_f32<T>(v[e] * inv);
       }
     }
   }
@@ -431,7 +491,7 @@ static bool encode_operand(CUtensorMap* map, MapOrder* order, const void* ptr, c
 template <typename T, int D>
 static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const MapOrder& oq,
                   const MapOrder& ok, const MapOrder& ov, const Args& a, int64_t B, int64_t H, cudaStream_t st) {
-  const size_t smem = Smem<D>::total + 1024;
+  const size_t smem = Smem<D>::total + kAlignSlack;
   cudaError_t e = cudaFuncSetAttribute(sdpa_tc_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return check_cuda(e, "sdpa_tc attribute");
   const dim3 grid((unsigned)((a.Sq + kBQ - 1) / kBQ), (unsigned)(B * H));

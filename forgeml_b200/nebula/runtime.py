@@ -226,13 +226,16 @@ class ShardedDecoder(nn.Module):
             es = torch.empty((), dtype=dtype).element_size()
             slot = max(16, (max(max_requests, 32) * h * es + 15) // 16 * 16)
             self._peer_ar = peer.PeerAllReduce(context, max_bytes=slot)
-        # Decode steps of 4 or more TP ranks run as two half-batches (_core);
-        # the second half reduces through its own peer context.
-        self.split_batches = context.tp_size >= 4
-        self._peer_ar2 = None
-        self._side_stream = None
-        if self._peer_ar is not None and context.pp_size == 1:
-            self._peer_ar2 = peer.PeerAllReduce(context, max_bytes=self._peer_ar.max_bytes)
+        # Decode steps of 4 or more TP ranks run as several batch lanes
+        # (_core), each lane reducing through its own peer context: two by
+        # default, up to MAX_LANES (every rank creates the same contexts, in
+        # the same order).
+        self.decode_lanes = 2 if context.tp_size >= 4 else 1
+        self._lane_ars = [self._peer_ar]
+        self._lane_streams: list = []
+        if self._peer_ar is not None and context.pp_size == 1 and context.tp_size >= 4:
+            self._lane_ars += [peer.PeerAllReduce(context, max_bytes=self._peer_ar.max_bytes)
+                               for _ in range(self.MAX_LANES - 1)]
         self._fused_cache: dict[tuple, bool] = {}
         # Decode-step layout choices (the defaults are the measured best; the
         # alternatives compute the same step and are kept for tests):
@@ -249,6 +252,8 @@ class ShardedDecoder(nn.Module):
         self.all_reduce_in_gemm = False
 
     # ------------------------------------------------------------------ math
+    MAX_LANES = 4
+
     def _fused_ok(self, bt: int) -> bool:
         """Whether a layer of ``bt`` tokens runs as the fused launches
         (LN+QKV+KV append, o+all-reduce, LN+up+GELU, down+all-reduce)."""
@@ -348,10 +353,14 @@ class ShardedDecoder(nn.Module):
         self.context.all_reduce(part)
         return ops.add(x, part)
 
-    def _split_ok(self, b: int, t: int) -> bool:
-        """Whether a step runs as two half-batches on two streams (see _core)."""
-        return (self.split_batches and t == 1 and b >= 2 and self.context.pp_size == 1
-                and self._peer_ar2 is not None and self._fused_ok(b - b // 2))
+    def _lanes(self, b: int, t: int) -> list[int]:
+        """Rows of each batch lane of a step of ``b`` requests (see _core):
+        ``decode_lanes`` contiguous groups of near-equal size, or one."""
+        n = min(self.decode_lanes, b, len(self._lane_ars))
+        if n <= 1 or t != 1 or self.context.pp_size != 1 or any(a is None for a in self._lane_ars[:n]):
+            return [b]
+        rows = [b // n + (1 if i < b % n else 0) for i in range(n)]
+        return rows if self._fused_ok(max(rows)) else [b]
 
     def _core(self, tokens: torch.Tensor, slots: torch.Tensor, starts: torch.Tensor, b: int, t: int,
               last_only: bool) -> torch.Tensor:
@@ -360,27 +369,36 @@ class ShardedDecoder(nn.Module):
         With tensor parallelism a decode step is a chain of short launches
         whose time is mostly latency (the weights a rank streams shrink with
         the TP degree, a launch's fixed cost does not).  There the batch runs
-        as two halves on two streams, each with its own peer all-reduce
-        context: one half's GEMMs, attention and reductions fill the other's
-        waits.  Every request's arithmetic is that of an unsplit step of half
-        the batch."""
-        if not self._split_ok(b, t):
+        as several lanes on their own streams, each with its own peer
+        all-reduce context: one lane's GEMMs, attention and reductions fill
+        the others' waits.  Every request's arithmetic is that of an unsplit
+        step of its lane's rows."""
+        lanes = self._lanes(b, t)
+        if len(lanes) == 1:
             return self._core_rows(tokens, slots, starts, b, t, last_only, self._peer_ar)
         dev = self.context.device
-        h0 = b // 2
         main = torch.cuda.current_stream(dev)
-        if self._side_stream is None:
-            self._side_stream = torch.cuda.Stream(device=dev)
-        side = self._side_stream
-        side.wait_stream(main)
-        # the layers per half; the final LayerNorm and lm_head once for the
-        # whole batch (the head's weights are streamed once per step)
-        xa = self._core_rows(tokens[:h0], slots[:h0], starts[:h0], h0, 1, last_only, self._peer_ar, head=False)
-        with torch.cuda.stream(side):
-            xb = self._core_rows(tokens[h0:], slots[h0:], starts[h0:], b - h0, 1, last_only, self._peer_ar2,
-                                 head=False)
-        main.wait_stream(side)
-        return self._head(torch.cat([xa, xb]), b, 1, last_only)
+        while len(self._lane_streams) < len(lanes) - 1:
+            self._lane_streams.append(torch.cuda.Stream(device=dev))
+        # the layers per lane (lane 0 on the calling stream); the final
+        # LayerNorm and lm_head once for the whole batch (the head's weights
+        # are streamed once per step)
+        outs, r0 = [], 0
+        for i, rows in enumerate(lanes):
+            sl = slice(r0, r0 + rows)
+            if i == 0:
+                outs.append(self._core_rows(tokens[sl], slots[sl], starts[sl], rows, 1, last_only,
+                                            self._lane_ars[0], head=False))
+            else:
+                st = self._lane_streams[i - 1]
+                st.wait_stream(main)
+                with torch.cuda.stream(st):
+                    outs.append(self._core_rows(tokens[sl], slots[sl], starts[sl], rows, 1, last_only,
+                                                self._lane_ars[i], head=False))
+            r0 += rows
+        for st in self._lane_streams[:len(lanes) - 1]:
+            main.wait_stream(st)
+        return self._head(torch.cat(outs), b, 1, last_only)
 
     def _core_rows(self, tokens: torch.Tensor, slots: torch.Tensor, starts: torch.Tensor, b: int, t: int,
                    last_only: bool, ar, head: bool = True) -> torch.Tensor:
@@ -519,11 +537,11 @@ class ShardedDecoder(nn.Module):
     def close(self) -> None:
         """Release the captured graphs and the peer all-reduce buffers."""
         self.release_graphs()
-        for name in ("_peer_ar", "_peer_ar2"):
-            ar = getattr(self, name)
+        for ar in self._lane_ars:  # lane 0 is the step's own context
             if ar is not None:
                 ar.close()
-                setattr(self, name, None)
+        self._lane_ars = [None]
+        self._peer_ar = None
 
 
 # The serving engine lives in engine.py; the reference exposes it from this module.

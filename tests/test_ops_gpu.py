@@ -91,6 +91,17 @@ def test_sdpa_tensor_core_path(cuda, dtype, b, s, h, d, causal):
     close(buf.transpose(1, 2), want, dtype)
 
 
+@pytest.mark.parametrize("dtype,s,causal", [(torch.bfloat16, 1000, False), (torch.float16, 777, True)])
+def test_sdpa_tensor_core_sharp_scores(cuda, dtype, s, causal):
+    """Large scores (q scaled by 6) over many key blocks: row maxima keep
+    moving, so the running output in TMEM is rescaled block after block."""
+    (q, k, v), (qc, kc, vc) = _qkv_views(1, s, 3, 64, dtype, cuda, seed=11 + s)
+    q, qc = (q * 6).to(dtype), (qc.float() * 6).to(dtype)
+    got = kernels.sdpa(q, k, v, is_causal=causal)
+    want = sdpa_ref(qc, kc, vc, is_causal=causal)
+    close(got, want, dtype)
+
+
 def test_sdpa_matches_torch_cpu_c2_slice(cuda):
     """c2 shapes (head_dim 64, 12 heads) on one batch element vs torch's own CPU SDPA."""
     (q, k, v), (qc, kc, vc) = _qkv_views(1, 512, 12, 64, torch.float32, cuda, seed=1)
