@@ -155,8 +155,9 @@ constexpr int kBarBytes = 8 * kNumBars + 16;  // + tmem holder
 // leaves the epilogue latency-bound; at short K (a few dozen slabs) that
 // epilogue, not the main loop, sets the tile rate.
 constexpr int kHelperWarp0 = 9;
-// Per epilogue warp (8 on wide tiles): a 32-row x 64-byte staging block.
-constexpr int kEpiStageBytes = 8 * 32 * 64;
+// Per epilogue warp (8 on wide tiles): a 32-row x 64-byte staging block and
+// 64 bytes of bias (kEpiWarpBytes).
+constexpr int kEpiStageBytes = 8 * (32 * 64 + 64);
 template <int BN, bool PROMOTE, bool FUSED>
 struct EpiHelp {
   static constexpr bool on = BN >= 128 && !PROMOTE && !FUSED;
@@ -798,34 +799,53 @@ __device__ bool ar_exchange(const Params& p, const Smem& s, int ti, int r0, int 
 // always through the split-K reduction buffer).
 // One warp's 32 rows x 32 columns of a wide 16-bit tile (thread = row, v =
 // its 32 accumulators, output columns n0..n0+31 of rows m0..m0+31), stored
-// coalesced: the rows are staged in this warp's 2 KB block of shared memory
+// coalesced: the rows are staged in this warp's block of shared memory
 // (16-byte chunk q of row r at r*64 + (q ^ ((r >> 1) & 3))*16, conflict-free
 // both ways) and written back by the warp 8 rows x 64 bytes per instruction,
 // so the L2 sees whole sectors instead of 16-byte pieces of 32 rows.  The
-// residual block comes in the same way.  Epilogue contract of
-// epilogue_store.  False (nothing done) when the block is not whole or not
-// 16-byte aligned; the caller then stores element-wise.  Warp-uniform.
-__device__ __forceinline__ bool stage_store32(const Params& p, uint32_t stg, int m0, int n0, int lane,
-                                              const float (&v)[32]) {
-  if (m0 + 32 > p.rows_out || n0 + 32 > p.cols_out || (p.ldo & 7) != 0 ||
-      (reinterpret_cast<uintptr_t>(p.out) & 15) != 0)
-    return false;
-  if (p.residual != nullptr && ((p.ldr & 7) != 0 || (reinterpret_cast<uintptr_t>(p.residual) & 15) != 0))
-    return false;
+// block's bias (64 bytes) and residual rows are loaded one block ahead
+// (stage_prefetch) so that their latency overlaps the previous block.
+// Epilogue contract of epilogue_store.
+constexpr int kEpiWarpBytes = 32 * 64 + 64;  // staged rows + the block's bias
+
+struct StageIn {
+  uint4 bias;    // lanes 0-3: 16 bytes each of bias[n0 .. n0+31]
+  uint4 res[4];  // residual rows cr + 8*it, 16-byte chunk cq
+};
+
+// Whether the block at (m0, n0) can take the staged path (warp-uniform).
+__device__ __forceinline__ bool stage_ok(const Params& p, int m0, int n0) {
+  return m0 + 32 <= p.rows_out && n0 + 32 <= p.cols_out && (p.ldo & 7) == 0 &&
+         (reinterpret_cast<uintptr_t>(p.out) & 15) == 0 &&
+         (p.bias == nullptr || (p.bias_stride == 1 && ((reinterpret_cast<uintptr_t>(p.bias) + 2 * n0) & 15) == 0)) &&
+         (p.residual == nullptr || ((p.ldr & 7) == 0 && (reinterpret_cast<uintptr_t>(p.residual) & 15) == 0));
+}
+
+__device__ __forceinline__ void stage_prefetch(const Params& p, int m0, int n0, int lane, StageIn& in) {
+  if (p.bias != nullptr && lane < 4)
+    in.bias = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.bias) + n0 + lane * 8);
+  if (p.residual != nullptr) {
+    const uint16_t* rb = reinterpret_cast<const uint16_t*>(p.residual);
+#pragma unroll
+    for (int it = 0; it < 4; ++it)
+      in.res[it] = *reinterpret_cast<const uint4*>(rb + (long long)(m0 + (lane >> 2) + 8 * it) * p.ldr + n0 +
+                                                   (lane & 3) * 8);
+  }
+}
+
+__device__ __forceinline__ void stage_store32(const Params& p, uint32_t stg, int m0, int n0, int lane,
+                                              const float (&v)[32], const StageIn& in) {
   const int od = p.out_dtype;
   const bool bf = od == FML_BF16;
   const int cr = lane >> 2, cq = lane & 3;  // coalesced pass: row within 8, 16-byte chunk
   auto slot = [&](int r, int q) { return stg + (uint32_t)(r * 64 + ((q ^ ((r >> 1) & 3)) * 16)); };
+  const uint32_t bslot = stg + 32 * 64;
+  if (p.bias != nullptr && lane < 4) st_shared_u4(bslot + lane * 16, in.bias.x, in.bias.y, in.bias.z, in.bias.w);
   if (p.residual != nullptr) {
-    const uint16_t* rb = reinterpret_cast<const uint16_t*>(p.residual);
 #pragma unroll
-    for (int it = 0; it < 4; ++it) {
-      const int r = cr + 8 * it;
-      const uint4 t = *reinterpret_cast<const uint4*>(rb + (long long)(m0 + r) * p.ldr + n0 + cq * 8);
-      st_shared_u4(slot(r, cq), t.x, t.y, t.z, t.w);
-    }
-    __syncwarp();
+    for (int it = 0; it < 4; ++it) st_shared_u4(slot(cr + 8 * it, cq), in.res[it].x, in.res[it].y, in.res[it].z, in.res[it].w);
   }
+  __syncwarp();
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     float x[8];
@@ -833,7 +853,7 @@ __device__ __forceinline__ bool stage_store32(const Params& p, uint32_t stg, int
     for (int e = 0; e < 8; ++e) x[e] = round_to(v[8 * q + e], od);
     if (p.bias != nullptr) {
       float bv[8];
-      load_bias8(p, n0 + 8 * q, bv);
+      unpack8(ld_shared_u4(bslot + q * 16), bf, bv);
 #pragma unroll
       for (int e = 0; e < 8; ++e) x[e] = round_to(x[e] + bv[e], od);
     }
@@ -863,8 +883,7 @@ __device__ __forceinline__ bool stage_store32(const Params& p, uint32_t stg, int
     const int r = cr + 8 * it;
     *reinterpret_cast<uint4*>(ob + (long long)(m0 + r) * p.ldo + n0 + cq * 8) = ld_shared_u4(slot(r, cq));
   }
-  __syncwarp();  // the block is refilled by the next chunk
-  return true;
+  __syncwarp();  // the block is refilled by the next one
 }
 
 template <int BN, bool PROMOTE, bool PAIR = false, bool FUSED = false>
@@ -1169,6 +1188,15 @@ __global__ void __launch_bounds__(threads_of<BN, PROMOTE, FUSED>(), (BN <= 64 &&
 #pragma unroll
       for (int e = 0; e < (PROMOTE ? BN : 1); ++e) racc[e] = 0.f;
       const int nchunks = PROMOTE ? (kb_end - kb_begin + p.promote_kb - 1) / p.promote_kb : 1;
+      // wide tiles: this warp's 32 x 32 blocks go through its staging slot;
+      // the first block's bias / residual are fetched before the tile's
+      // accumulator is ready
+      const uint32_t stg = s.red + (uint32_t)((helper ? warp - kHelperWarp0 + 4 : warp) * kEpiWarpBytes);
+      const bool staged = kHelp && help_on && !p.swap && p.out_dtype != FML_F32 &&
+                          stage_ok(p, i - lane, tj * BN + c_begin * 32) &&
+                          stage_ok(p, i - lane, tj * BN + (c_end - 1) * 32);
+      StageIn pf;
+      if (staged) stage_prefetch(p, i - lane, tj * BN + c_begin * 32, lane, pf);
       for (int ch = 0; ch < nchunks && ok; ++ch) {
         if (!mbar_wait(bar_tfull(s, acc), acc_phase, DEV_ERR_GEMM_TIMEOUT)) { ok = false; break; }
         tc_fence_after();
@@ -1204,12 +1232,11 @@ __global__ void __launch_bounds__(threads_of<BN, PROMOTE, FUSED>(), (BN <= 64 &&
             const int nvalid = min(32, BN - c * 32);
             if (!use_red) {
               const int j0 = tj * BN + c * 32;
-              if constexpr (kHelp) {
-                // wide tiles: this warp's 32 x 32 block through its staging slot
-                const uint32_t stg = s.red + (uint32_t)((helper ? warp - kHelperWarp0 + 4 : warp) * 2048);
-                if (help_on && !p.swap && p.out_dtype != FML_F32 && nvalid == 32 &&
-                    stage_store32(p, stg, i - lane, j0, lane, v))
-                  continue;
+              if (staged) {
+                const StageIn cur = pf;
+                if (c + 1 < c_end) stage_prefetch(p, i - lane, j0 + 32, lane, pf);
+                stage_store32(p, stg, i - lane, j0, lane, v, cur);
+                continue;
               }
               if (nvalid == 32 && epilogue_row32_fast(p, i, j0, v)) continue;
               if (!p.swap) {
@@ -1763,13 +1790,14 @@ static int make_plan(Plan& pl, const void* a, long long lda_m, long long lda_k, 
   const long long tiles = ((I + kBM - 1) / kBM) * ((J + pl.bn - 1) / pl.bn);
   const long long num_kb = (pl.keff * es + kSlab - 1) / kSlab;
   pl.slabs = slabs_for(cfg, dtype, pl.promote, pl.bn);
-  // Large 16-bit tiles run as CTA pairs (256 x 256 per pair, each CTA
-  // loading half of Q) when there are enough pair tiles to fill the GPU.
-  {
-    const long long pair_tiles = ((I + 2 * kBM - 1) / (2 * kBM)) * ((J + 255) / 256);
-    pl.pair = !pl.swap && !pl.promote && dtype != FML_F32 && pl.bn == 256 && I >= 2 * kBM &&
-              pair_tiles * 2 >= sms && pl.slabs == 1;
-  }
+  // Wide 16-bit tiles run as CTA pairs (256 x 256 per pair, each CTA loading
+  // half of Q): the same MMA work per SM as a 128 x 256 tile for two thirds
+  // of the operand bytes, and the main loop is bound by the L2's delivery
+  // to the SMs (measured on B200: about 9.2 TB/s in all, per-stage rates of
+  // every tile shape consistent with it).  Not when rounding M up to whole
+  // pair tiles would leave half a pair tile empty.
+  pl.pair = !pl.swap && !pl.promote && dtype != FML_F32 && pl.bn == 256 && I >= 2 * kBM &&
+            (I % (2 * kBM) == 0 || I % (2 * kBM) > kBM) && pl.slabs == 1;
   if (pl.pair) {
     pl.ksplit = 1;
     pl.stages = stages_for(pl.bn, 1, cfg, pl.slabs, false, true);
