@@ -846,11 +846,20 @@ __device__ __forceinline__ void stage_store32(const Params& p, uint32_t stg, int
     for (int it = 0; it < 4; ++it) st_shared_u4(slot(cr + 8 * it, cq), in.res[it].x, in.res[it].y, in.res[it].z, in.res[it].w);
   }
   __syncwarp();
+  // One copy of the per-8-column code (a rolled loop; the 32 values rotate
+  // by 8 registers per pass, nothing is indexed dynamically): the epilogue
+  // runs beside the producer and MMA warps' code on each SM sub-partition,
+  // and a small instruction footprint keeps it out of instruction misses.
+  float w[32];
 #pragma unroll
+  for (int e = 0; e < 32; ++e) w[e] = v[e];
+#pragma unroll 1
   for (int q = 0; q < 4; ++q) {
     float x[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) x[e] = round_to(v[8 * q + e], od);
+    for (int e = 0; e < 8; ++e) x[e] = round_to(w[e], od);
+#pragma unroll
+    for (int e = 0; e < 24; ++e) w[e] = w[e + 8];
     if (p.bias != nullptr) {
       float bv[8];
       unpack8(ld_shared_u4(bslot + q * 16), bf, bv);

@@ -196,3 +196,18 @@ def test_packed_b_fp32(cuda, m, n, k, epi, layout):
     launch(*args, residual=None if res_cpu is None else res_cpu.to(cuda))
     want = matmul_epilogue(a_cpu, b_cpu * 0.5, bias_cpu, activation=act, residual=res_cpu)
     close(out, want, torch.float32)
+
+
+@pytest.mark.parametrize("approximate", ["none", "tanh"])
+def test_gelu_epilogue_accuracy(cuda, approximate):
+    """The epilogue's GELU against torch's (fp64) over [-8, 8): an fp32
+    identity product passes the values through exactly (multiples of 1/64
+    are exact in the 3xTF32 split), so out = gelu(b) elementwise.  The erf
+    form uses the Abramowitz & Stegun 7.1.26 erf (|error| <= 1.5e-7)."""
+    xs = (torch.arange(1024, dtype=torch.float64) / 64 - 8).to(torch.float32)
+    b = xs.view(8, 128).t().contiguous()          # [K=128, N=8]: every value in some column
+    a = torch.eye(128, dtype=torch.float32)
+    got = kernels.matmul(a.to(cuda), b.to(cuda), activation="gelu", approximate=approximate).cpu().double()
+    want = torch.nn.functional.gelu(b.double(), approximate=approximate)
+    err = (got - want).abs()
+    assert float(err.max()) <= 2e-7 * max(1.0, float(b.abs().max())) + 1e-7, float(err.max())
