@@ -1799,14 +1799,14 @@ static int make_plan(Plan& pl, const void* a, long long lda_m, long long lda_k, 
   const long long tiles = ((I + kBM - 1) / kBM) * ((J + pl.bn - 1) / pl.bn);
   const long long num_kb = (pl.keff * es + kSlab - 1) / kSlab;
   pl.slabs = slabs_for(cfg, dtype, pl.promote, pl.bn);
-  // Wide 16-bit tiles run as CTA pairs (256 x 256 per pair, each CTA loading
-  // half of Q): the same MMA work per SM as a 128 x 256 tile for two thirds
-  // of the operand bytes, and the main loop is bound by the L2's delivery
-  // to the SMs (measured on B200: about 9.2 TB/s in all, per-stage rates of
-  // every tile shape consistent with it).  Not when rounding M up to whole
-  // pair tiles would leave half a pair tile empty.
-  pl.pair = !pl.swap && !pl.promote && dtype != FML_F32 && pl.bn == 256 && I >= 2 * kBM &&
-            (I % (2 * kBM) == 0 || I % (2 * kBM) > kBM) && pl.slabs == 1;
+  // CTA pairs (256 x 256 per pair, each CTA loading half of Q) when the tile
+  // hint asks for 256-row tiles (block_m = 256).  By default wide tiles run
+  // on single CTAs: measured on B200, a stage lands about every 1000 cycles
+  // in both forms whatever its bytes, and single 128 x 256 tiles with the
+  // eight-warp staged epilogue were 2-20 % faster than pairs on every shape
+  // of configs 2 and 3 (8192^3, 4096 x 768 x 3072, 4096 x 2304 x 768).
+  pl.pair = cfg && cfg->block_m == 256 && !pl.swap && !pl.promote && dtype != FML_F32 && pl.bn == 256 &&
+            I >= 2 * kBM && pl.slabs == 1;
   if (pl.pair) {
     pl.ksplit = 1;
     pl.stages = stages_for(pl.bn, 1, cfg, pl.slabs, false, true);

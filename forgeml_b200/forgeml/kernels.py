@@ -32,9 +32,11 @@ class KernelConfig:
     """Tile hints for the native GEMM (fields as in src/forgeml/kernels.py:12-18).
 
     ``block_n`` is the UMMA N tile (16..256) and ``num_stages`` the shared-memory
-    pipeline depth.  ``block_m`` (128-row UMMA tile), ``block_k`` (128-byte K
-    slab) and ``num_warps`` (6: TMA, MMA, 4 epilogue) are fixed by the kernel
-    design and only validated.
+    pipeline depth of single-CTA tiles.  ``block_m`` 256 (with ``block_n``
+    256) asks for CTA-pair tiles (``cta_group::2``, 256 x 256 per pair, the
+    deepest ring that fits); other ``block_m`` values are the 128-row UMMA
+    tile.  ``block_k`` (128-byte K slab) and ``num_warps`` (TMA, MMA and
+    epilogue warps) are fixed by the kernel design and only validated.
     """
 
     block_m: int = 128
@@ -47,12 +49,13 @@ class KernelConfig:
 DEFAULT_CONFIG = KernelConfig()
 CANDIDATES = (
     KernelConfig(128, 256, 64, 6, 4),
+    KernelConfig(256, 256, 64, 6, 7),
     KernelConfig(128, 128, 64, 6, 6),
     KernelConfig(128, 64, 64, 6, 8),
     KernelConfig(128, 32, 64, 6, 8),
 )
 
-_TILES_M = {16, 32, 64, 128}
+_TILES_M = {16, 32, 64, 128, 256}
 _TILES_N = {16, 32, 64, 128, 256}
 _TILES_K = {16, 32, 64, 128, 256}
 _WARPS = {4, 6, 8}

@@ -62,7 +62,7 @@ def test_fastest_correct_candidate_wins(monkeypatch):
     _native_plan(c)
     monkeypatch.setattr(kernels.PreparedGemm, "__call__", _fake_launch(bad={CANDIDATES[1]}, raising={CANDIDATES[2]}))
     # candidate 1 is the fastest but wrong, 2 fails to launch, 3 is the fastest survivor
-    monkeypatch.setattr(autotune, "_time_candidates", _fake_timer([4.0, 0.5, 0.1, 1.0]))
+    monkeypatch.setattr(autotune, "_time_candidates", _fake_timer([4.0, 0.5, 0.1, 1.0, 2.0]))
     rep = autotune.tune_graph(c, (x,), warmup=0, repeats=2)
     assert rep["scope"] == "this_compiled_model_instance_only"
     assert rep["nodes"], "no native GEMM node was tuned"
@@ -71,7 +71,7 @@ def test_fastest_correct_candidate_wins(monkeypatch):
         assert set(rec["rejected"]) == {"candidate_1", "candidate_2"}
         assert "launch failed" in rec["rejected"]["candidate_2"]
         assert "wrong result" in rec["rejected"]["candidate_1"]
-        assert set(rec["candidates"]) == {"candidate_0", "candidate_3"}
+        assert set(rec["candidates"]) == {"candidate_0", "candidate_3", "candidate_4"}
         assert all(v["correctness"]["passed"] for v in rec["candidates"].values())
         assert c.kernel_configs[name] == CANDIDATES[3]
     other = compile(m, (x,), backend="torch")

@@ -128,7 +128,7 @@ def test_kernel_front_door_cpu_errors():
         kernels.matmul(a, a)
     with pytest.raises(GraphError):
         kernels._check_config(KernelConfig(block_m=8))
-    assert isinstance(DEFAULT_CONFIG, KernelConfig) and len(CANDIDATES) == 4
+    assert isinstance(DEFAULT_CONFIG, KernelConfig) and len(CANDIDATES) == 5
     assert kernels.available() is False
     assert "tcgen05.mma" in kernels.kernel_source()
 

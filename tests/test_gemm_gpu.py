@@ -211,3 +211,20 @@ def test_gelu_epilogue_accuracy(cuda, approximate):
     want = torch.nn.functional.gelu(b.double(), approximate=approximate)
     err = (got - want).abs()
     assert float(err.max()) <= 2e-7 * max(1.0, float(b.abs().max())) + 1e-7, float(err.max())
+
+
+@pytest.mark.parametrize("m,n,k,epi", [(512, 1024, 768, "bias_gelu"), (1024, 768, 3072, "residual"),
+                                       (384, 512, 256, "plain")])
+def test_cta_pair_tiles(cuda, m, n, k, epi):
+    """CTA-pair tiles (tile hint block_m = 256: cta_group::2, 256 x 256 per
+    pair) against the oracle, including an M that leaves half a pair tile."""
+    g = torch.Generator().manual_seed(m + n + k)
+    a = (torch.rand(m, k, generator=g) * 2 - 1).to(torch.bfloat16)
+    w = (torch.rand(n, k, generator=g) * 2 - 1).to(torch.bfloat16)
+    bias = torch.randn(n, generator=g).to(torch.bfloat16) if epi == "bias_gelu" else None
+    res = torch.randn(m, n, generator=g).to(torch.bfloat16) if epi == "residual" else None
+    act = "gelu" if epi == "bias_gelu" else "none"
+    cfg = kernels.KernelConfig(256, 256, 64, 6, 7)
+    got = kernels.matmul(a.to(cuda), w.to(cuda).t(), None if bias is None else bias.to(cuda), activation=act,
+                         residual=None if res is None else res.to(cuda), config=cfg)
+    close(got, matmul_epilogue(a, w.t(), bias, activation=act, residual=res), torch.bfloat16)
