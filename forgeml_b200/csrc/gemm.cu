@@ -402,7 +402,8 @@ __device__ __forceinline__ uint4 pack8_16(const float (&x)[8], bool bf) {
 // loads) and 16-byte stores; GELU runs in a rolled loop that rotates the
 // eight registers (one copy of its code, nothing indexed dynamically, so
 // nothing goes to local memory).  Other cases store element by element.
-__device__ __forceinline__ void epilogue_store8(const Params& p, int m, int n0, float (&x)[8]) {
+__device__ __forceinline__ void epilogue_store8(const Params& p, int m, int n0, float (&x)[8],
+                                                const uint4* res_pre = nullptr) {
   if (m >= p.rows_out || n0 >= p.cols_out) return;
   const int od = p.out_dtype;
   const long long off = (long long)m * p.ldo + n0;
@@ -463,7 +464,8 @@ __device__ __forceinline__ void epilogue_store8(const Params& p, int m, int n0, 
     return;
   }
   if (p.residual != nullptr) {
-    const uint4 rv = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.residual) + roff);
+    const uint4 rv = res_pre != nullptr ? *res_pre
+                                        : *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.residual) + roff);
     float r[8];
     unpack8(rv, bf, r);
 #pragma unroll
@@ -708,6 +710,35 @@ __device__ __forceinline__ void ln_fold8(const Params& p, const Smem& s, int BNv
     const float c = p.fold_c != nullptr ? p.fold_c[n] : 0.f;
     x[e] = ms.y * (x[e] - ms.x * p.fold_s[n]) + c;
   }
+}
+
+// The global inputs of one reduction item (output row m, features n0..n0+7):
+// the LayerNorm-fold vectors and the residual row segment, loaded before the
+// accumulator is ready so that their latency is off the epilogue's path.
+struct ItemInputs {
+  float fs[8], fc[8];
+  uint4 res;
+};
+__device__ __forceinline__ void item_prefetch(const Params& p, int m, int n0, ItemInputs& in) {
+  if (p.ln_mode == 2) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int n = min(n0 + e, p.cols_out - 1);
+      in.fs[e] = p.fold_s[n];
+      in.fc[e] = p.fold_c != nullptr ? p.fold_c[n] : 0.f;
+    }
+  }
+  if (p.residual != nullptr && p.out_dtype != FML_F32 && m < p.rows_out && n0 + 8 <= p.cols_out) {
+    const long long roff = (long long)m * p.ldr + n0;
+    if ((roff & 7) == 0 && (reinterpret_cast<uintptr_t>(p.residual) & 15) == 0)
+      in.res = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.residual) + roff);
+  }
+}
+__device__ __forceinline__ void ln_fold8_pre(const Params& p, const Smem& s, int BNv, int r, const ItemInputs& in,
+                                             float (&x)[8]) {
+  const float2 ms = ld_shared_v2(s.aux + (uint32_t)aux_rowst(BNv) + (uint32_t)(r * 8));
+#pragma unroll
+  for (int e = 0; e < 8; ++e) x[e] = ms.y * (x[e] - ms.x * in.fs[e]) + in.fc[e];
 }
 
 // All-reduce epilogue of one owner CTA: its rows_per features (rows r0.. of
@@ -1193,6 +1224,12 @@ __global__ void __launch_bounds__(threads_of<BN, PROMOTE, FUSED>(), (BN <= 64 &&
       const int i = ti * kTileM + prank * kBM + row;
       if (ksplit > 1 && ep_tid == 0)
         mbar_arrive_expect_tx(bar_recv(s), (uint32_t)((ksplit - 1) * rows_per * BN * 4));
+      // swapped reduction tiles (the decode linears): this thread's first
+      // item's global inputs, fetched while the main loop still runs
+      ItemInputs pre;
+      const bool have_pre = use_red && p.swap && ep_tid < (rows_per / 8) * BN;
+      if (have_pre)
+        item_prefetch(p, tj * BN + ep_tid % BN, ti * kBM + crank * rows_per + (ep_tid / BN) * 8, pre);
       float racc[PROMOTE ? BN : 1];
 #pragma unroll
       for (int e = 0; e < (PROMOTE ? BN : 1); ++e) racc[e] = 0.f;
@@ -1334,7 +1371,10 @@ __global__ void __launch_bounds__(threads_of<BN, PROMOTE, FUSED>(), (BN <= 64 &&
             const int m = tj * BN + c0;
             float x[8];
             red_sum8(base, src_stride, row_bytes, ksplit, x);
-            if (p.ln_mode == 2) ln_fold8(p, s, BN, c0, n0, x);
+            if (p.ln_mode == 2) {
+              if (have_pre && idx == ep_tid) ln_fold8_pre(p, s, BN, c0, pre, x);
+              else ln_fold8(p, s, BN, c0, n0, x);
+            }
             if (p.ar_on) {
               // rounded partial -> staging block [feature][token] for the exchange
               const bool bf = p.fmt == 1;
@@ -1352,7 +1392,8 @@ __global__ void __launch_bounds__(threads_of<BN, PROMOTE, FUSED>(), (BN <= 64 &&
           }
           float x[8];
           red_sum8(base, src_stride, p.swap ? row_bytes : 4, ksplit, x);
-          if (p.swap) epilogue_store8(p, tj * BN + c0, ti * kBM + r0 + rr0, x);
+          if (p.swap) epilogue_store8(p, tj * BN + c0, ti * kBM + r0 + rr0, x,
+                                      have_pre && idx == ep_tid && p.residual != nullptr ? &pre.res : nullptr);
           else epilogue_store8(p, ti * kBM + r0 + rr0, tj * BN + c0, x);
         }
         if (ksplit == 1) epi_bar_sync();  // the buffer is refilled by this CTA's next tile

@@ -167,6 +167,16 @@ def _launch_gemm(a, b, bias, out, act: int, config: KernelConfig, residual=None)
     del ws  # the caching allocator keeps it alive until the stream is done with it
 
 
+def _version_of(t: torch.Tensor) -> int | None:
+    """The tensor's in-place version counter; None for inference tensors
+    (made under torch.inference_mode), which carry none: a compiled graph's
+    weights made that way are taken as constant."""
+    try:
+        return t._version
+    except RuntimeError:
+        return None
+
+
 def _aligned(buf: torch.Tensor, align: int) -> int:
     return (buf.data_ptr() + align - 1) // align * align
 
@@ -208,14 +218,14 @@ class PreparedGemm:
         with torch.cuda.device(b.device):
             _native.call("fml_gemm_pack_b", b.data_ptr(), b.stride(0), b.stride(1), k, n, self.code,
                          _aligned(img, 256), nbytes, torch.cuda.current_stream(b.device).cuda_stream)
-        self._b_const, self._b_image, self._b_version = b, img, b._version
+        self._b_const, self._b_image, self._b_version = b, img, _version_of(b)
 
     def _packed_call(self, a, b, bias, out, residual) -> bool:
         """Run on B's image when b is the packed constant (re-split first if
         it was written in place since); False when b is another tensor."""
         if b is not self._b_const:
             return False
-        if b._version != self._b_version:
+        if _version_of(b) != self._b_version:
             self.pack_constant_b(b)
         m, k = a.shape
         n = b.shape[1]

@@ -228,3 +228,17 @@ def test_cta_pair_tiles(cuda, m, n, k, epi):
     got = kernels.matmul(a.to(cuda), w.to(cuda).t(), None if bias is None else bias.to(cuda), activation=act,
                          residual=None if res is None else res.to(cuda), config=cfg)
     close(got, matmul_epilogue(a, w.t(), bias, activation=act, residual=res), torch.bfloat16)
+
+
+def test_packed_b_inference_tensors(cuda):
+    """A graph compiled under torch.inference_mode holds inference-tensor
+    weights (no version counter): the fp32 split is made once and used."""
+    from forgeml_b200.forgeml import compile as fml_compile
+
+    with torch.inference_mode():
+        lin = torch.nn.Linear(96, 160).to(cuda)
+        x = torch.randn(8, 96, device=cuda)
+        c = fml_compile(torch.nn.Sequential(lin), (x,), backend="triton")
+        got = c(x)
+        want = lin(x)
+    close(got, want.cpu(), torch.float32)
