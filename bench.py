@@ -85,11 +85,27 @@ class Clocks:
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
-        time.sleep(0.15)
+        # nvidia-smi takes a while to start (longer on an 8-GPU host): wait for
+        # its first sample so that the timed region falls in its sampling
+        self._lines_at_start = self._wait_lines(1, 3.0)
         return self
+
+    def _lines(self) -> int:
+        try:
+            return sum(1 for line in self.path.read_text().splitlines() if line.strip())
+        except OSError:
+            return 0
+
+    def _wait_lines(self, n: int, timeout: float) -> int:
+        t0 = time.perf_counter()
+        while self.proc is not None and self._lines() < n and time.perf_counter() - t0 < timeout:
+            time.sleep(0.02)
+        return self._lines()
 
     def __exit__(self, *exc):
         if self.proc is not None:
+            # at least one sample taken after the timed region began
+            self._wait_lines(self._lines_at_start + 1, 0.5)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)

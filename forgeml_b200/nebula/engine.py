@@ -112,30 +112,41 @@ class _CommandWire:
              positions: tuple = ()) -> None:
         b = len(ids)
         t = 0 if tokens is None else int(tokens.shape[1])
-        head = torch.tensor([cmd, b, t, start, *ids], dtype=torch.int64)
-        tail = torch.tensor(list(positions), dtype=torch.int64)
         body_words = b + b * t + len(positions)
-        nb = self.device.type == "cuda"  # host-asynchronous copies only into device memory
-        frame = torch.zeros(self.frame_words, dtype=torch.int64, device=self.device)
         if 4 + body_words <= self.frame_words:
-            body = frame[4:4 + body_words]
-            frame[:4].copy_(head[:4], non_blocking=nb)
-        else:
-            frame[:4].copy_(head[:4], non_blocking=nb)
+            # the whole message in one frame, assembled on the host and copied
+            # to the device once (tokens that already live there are copied
+            # on the device)
+            host = torch.zeros(self.frame_words, dtype=torch.int64)
+            host[:4 + b] = torch.tensor([cmd, b, t, start, *ids], dtype=torch.int64)
+            on_host = tokens is not None and tokens.device.type == "cpu"
+            if t and on_host:
+                host[4 + b:4 + b + b * t] = tokens.reshape(-1)
+            if positions:
+                host[4 + b + b * t:4 + body_words] = torch.tensor(list(positions), dtype=torch.int64)
+            frame = host.to(self.device) if self.device.type == "cuda" else host
+            if t and not on_host:
+                frame[4 + b:4 + b + b * t].copy_(tokens.reshape(-1))
             self.broadcast(frame)
-            frame = body = torch.empty(body_words, dtype=torch.int64, device=self.device)
-        body[:b].copy_(head[4:], non_blocking=nb)
-        if t:
-            body[b:b + b * t].copy_(tokens.reshape(-1), non_blocking=nb)
+            return
+        frame = torch.zeros(self.frame_words, dtype=torch.int64)
+        frame[:4] = torch.tensor([cmd, b, t, start], dtype=torch.int64)
+        self.broadcast(frame.to(self.device))
+        body = torch.empty(body_words, dtype=torch.int64)
+        body[:b] = torch.tensor(list(ids), dtype=torch.int64)
         if positions:
-            body[b + b * t:].copy_(tail, non_blocking=nb)
-        self.broadcast(frame)
+            body[b + b * t:] = torch.tensor(list(positions), dtype=torch.int64)
+        body = body.to(self.device)
+        if t:
+            body[b:b + b * t].copy_(tokens.reshape(-1))
+        self.broadcast(body)
 
     # ------------------------------------------------------------ worker
     def receive(self) -> _Command:
         frame = torch.zeros(self.frame_words, dtype=torch.int64, device=self.device)
         self.broadcast(frame)
-        cmd, b, t, start = frame[:4].tolist()
+        words = frame.tolist()  # one device -> host read of the whole frame
+        cmd, b, t, start = words[:4]
         if cmd == CMD_STOP:
             if (b, t, start) != (0, 0, 0):
                 raise EngineFailed("malformed STOP header")
@@ -156,10 +167,12 @@ class _CommandWire:
         body_words = b + b * t + extra
         if 4 + body_words <= self.frame_words:
             body = frame[4:4 + body_words]
+            bw = words[4:4 + body_words]
         else:
             body = torch.zeros(body_words, dtype=torch.int64, device=self.device)
             self.broadcast(body)
-        head = body[:b].tolist() + (body[b + b * t:].tolist() if extra else [])
+            bw = body.tolist()
+        head = bw[:b] + (bw[b + b * t:] if extra else [])
         tokens = body[b:b + b * t].view(b, t) if t else None
         return _Command(cmd, b, t, start, tuple(head[:b]), tokens, tuple(head[b:]))
 

@@ -226,11 +226,14 @@ class ShardedDecoder(nn.Module):
             es = torch.empty((), dtype=dtype).element_size()
             slot = max(16, (max(max_requests, 32) * h * es + 15) // 16 * 16)
             self._peer_ar = peer.PeerAllReduce(context, max_bytes=slot)
-        # Decode steps of 4 or more TP ranks run as several batch lanes
-        # (_core), each lane reducing through its own peer context: two by
-        # default, up to MAX_LANES (every rank creates the same contexts, in
-        # the same order).
-        self.decode_lanes = 2 if context.tp_size >= 4 else 1
+        # Decode steps of 4 or more TP ranks can run as several batch lanes
+        # (_core), each lane reducing through its own peer context, up to
+        # MAX_LANES (every rank creates the same contexts, in the same
+        # order).  One lane is the default: measured at TP8 on B200s (c4,
+        # batch 32), two lanes took 1.32 ms per step against 0.79 ms for
+        # one -- the lanes' launches contend instead of filling each other's
+        # latency.
+        self.decode_lanes = 1
         self._lane_ars = [self._peer_ar]
         self._lane_streams: list = []
         if self._peer_ar is not None and context.pp_size == 1 and context.tp_size >= 4:
