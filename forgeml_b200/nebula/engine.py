@@ -12,11 +12,15 @@ order: the header [cmd, B, T, start_pos], then the B request ids, then the
 B x T tokens (STEP), the B ids (RELEASE) or nothing (STOP).  They travel in one
 broadcast of a fixed frame of 4 + 3 * max_requests words when the message fits
 (every decode step), otherwise as the header frame followed by one broadcast
-of ids and tokens.  One command extends the reference's set: STEP_AT, a
+of ids and tokens.  Two commands extend the reference's set: STEP_AT, a
 single-token step whose requests each sit at their own position (the decode
-phase of ``generate_mixed``).  On an NCCL world the frame is assembled on the device, so
-the leader's tokens (on the device during ``generate``) never pass through the
-host.
+phase of ``generate_mixed``), and PREFILL, the prefills of several
+equal-length groups in one command with their logits broadcasts deferred
+(``generate_mixed`` over pipeline stages: stage s + 1 prefills one group while
+stage s prefills the next).  The frame is assembled on the host and copied to
+the device once; tokens already on the device (the leader's during
+``generate``) are copied into it there, never through the host.  A worker
+reads a frame back to the host once.
 
 Cache preflight.  Each rank checks a STEP against its own cache replica
 (admission of new requests, or positions of running ones) and the ranks agree
@@ -56,6 +60,14 @@ CMD_RELEASE = 2
 # which every request sits at its own position.  Header [3, B, 1, 0], then the
 # B ids, the B tokens and the B positions.
 CMD_STEP_AT = 3
+# Extension (generate_mixed over pipeline stages): the prefills of several
+# equal-length groups in one command.  Header [4, G, W, 0], then W body words:
+# b_1, t_1, ..., b_G, t_G, every group's ids, every group's tokens.  All ranks
+# agree on the whole batch once, run the groups back to back and broadcast the
+# groups' last-position logits from the last stage only after every group has
+# been issued, so that stage s + 1 prefills group g while stage s prefills
+# group g + 1.
+CMD_PREFILL = 4
 _GENERATE_ID_BASE = 1 << 62  # engine-issued request ids start here
 _MAX_REQUEST_ID = _GENERATE_ID_BASE - 1  # caller-chosen ids stay at or below this
 _ID_LIMIT = 1 << 63
@@ -93,6 +105,7 @@ class _Command(NamedTuple):
     ids: tuple
     tokens: torch.Tensor | None
     positions: tuple = ()
+    groups: tuple = ()  # CMD_PREFILL: ((ids, tokens [b, t]), ...)
 
 
 class _CommandWire:
@@ -141,6 +154,45 @@ class _CommandWire:
             body[b:b + b * t].copy_(tokens.reshape(-1))
         self.broadcast(body)
 
+    def send_prefill(self, groups: list) -> None:
+        """CMD_PREFILL: groups of (ids, host tokens [b, t])."""
+        words = [v for ids, tok in groups for v in (len(ids), int(tok.shape[1]))]
+        words += [r for ids, _ in groups for r in ids]
+        body = torch.tensor(words, dtype=torch.int64)
+        body = torch.cat([body] + [tok.reshape(-1).to(torch.int64) for _, tok in groups])
+        n = int(body.numel())
+        head = torch.tensor([CMD_PREFILL, len(groups), n, 0], dtype=torch.int64)
+        if 4 + n <= self.frame_words:
+            frame = torch.zeros(self.frame_words, dtype=torch.int64)
+            frame[:4], frame[4:4 + n] = head, body
+            self.broadcast(frame.to(self.device))
+            return
+        frame = torch.zeros(self.frame_words, dtype=torch.int64)
+        frame[:4] = head
+        self.broadcast(frame.to(self.device))
+        self.broadcast(body.to(self.device))
+
+    def _receive_prefill(self, frame: torch.Tensor, words: list, g: int, n: int) -> _Command:
+        if not (0 < g <= self.max_requests and 0 < n <= 3 * self.max_requests * (self.max_seq_len + 1)):
+            raise EngineFailed("malformed PREFILL header")
+        if 4 + n <= self.frame_words:
+            body = frame[4:4 + n]
+            bw = words[4:4 + n]
+        else:
+            body = torch.zeros(n, dtype=torch.int64, device=self.device)
+            self.broadcast(body)
+            bw = body.tolist()
+        sizes = [(bw[2 * i], bw[2 * i + 1]) for i in range(g)]
+        total_ids = sum(b for b, _ in sizes)
+        if any(b <= 0 or t <= 0 or t > self.max_seq_len for b, t in sizes) or total_ids > self.max_requests or \
+                2 * g + total_ids + sum(b * t for b, t in sizes) != n:
+            raise EngineFailed("malformed PREFILL body")
+        groups, at_id, at_tok = [], 2 * g, 2 * g + total_ids
+        for b, t in sizes:
+            groups.append((tuple(bw[at_id:at_id + b]), body[at_tok:at_tok + b * t].view(b, t)))
+            at_id, at_tok = at_id + b, at_tok + b * t
+        return _Command(CMD_PREFILL, g, 0, 0, (), None, (), tuple(groups))
+
     # ------------------------------------------------------------ worker
     def receive(self) -> _Command:
         frame = torch.zeros(self.frame_words, dtype=torch.int64, device=self.device)
@@ -151,6 +203,10 @@ class _CommandWire:
             if (b, t, start) != (0, 0, 0):
                 raise EngineFailed("malformed STOP header")
             return _Command(cmd, 0, 0, 0, (), None)
+        if cmd == CMD_PREFILL:
+            if start != 0:
+                raise EngineFailed("malformed PREFILL header")
+            return self._receive_prefill(frame, words, b, t)
         if cmd == CMD_STEP:
             if not (0 < b <= self.max_requests and 0 < t <= self.max_seq_len and start >= 0
                     and start + t <= self.max_seq_len):
@@ -257,6 +313,10 @@ class Engine:
         self._healthy = True
         self._closed = False
         self._lock = threading.RLock()
+        # generate_mixed over pipeline stages sends its prefill groups as one
+        # CMD_PREFILL (stages overlap on consecutive groups); False sends them
+        # as separate steps, each waiting for the last stage
+        self.pipelined_prefill = context.pp_size > 1
         self._next_generated_id = _GENERATE_ID_BASE
 
     def _handshake(self, dtype: torch.dtype) -> None:
@@ -347,6 +407,27 @@ class Engine:
         self._health.after_step(agreed)
         return logits
 
+    def _run_prefill(self, groups) -> list:
+        """CMD_PREFILL on this rank: one admission check and agreement for
+        every group, the groups' prefills back to back with their logits
+        broadcasts deferred, then the broadcasts in group order.  Returns each
+        group's last-position logits [b, 1, V]."""
+        all_ids = tuple(r for ids, _ in groups for r in ids)
+        err = self._preflight_error(all_ids, 0, 1)
+        agreed = None
+        if self._multi:
+            agreed = torch.tensor([err], dtype=torch.int64, device=self._wire.device)
+            dist.all_reduce(agreed, op=dist.ReduceOp.MAX)
+        if err:
+            raise EngineFailed("cache preflight failed")
+        dev = self.context.device
+        with torch.inference_mode():
+            for ids, tok in groups:
+                self.decoder.forward(tok.to(dev), tuple(ids), 0, last_only=True, defer_broadcast=True)
+            logits = self.decoder.flush_deferred()
+        self._health.after_step(agreed)
+        return logits
+
     def forward(self, tokens: torch.Tensor, request_ids: tuple[int, ...], start_pos: int = 0,
                 _internal: bool = False, _last_only: bool = False) -> torch.Tensor:
         with self._lock:
@@ -378,6 +459,8 @@ class Engine:
                     self._run_step(c.tokens.to(self.context.device), c.ids, c.start, False)
                 elif c.cmd == CMD_STEP_AT:
                     self._run_step(c.tokens.to(self.context.device), c.ids, c.positions, False)
+                elif c.cmd == CMD_PREFILL:
+                    self._run_prefill(c.groups)
                 else:
                     self.decoder.cache.release(c.ids)
         except Exception as exc:
@@ -510,10 +593,25 @@ class Engine:
             try:
                 dev = self.context.device
                 cur = torch.empty(len(prompts), dtype=torch.long, device=dev)
-                for plen, members in groups.items():
-                    logits = self.forward(torch.tensor([prompts[i] for i in members], dtype=torch.long),
-                                          tuple(ids[i] for i in members), 0, _internal=True, _last_only=True)
-                    cur.index_copy_(0, torch.tensor(members, device=dev), self._argmax(logits))
+                if self._multi and self.pipelined_prefill:
+                    # pipeline stages: every group's prefill in one command
+                    batch = [(tuple(ids[i] for i in members), torch.tensor([prompts[i] for i in members],
+                                                                           dtype=torch.long))
+                             for members in groups.values()]
+                    try:
+                        self._health.check(wait=False)
+                        self._wire.send_prefill(batch)
+                        group_logits = self._run_prefill(batch)
+                    except Exception as exc:
+                        self._invalidate()
+                        raise EngineFailed("engine execution failed") from exc
+                    for members, logits in zip(groups.values(), group_logits):
+                        cur.index_copy_(0, torch.tensor(members, device=dev), self._argmax(logits))
+                else:
+                    for plen, members in groups.items():
+                        logits = self.forward(torch.tensor([prompts[i] for i in members], dtype=torch.long),
+                                              tuple(ids[i] for i in members), 0, _internal=True, _last_only=True)
+                        cur.index_copy_(0, torch.tensor(members, device=dev), self._argmax(logits))
                 produced = [cur]
                 positions = tuple(len(p) for p in prompts)
                 for _ in range(1, max_new_tokens):

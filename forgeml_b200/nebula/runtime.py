@@ -217,6 +217,7 @@ class ShardedDecoder(nn.Module):
                              max_seq_len=config.max_seq_len, max_requests=max_requests, device=dev, dtype=dtype)
         self._hl_hd = hl_hd
         self._graphs: dict[int, dict] = {}
+        self._deferred: list[torch.Tensor] = []  # logits awaiting flush_deferred()
         self.use_cuda_graphs = True
         # Decode-step TP reductions (B x 1 x d per call) go through the NVLink
         # peer all-reduce fused with the residual add; collective over the TP
@@ -438,7 +439,7 @@ class ShardedDecoder(nn.Module):
 
     # ------------------------------------------------------------------ API
     def forward(self, tokens: torch.Tensor, request_ids: tuple[int, ...], start_pos,
-                last_only: bool = False) -> torch.Tensor:
+                last_only: bool = False, defer_broadcast: bool = False) -> torch.Tensor:
         """Logits [B, T or 1, V] of one step.  ``start_pos`` is the position of
         the batch's first token (0 reserves the requests), or -- for
         single-token steps of requests already in the cache -- a sequence with
@@ -473,7 +474,10 @@ class ShardedDecoder(nn.Module):
         tt = 1 if last_only else t
         if logits is None:
             logits = torch.empty((b * tt, v), dtype=self.dtype, device=ctx.device)
-        if ctx.pp_size > 1:
+        if defer_broadcast:
+            # the logits travel later, in order, with flush_deferred()
+            self._deferred.append(logits.view(b, 1 if last_only else t, v))
+        elif ctx.pp_size > 1:
             # Only the last pipeline stage computes logits.  (With tensor
             # parallelism alone every rank already holds the same logits: the
             # TP reductions give bit-identical results on all ranks and the
@@ -486,6 +490,19 @@ class ShardedDecoder(nn.Module):
             for r, p in zip(request_ids, positions):
                 self.cache.advance((r,), p + t)
         return logits.view(b, tt, v)
+
+    def flush_deferred(self) -> list[torch.Tensor]:
+        """Broadcast, from the last pipeline stage and in call order, the
+        logits of every forward(..., defer_broadcast=True) since the last
+        flush; returns them ([B, T or 1, V] each).  Deferring lets the stages
+        of a pipeline work on consecutive steps at once: no rank waits for the
+        last stage between them."""
+        out, self._deferred = self._deferred, []
+        ctx = self.context
+        if ctx.pp_size > 1:
+            for lg in out:
+                dist.broadcast(lg, src=(ctx.pp_size - 1) * ctx.tp_size)
+        return out
 
     def _replay(self, tokens: torch.Tensor, slots_host: torch.Tensor, starts_host: torch.Tensor,
                 b: int) -> torch.Tensor:

@@ -43,6 +43,7 @@ class CpuShardedDecoder:
         self.pos = ref.position_embedding.weight.detach()
         self.lnf = (ref.final_norm.weight.detach(), ref.final_norm.bias.detach())
         self.head = ref.lm_head.weight.detach()
+        self._deferred = []
         self.hl = config.num_heads // tp
         self.hd = h // config.num_heads
         self.cache = KVCache(layer_ids=self.owned_layer_ids, num_heads=self.hl, head_dim=self.hd,
@@ -50,7 +51,7 @@ class CpuShardedDecoder:
                              device=torch.device("cpu"), dtype=dtype)
 
     @torch.inference_mode()
-    def forward(self, tokens, request_ids, start_pos, last_only=False):
+    def forward(self, tokens, request_ids, start_pos, last_only=False, defer_broadcast=False):
         if not isinstance(start_pos, int):  # per-request positions: one request at a time
             return torch.cat([self.forward(tokens[i:i + 1], (r,), int(p), last_only)
                               for i, (r, p) in enumerate(zip(request_ids, start_pos))])
@@ -88,6 +89,15 @@ class CpuShardedDecoder:
         else:
             xs = x[:, -1:] if last_only else x
             logits = F.linear(F.layer_norm(xs, (h,), *self.lnf, 1e-5), self.head)
-        if ctx.world_size > 1:
+        if defer_broadcast:
+            self._deferred.append(logits)
+        elif ctx.world_size > 1:
             dist.broadcast(logits, src=(ctx.pp_size - 1) * ctx.tp_size)
         return logits
+
+    def flush_deferred(self):
+        out, self._deferred = self._deferred, []
+        if self.context.world_size > 1:
+            for lg in out:
+                dist.broadcast(lg, src=(self.context.pp_size - 1) * self.context.tp_size)
+        return out

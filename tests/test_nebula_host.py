@@ -204,6 +204,47 @@ def test_wire_frames_split_when_the_message_is_long():
     assert c.tokens.tolist() == [[1, 2, 3], [4, 5, 6]]
 
 
+@pytest.mark.parametrize("max_requests", [4, 2])
+def test_wire_prefill_batches_round_trip(max_requests):
+    """CMD_PREFILL: groups of equal-length prompts in one command (in the
+    fixed frame when they fit, else header frame + body), rebuilt word for
+    word on the receiving side."""
+    from forgeml_b200.nebula.engine import CMD_PREFILL, _CommandWire
+
+    groups = [((11,), torch.tensor([[1, 2, 3]])), ((12, 13), torch.tensor([[4, 5], [6, 7]]))]
+    if max_requests == 2:  # 3 ids do not fit a 2-request engine's admission, so use smaller groups
+        groups = [((11,), torch.tensor([[1, 2, 3, 4, 5, 6, 7]])), ((12,), torch.tensor([[8, 9]]))]
+    w = _CommandWire(max_requests=max_requests, max_seq_len=16, device=torch.device("cpu"))
+    sent = []
+    w.broadcast = lambda t: sent.append(t.clone())
+    w.send_prefill(groups)
+    body = [v for ids, tok in groups for v in (len(ids), tok.shape[1])] + [r for ids, _ in groups for r in ids]
+    body += [x for _, tok in groups for x in tok.reshape(-1).tolist()]
+    head = [CMD_PREFILL, len(groups), len(body), 0]
+    if 4 + len(body) <= w.frame_words:
+        assert [t.tolist() for t in sent] == [head + body + [0] * (w.frame_words - 4 - len(body))]
+    else:
+        assert [t.tolist() for t in sent] == [head + [0] * (w.frame_words - 4), body]
+    frames = iter(sent)
+    r = _CommandWire(max_requests=max_requests, max_seq_len=16, device=torch.device("cpu"))
+    r.broadcast = lambda t: t.copy_(next(frames))
+    c = r.receive()
+    assert c.cmd == CMD_PREFILL and len(c.groups) == len(groups)
+    for (ids, tok), (gids, gtok) in zip(groups, c.groups):
+        assert tuple(gids) == ids and gtok.tolist() == tok.tolist()
+
+
+def test_wire_rejects_malformed_prefill():
+    from forgeml_b200.nebula.engine import _CommandWire
+
+    # header fits, body sizes inconsistent with the word count
+    for words in ([4, 1, 6, 0, 1, 2, 7, 1, 2, 3], [4, 0, 3, 0], [4, 1, 4, 1, 1, 1, 7, 1], [4, 1, 4, 0, 1, 17, 7, 1]):
+        r = _CommandWire(max_requests=2, max_seq_len=16, device=torch.device("cpu"))
+        r.broadcast = lambda t, words=words: t[:len(words)].copy_(torch.tensor(words))
+        with pytest.raises(EngineFailed):
+            r.receive()
+
+
 def test_wire_rejects_malformed_headers():
     from forgeml_b200.nebula.engine import _CommandWire
 
