@@ -31,7 +31,9 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-sys.path.insert(0, os.environ.get("REFERENCE_SRC", "/root/reference/src"))
+if "REFERENCE_SRC" not in os.environ:
+    sys.exit("set REFERENCE_SRC to the reference project's src directory (the one holding forgeml/ and nebula/)")
+sys.path.insert(0, os.environ["REFERENCE_SRC"])
 sys.path.insert(0, str(REPO))
 
 from forgeml import compile as ref_compile  # noqa: E402
