@@ -126,3 +126,42 @@ def test_worker_failure_propagates():
         procs = _spawn(_failing, (f"{d}/store",), 2, 60)
         assert procs.processes[0].exitcode == 0
         assert procs.processes[1].exitcode != 0
+
+
+def _dying_in_prefill(rank, store):
+    """TP1 x PP2: the second stage dies inside a pipelined PREFILL command."""
+    from forgeml_b200.nebula import DecoderConfig, Engine, EngineFailed, ParallelContext
+    from tests.cpu_engine import CpuShardedDecoder
+
+    class _Dying(CpuShardedDecoder):
+        def forward(self, *args, defer_broadcast=False, **kw):
+            if defer_broadcast:
+                raise RuntimeError("deliberate stage failure during prefill")
+            return super().forward(*args, defer_broadcast=defer_broadcast, **kw)
+
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", init_method=f"file://{store}", rank=rank, world_size=2,
+                            timeout=timedelta(seconds=10))
+    ctx = ParallelContext.from_env(tp_size=1, pp_size=2, timeout_s=10)
+    engine = Engine(DecoderConfig(**CFG), context=ctx, max_requests=4,
+                    decoder_factory=CpuShardedDecoder if rank == 0 else _Dying)
+    if rank == 0:
+        assert engine.pipelined_prefill
+        try:
+            engine.generate_mixed([[1, 2, 3], [4, 5]], 2)
+        except EngineFailed:
+            assert not engine.healthy and engine.decoder.cache.active_requests == 0
+            try:
+                engine.generate_mixed([[1, 2]], 1)
+            except EngineFailed:
+                return
+            raise AssertionError("a failed engine accepted another request")
+        raise AssertionError("generate_mixed did not fail after a stage died in prefill")
+    engine.serve()
+
+
+def test_stage_failure_in_pipelined_prefill_poisons_the_leader():
+    with tempfile.TemporaryDirectory() as d:
+        procs = _spawn(_dying_in_prefill, (f"{d}/store",), 2, 60)
+        assert procs.processes[0].exitcode == 0
+        assert procs.processes[1].exitcode != 0
