@@ -165,3 +165,56 @@ def test_stage_failure_in_pipelined_prefill_poisons_the_leader():
         procs = _spawn(_dying_in_prefill, (f"{d}/store",), 2, 60)
         assert procs.processes[0].exitcode == 0
         assert procs.processes[1].exitcode != 0
+
+
+def _batcher_worker(rank, store):
+    """TP2 x PP2 serving as in config 5: an AsyncBatcher that mixes prompt
+    lengths in front of the leader; workers in serve()."""
+    import asyncio
+
+    from forgeml_b200.nebula import AsyncBatcher, DecoderConfig, Engine, ParallelContext, TinyDecoder
+    from tests.cpu_engine import CpuShardedDecoder
+
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", init_method=f"file://{store}", rank=rank, world_size=4,
+                            timeout=timedelta(seconds=20))
+    cfg = DecoderConfig(**CFG)
+    ctx = ParallelContext.from_env(tp_size=2, pp_size=2, timeout_s=20)
+    engine = Engine(cfg, context=ctx, max_requests=4, decoder_factory=CpuShardedDecoder)
+    try:
+        if rank == 0:
+            ref = TinyDecoder(cfg).eval()
+            prompts = [[1, 2, 3], [4], [5, 6, 7, 8], [9, 10]]
+            batches = []
+            mixed = engine.generate_mixed
+
+            def recording(ps, n):
+                batches.append(sorted(len(p) for p in ps))
+                return mixed(ps, n)
+
+            engine.generate_mixed = recording
+
+            async def go():
+                async with AsyncBatcher(engine, max_batch_size=4, batch_window_ms=50,
+                                        mix_prompt_lengths=True) as b:
+                    return await asyncio.gather(*(b.submit(p, 3) for p in prompts))
+
+            assert asyncio.run(go()) == [_ref_generate(ref, p, 3) for p in prompts]
+            # every request served once, and prompts of different lengths shared a batch
+            assert sorted(n for b in batches for n in b) == [1, 2, 3, 4]
+            assert max(len(set(b)) for b in batches) > 1
+            assert engine.decoder.cache.active_requests == 0
+        else:
+            engine.serve()
+            assert engine.decoder.cache.active_requests == 0
+    finally:
+        engine.close()
+        ctx.close()
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def test_batcher_mixing_prompt_lengths_on_tp2_pp2():
+    with tempfile.TemporaryDirectory() as d:
+        procs = _spawn(_batcher_worker, (f"{d}/store",), 4, 90)
+        assert [p.exitcode for p in procs.processes] == [0] * 4
