@@ -218,3 +218,40 @@ def test_batcher_mixing_prompt_lengths_on_tp2_pp2():
     with tempfile.TemporaryDirectory() as d:
         procs = _spawn(_batcher_worker, (f"{d}/store",), 4, 90)
         assert [p.exitcode for p in procs.processes] == [0] * 4
+
+
+def _preflight_all(rank, store):
+    """A command the cache replicas reject (a reserved id at position 0)
+    fails on every rank at once: the leader and the worker both end poisoned
+    with their caches cleared, none waiting on the other."""
+    from forgeml_b200.nebula import DecoderConfig, Engine, EngineFailed, ParallelContext
+    from tests.cpu_engine import CpuShardedDecoder
+
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", init_method=f"file://{store}", rank=rank, world_size=2,
+                            timeout=timedelta(seconds=20))
+    ctx = ParallelContext.from_env(tp_size=1, pp_size=2, timeout_s=20)
+    engine = Engine(DecoderConfig(**CFG), context=ctx, max_requests=4, decoder_factory=CpuShardedDecoder)
+    if rank == 0:
+        engine.forward(torch.tensor([[1, 2, 3]]), (5,), 0)
+        t0 = time.monotonic()
+        try:
+            engine.forward(torch.tensor([[4, 5]]), (5,), 0)
+        except EngineFailed as exc:
+            assert "preflight" in str(exc.__cause__)
+            assert not engine.healthy and engine.decoder.cache.active_requests == 0
+            assert time.monotonic() - t0 < 10  # no collective timeout was waited out
+            return
+        raise AssertionError("a reserved id was admitted again")
+    try:
+        engine.serve()
+    except EngineFailed:
+        assert not engine.healthy and engine.decoder.cache.active_requests == 0
+        return
+    raise AssertionError("the worker served past a failed preflight")
+
+
+def test_preflight_failure_fails_every_rank_together():
+    with tempfile.TemporaryDirectory() as d:
+        procs = _spawn(_preflight_all, (f"{d}/store",), 2, 60)
+        assert [p.exitcode for p in procs.processes] == [0, 0]
