@@ -950,6 +950,11 @@ def run_case(args) -> None:
     gemm-fused   the decode step's fused launches at batch 32 for the TP
                  shard of --tp ranks: LayerNorm-folded QKV + KV append, o,
                  folded up + tanh GELU, down (residuals at TP1)
+    gemm-l2      the c4 decode GEMMs at batch 32 as fused launches with the
+                 residual epilogue, 20 launches replayed from a CUDA graph on
+                 one L2-resident weight ("warm") and on 20 copies of it
+                 ("cold", 20 x the bytes > L2): how much a launch depends on
+                 where its weights come from
     gemm         8192^3 bf16 + bias + GELU
     c2           the compiled config-2 encoder block (bf16, then fp32): every
                  instruction's device time alone and the whole call
@@ -1041,6 +1046,21 @@ def run_case(args) -> None:
             us = _graph_time_us(lst * max(1, reps // n_layers)) / (len(lst) * max(1, reps // n_layers))
             res[k] = {"us": us, "GB/s": algo[k] / (us * 1e-6) / 1e9, "algo_bytes": algo[k], "tp_shard": tp}
         res["chain_avg_us"] = us_chain
+    elif args.case == "gemm-l2":
+        from forgeml_b200.linear import PackedLinear
+
+        m, n_copies = BATCH, 20
+        for name, n, k in (("up", 8192, 2048), ("down", 2048, 8192), ("qkv", 6144, 2048), ("o", 2048, 2048)):
+            ws = [PackedLinear((torch.randn(n, k, device=dev, generator=g) * 0.02).to(torch.bfloat16))
+                  for _ in range(n_copies)]
+            x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+            r = torch.randn(m, n, device=dev, generator=g).to(torch.bfloat16)
+            out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+            warm = _graph_time_us([lambda: ws[0].fused(x, out, residual=r)] * n_copies) / n_copies
+            cold = _graph_time_us([lambda w=w: w.fused(x, out, residual=r) for w in ws]) / n_copies
+            res[name] = {"warm_us": warm, "cold_us": cold, "weight_mb": n * k * 2 / 1e6}
+            del ws
+            torch.cuda.empty_cache()
     elif args.case == "gemm":
         res["gemm"] = gemm_headline(dev)
     elif args.case == "c2":
@@ -1072,7 +1092,7 @@ def main() -> None:
     ap.add_argument("--cpu-steps", type=int, default=3)
     ap.add_argument("--cpu-layers", type=int, default=None, help="time this many layers of the CPU oracle")
     ap.add_argument("--tp", type=int, default=1, help="--case gemm-fused: TP shard shapes of this degree")
-    ap.add_argument("--case", choices=("attention", "gemm-decode", "gemm-fused", "gemm", "c2"), default=None,
+    ap.add_argument("--case", choices=("attention", "gemm-decode", "gemm-fused", "gemm-l2", "gemm", "c2"), default=None,
                     help="run one kernel micro-benchmark instead of the decode bench")
     ap.add_argument("--workload", choices=("c4", "c5"), default="c4",
                     help="c5: serve config 5 through the AsyncBatcher over TP x PP (launch with torchrun)")
