@@ -16,7 +16,9 @@ message texts.  The storage is designed for the decode kernels instead:
 * bookkeeping is one ``_Ticket`` per request: its slot and the number of
   positions held for each owned layer.  The fused decode step writes K/V of
   every layer inside its kernels and records the new length of all layers at
-  once (``advance``).
+  once (``advance``), so a ticket keeps one count while its layers agree and
+  per-layer counts only while the reference-style ``append`` moves them
+  apart: a step's bookkeeping is per request, not per request and layer.
 
 ``append`` keeps the reference's contract (write [B, heads, T, hd] at
 ``start_pos``, return the stacked prefixes [B, heads, end, hd] as a copy) for
@@ -42,13 +44,32 @@ def _plain_int(v) -> bool:
 
 
 class _Ticket:
-    """A reserved request: its pool slot and positions held per owned layer."""
+    """A reserved request: its pool slot and the positions held per owned
+    layer -- ``level`` while every owned layer holds the same count
+    (``per_layer`` None), else ``per_layer`` {layer id: count}."""
 
-    __slots__ = ("slot", "held")
+    __slots__ = ("slot", "level", "per_layer")
 
-    def __init__(self, slot: int, layer_ids: tuple[int, ...]):
+    def __init__(self, slot: int):
         self.slot = slot
-        self.held = dict.fromkeys(layer_ids, 0)
+        self.level = 0
+        self.per_layer: dict[int, int] | None = None
+
+    def counts(self, layer_ids: tuple[int, ...]) -> dict[int, int]:
+        """{layer id: positions held}, in ``layer_ids`` order."""
+        return dict.fromkeys(layer_ids, self.level) if self.per_layer is None else self.per_layer
+
+    def set_all(self, end: int) -> None:
+        self.level, self.per_layer = end, None
+
+    def set_layer(self, layer_ids: tuple[int, ...], layer_id: int, end: int) -> None:
+        if self.per_layer is None:
+            if end == self.level:
+                return
+            self.per_layer = dict.fromkeys(layer_ids, self.level)
+        self.per_layer[layer_id] = end
+        if all(n == end for n in self.per_layer.values()):
+            self.set_all(end)
 
 
 class KVCache:
@@ -75,6 +96,9 @@ class KVCache:
         self.v_pool = {lid: torch.empty(pool_shape, device=device, dtype=dtype) for lid in ids}
         self._tickets: dict[int, _Ticket] = {}
         self._free_slots = list(range(max_requests))  # min-heap: the lowest free slot goes first
+        # the last request-id tuple check_ids accepted: a decode loop passes
+        # the same tuple every step, and a tuple of ints cannot change
+        self._ids_ok: tuple | None = None
 
     # ----------------------------------------------------------- inspection
     @property
@@ -89,8 +113,9 @@ class KVCache:
         return [self._tickets[r].slot for r in request_ids]
 
     # ---------------------------------------------------------- validation
-    @staticmethod
-    def check_ids(request_ids: tuple[int, ...]) -> None:
+    def check_ids(self, request_ids: tuple[int, ...]) -> None:
+        if request_ids is self._ids_ok:
+            return
         if not request_ids:
             raise CacheError("request_ids must be non-empty")
         seen = set()
@@ -100,6 +125,8 @@ class KVCache:
             if r in seen:
                 raise CacheError("duplicate request ids")
             seen.add(r)
+        if type(request_ids) is tuple:
+            self._ids_ok = request_ids
 
     def check_admission(self, request_ids: tuple[int, ...]) -> None:
         """Raise CacheError unless ``reserve(request_ids)`` would succeed."""
@@ -130,7 +157,11 @@ class KVCache:
         if start_pos < 0 or start_pos + count > self.max_seq_len:
             raise CacheError("positions out of range")
         for r, tk in zip(request_ids, tickets):
-            for lid, n in tk.held.items():
+            if tk.per_layer is None:
+                if tk.level != start_pos:
+                    raise CacheError(f"layer {self.layer_ids[0]} for request {r} at {tk.level}, expected {start_pos}")
+                continue
+            for lid, n in tk.per_layer.items():
                 if n != start_pos:
                     raise CacheError(f"layer {lid} for request {r} at {n}, expected {start_pos}")
 
@@ -138,15 +169,13 @@ class KVCache:
     def reserve(self, request_ids: tuple[int, ...]) -> None:
         self.check_admission(request_ids)
         for r in request_ids:
-            self._tickets[r] = _Ticket(heapq.heappop(self._free_slots), self.layer_ids)
+            self._tickets[r] = _Ticket(heapq.heappop(self._free_slots))
 
     def advance(self, request_ids: tuple[int, ...], end: int) -> None:
         """Record that every owned layer of these requests now holds ``end``
         positions (the decode kernels wrote them)."""
         for r in request_ids:
-            held = self._tickets[r].held
-            for lid in held:
-                held[lid] = end
+            self._tickets[r].set_all(end)
 
     def append(self, layer_id: int, request_ids: tuple[int, ...], key: torch.Tensor, value: torch.Tensor,
                start_pos: int) -> tuple[torch.Tensor, torch.Tensor]:
@@ -167,7 +196,7 @@ class KVCache:
                 kp[tk.slot, :, start_pos:end].copy_(key[i])
                 vp[tk.slot, :, start_pos:end].copy_(value[i])
         for tk in tickets:
-            tk.held[layer_id] = end
+            tk.set_layer(self.layer_ids, layer_id, end)
         index = torch.tensor([tk.slot for tk in tickets], device=self.device)
         return kp.index_select(0, index)[:, :, :end], vp.index_select(0, index)[:, :, :end]
 
@@ -193,7 +222,7 @@ class KVCache:
         # Layers are appended one after another within a step: the layer being
         # written must be at start_pos, the others at start_pos or already past it.
         for r, tk in zip(request_ids, tickets):
-            for lid, n in tk.held.items():
+            for lid, n in tk.counts(self.layer_ids).items():
                 if lid == layer_id and n != start_pos:
                     raise CacheError(f"layer {layer_id} request {r} at {n}, expected {start_pos}")
                 if lid != layer_id and n not in (start_pos, start_pos + count):

@@ -313,6 +313,8 @@ class Engine:
         self._healthy = True
         self._closed = False
         self._lock = threading.RLock()
+        self._ids_ok: tuple | None = None  # the last request-id tuple _validate_request accepted
+        self._ids_ok_internal = False  # ... and whether under the engine's own (internal) rules
         # generate_mixed over pipeline stages sends its prefill groups as one
         # CMD_PREFILL (stages overlap on consecutive groups); False sends them
         # as separate steps, each waiting for the last stage
@@ -363,15 +365,22 @@ class Engine:
             raise TypeError("start_pos must be an integer")
         if start_pos < 0 or start_pos + t > self.config.max_seq_len:
             raise ValueError("sequence exceeds max_seq_len")
-        if len(set(request_ids)) != b:
-            raise ValueError("duplicate request ids")
-        for r in request_ids:
-            if not _plain_int(r) or r < 0:
-                raise ValueError(f"invalid request id {r!r}")
-            if r >= _ID_LIMIT:
-                raise ValueError("request id exceeds int64 range")
-            if r > _MAX_REQUEST_ID and not internal:
-                raise ValueError("request id exceeds manual range")
+        # A decode loop passes the same id tuple every step; a tuple of ints
+        # cannot change, so one accepted under the same rules is not re-checked.
+        # (a tuple accepted by the caller's stricter rules also passes the
+        # engine's own; not the other way round)
+        if request_ids is not self._ids_ok or (self._ids_ok_internal and not internal):
+            if len(set(request_ids)) != b:
+                raise ValueError("duplicate request ids")
+            for r in request_ids:
+                if not _plain_int(r) or r < 0:
+                    raise ValueError(f"invalid request id {r!r}")
+                if r >= _ID_LIMIT:
+                    raise ValueError("request id exceeds int64 range")
+                if r > _MAX_REQUEST_ID and not internal:
+                    raise ValueError("request id exceeds manual range")
+            if type(request_ids) is tuple:
+                self._ids_ok, self._ids_ok_internal = request_ids, internal
         # Ids the engine produced itself (generate) are in range by
         # construction; a caller's are checked here (one host sync).
         if not internal and bool(((tokens < 0) | (tokens >= self.config.vocab_size)).any()):

@@ -268,3 +268,66 @@ def test_closed_engine_and_release_checks():
         e.forward(torch.tensor([[1]]), (1,), 0)
     with pytest.raises(EngineFailed):
         e.generate([[1]], 1)
+
+
+def test_cache_layers_move_apart_and_back_together():
+    """Per-layer counts appear while reference-style appends move one layer
+    ahead of the others and merge again once they agree; the checks and their
+    messages are per layer in layer order throughout."""
+    c = cache(layer_ids=(3, 5, 7))
+    c.reserve((1, 2))
+    c.append(3, (1, 2), kv(2, 2), kv(2, 2), 0)
+    with pytest.raises(CacheError, match="layer 5 for request 1 at 0, expected 2"):
+        c.validate((1, 2), 2, 1)
+    with pytest.raises(CacheError, match="layer 3 for request 1 at 2, expected 0"):
+        c.validate((1, 2), 0, 1)
+    with pytest.raises(CacheError, match="layer 3 request 1 at 2, expected 0"):
+        c.append(3, (1, 2), kv(2, 2), kv(2, 2), 0)
+    c.append(5, (1, 2), kv(2, 2), kv(2, 2), 0)
+    c.append(7, (1, 2), kv(2, 2), kv(2, 2), 0)
+    c.validate((1, 2), 2, 1)  # all three layers at 2 again
+    with pytest.raises(CacheError, match="layer 3 for request 2 at 2, expected 3"):
+        c.validate((2,), 3, 1)
+    c.advance((1,), 5)  # the decode step: every layer of request 1 at once
+    c.validate((1,), 5, 1)
+    c.validate((2,), 2, 1)
+    with pytest.raises(CacheError, match="layer 3 for request 1 at 5, expected 2"):
+        c.validate((1, 2), 2, 1)
+    c.append(7, (2,), kv(1, 1), kv(1, 1), 2)  # layer 7 ahead: others may follow
+    c.advance((2,), 3)
+    c.validate((2,), 3, 1)
+
+
+def test_cache_id_checks_hold_for_reused_and_new_tuples():
+    c = cache()
+    ids = (1, 2)
+    c.reserve(ids)
+    c.validate(ids, 0, 1)
+    c.validate(ids, 0, 1)  # the same tuple again
+    for bad, msg in (((1, 1), "duplicate"), ((1, True), "invalid request id"), ((1, -1), "invalid request id"),
+                     ([1, 2.0], "invalid request id"), ((), "non-empty")):
+        with pytest.raises(CacheError, match=msg):
+            c.validate(bad, 0, 1)
+    lst = [1, 2]
+    c.validate(lst, 0, 1)
+    lst[1] = 1  # a list can change between calls: checked every time
+    with pytest.raises(CacheError, match="duplicate"):
+        c.validate(lst, 0, 1)
+
+
+def test_engine_id_checks_keep_the_manual_range_for_reused_tuples():
+    """A tuple accepted for an engine-internal call (ids above the manual
+    range are allowed there) is checked again when a caller passes it."""
+    e = engine()
+    big = ((1 << 62) + 5,)
+    out = e.forward(torch.tensor([[1, 2]]), big, 0, _internal=True)
+    assert out.shape == (1, 2, 32)
+    with pytest.raises(ValueError, match="manual range"):
+        e.forward(torch.tensor([[3]]), big, 2)
+    assert e.healthy
+    ids = (7, 8)
+    e.forward(torch.tensor([[1], [2]]), ids, 0)
+    e.forward(torch.tensor([[1], [2]]), ids, 1, _internal=True)  # accepted by the stricter rules before
+    e.forward(torch.tensor([[1], [2]]), ids, 2)
+    assert e.healthy
+    e.close()
