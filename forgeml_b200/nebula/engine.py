@@ -115,6 +115,10 @@ class _CommandWire:
         self.frame_words = 4 + 3 * max_requests
         self.max_requests, self.max_seq_len = max_requests, max_seq_len
         self.device = device
+        # the ids of the last command received: equal ids of the next one
+        # come back as this same tuple, so the id checks downstream see a
+        # tuple they already accepted (both are tuples of plain ints)
+        self._last_ids: tuple = ()
 
     def broadcast(self, t: torch.Tensor) -> None:
         """The transport: every frame and body goes through this one call."""
@@ -230,7 +234,12 @@ class _CommandWire:
             bw = body.tolist()
         head = bw[:b] + (bw[b + b * t:] if extra else [])
         tokens = body[b:b + b * t].view(b, t) if t else None
-        return _Command(cmd, b, t, start, tuple(head[:b]), tokens, tuple(head[b:]))
+        ids = tuple(head[:b])
+        if ids == self._last_ids:
+            ids = self._last_ids
+        else:
+            self._last_ids = ids
+        return _Command(cmd, b, t, start, ids, tokens, tuple(head[b:]))
 
 
 class _StepHealth:

@@ -331,3 +331,27 @@ def test_engine_id_checks_keep_the_manual_range_for_reused_tuples():
     e.forward(torch.tensor([[1], [2]]), ids, 2)
     assert e.healthy
     e.close()
+
+
+def test_wire_returns_one_tuple_for_repeated_ids():
+    """A worker receiving consecutive commands with equal ids gets the same
+    tuple object back (its id checks then see a tuple they accepted);
+    different ids give a new tuple."""
+    from forgeml_b200.nebula.engine import CMD_RELEASE, CMD_STEP, CMD_STEP_AT, _CommandWire
+
+    w = _CommandWire(max_requests=4, max_seq_len=16, device=torch.device("cpu"))
+    sent = []
+    w.broadcast = lambda t: sent.append(t.clone())
+    w.send(CMD_STEP, 3, (7, 9), torch.tensor([[1], [2]]))
+    w.send(CMD_STEP, 4, (7, 9), torch.tensor([[3], [4]]))
+    w.send(CMD_STEP_AT, 0, (7, 9), torch.tensor([[5], [6]]), positions=(5, 6))
+    w.send(CMD_STEP, 6, (7, 8), torch.tensor([[5], [6]]))
+    w.send(CMD_RELEASE, 0, (7, 8))
+    frames = iter(sent)
+    r = _CommandWire(max_requests=4, max_seq_len=16, device=torch.device("cpu"))
+    r.broadcast = lambda t: t.copy_(next(frames))
+    a, b, c, d, e = (r.receive() for _ in range(5))
+    assert a.ids == b.ids == c.ids == (7, 9) and a.ids is b.ids and b.ids is c.ids
+    assert c.positions == (5, 6) and c.tokens.tolist() == [[5], [6]]
+    assert d.ids == (7, 8) and d.ids is not a.ids and e.ids is d.ids
+    assert all(type(v) is int for v in d.ids)
