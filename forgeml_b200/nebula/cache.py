@@ -165,6 +165,30 @@ class KVCache:
                 if n != start_pos:
                     raise CacheError(f"layer {lid} for request {r} at {n}, expected {start_pos}")
 
+    def validate_at(self, request_ids: tuple[int, ...], positions: tuple[int, ...], count: int) -> None:
+        """``validate((r,), p, count)`` for every request r at its own
+        position p (a step whose requests sit at different positions), with
+        the ids checked once for the batch (duplicates included)."""
+        tickets = self._tickets_of(request_ids)
+        if len(positions) != len(request_ids):
+            raise CacheError("one position per request")
+        if not _plain_int(count):
+            raise CacheError("count must be an integer")
+        if count <= 0:
+            raise CacheError("count must be positive")
+        for r, p, tk in zip(request_ids, positions, tickets):
+            if not _plain_int(p):
+                raise CacheError("start_pos must be an integer")
+            if p < 0 or p + count > self.max_seq_len:
+                raise CacheError("positions out of range")
+            if tk.per_layer is None:
+                if tk.level != p:
+                    raise CacheError(f"layer {self.layer_ids[0]} for request {r} at {tk.level}, expected {p}")
+                continue
+            for lid, n in tk.per_layer.items():
+                if n != p:
+                    raise CacheError(f"layer {lid} for request {r} at {n}, expected {p}")
+
     # -------------------------------------------------------------- updates
     def reserve(self, request_ids: tuple[int, ...]) -> None:
         self.check_admission(request_ids)

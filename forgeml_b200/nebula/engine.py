@@ -399,8 +399,7 @@ class Engine:
         cache = self.decoder.cache
         try:
             if not isinstance(start_pos, int):  # per-request positions (STEP_AT)
-                for r, p in zip(request_ids, start_pos, strict=True):
-                    cache.validate((r,), p, steps)
+                cache.validate_at(request_ids, start_pos, steps)
             elif start_pos == 0:
                 cache.check_admission(request_ids)
             else:

@@ -355,3 +355,47 @@ def test_wire_returns_one_tuple_for_repeated_ids():
     assert c.positions == (5, 6) and c.tokens.tolist() == [[5], [6]]
     assert d.ids == (7, 8) and d.ids is not a.ids and e.ids is d.ids
     assert all(type(v) is int for v in d.ids)
+
+
+def test_cache_validate_at_agrees_with_per_request_validate():
+    """validate_at(ids, positions, n) raises exactly when validate((r,), p, n)
+    raises for some request, and also for duplicate ids."""
+    import random
+
+    rng = random.Random(5)
+    for trial in range(300):
+        c = cache(layer_ids=(2, 4, 6), max_requests=6, max_seq_len=12)
+        ids = tuple(rng.sample(range(20), 4))
+        c.reserve(ids)
+        level = {}
+        for r in ids:  # each request at its own length; some with a layer ahead
+            level[r] = n = rng.randrange(0, 8)
+            if n:
+                c.advance((r,), n)
+            if rng.random() < 0.15:
+                c.append(rng.choice((2, 4, 6)), (r,), kv(1, 1), kv(1, 1), n)
+        if rng.random() < 0.9:  # mostly distinct reserved ids
+            q = tuple(rng.sample(ids, rng.randrange(1, 5)))
+        else:
+            q = tuple(rng.choice(ids + (99,)) for _ in range(rng.randrange(1, 5)))
+        # mostly each request's own position
+        pos = tuple(level.get(r, 0) if rng.random() < 0.9 else rng.randrange(-1, 12) for r in q)
+        count = rng.choice((1, 1, 1, 2, 0))
+
+        def per_request():
+            for r, p in zip(q, pos):
+                c.validate((r,), p, count)
+
+        want = None
+        try:
+            per_request()
+        except CacheError as e:
+            want = e
+        dup = len(set(q)) != len(q)
+        if want is None and not dup:
+            c.validate_at(q, pos, count)
+        else:
+            with pytest.raises(CacheError):
+                c.validate_at(q, pos, count)
+    with pytest.raises(CacheError, match="one position per request"):
+        c.validate_at(ids[:2], (0,), 1)
