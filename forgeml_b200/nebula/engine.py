@@ -28,8 +28,12 @@ on the outcome with a MAX all-reduce.  The agreed value is not waited for on
 the host before the step: a rank whose own check failed raises before it
 launches anything; a rank whose check passed launches the step and reads the
 agreed value afterwards together with the device error word (``_StepHealth``).
-Replicas that follow the same commands always agree, so well-formed use
-behaves exactly as the reference; a disagreement poisons every rank.
+Replicas that follow the same commands always agree: a command the cache
+rejects fails on every rank before the step, as in the reference.  A replica
+that alone disagrees (only a bug or a lost rank makes one) leaves the step
+before launching it; the other ranks run the step and fail at their next
+collective with that rank -- at once when its process has ended, otherwise
+when the bounded peer wait or the process group's timeout expires.
 
 Device health.  After each step the engine queues copies of the agreed
 preflight value and of the library's device error word (bounded waits that
